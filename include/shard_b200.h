@@ -1,0 +1,134 @@
+/* shard_b200 — C ABI of the B200 (sm_100a) MoE stage forward.
+ *
+ * One shared library, libshard_b200.so, exports every entry point below. Signatures carry plain
+ * device pointers, sizes and a cudaStream_t (passed as void*), never framework types, so any host
+ * (Python ctypes, cgo, JNI, C++) can bind them. All work is enqueued on the caller's stream; no
+ * entry point synchronises the device, allocates device memory or branches on device data on the
+ * host, so the forward is capturable into a CUDA graph and needs no host sync.
+ *
+ * Reference interfaces each entry point replaces are cited as leyten/shard file:line.
+ *
+ * Return value: SB_OK (0) or a negative SB_ERR_* code; sb_last_error() describes the last failure
+ * on the calling thread.
+ */
+#ifndef SHARD_B200_H
+#define SHARD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_ABI_VERSION 1
+
+enum sb_status {
+  SB_OK = 0,
+  SB_ERR_ARG = -1,        /* null pointer / bad enum */
+  SB_ERR_SHAPE = -2,      /* a dimension the kernels cannot hold (see each entry) */
+  SB_ERR_FORMAT = -3,     /* unsupported weight format */
+  SB_ERR_WORKSPACE = -4,  /* workspace too small */
+  SB_ERR_CUDA = -5,       /* a CUDA launch failed */
+  SB_ERR_UNSUPPORTED = -6 /* a configuration the forward declines (caller falls back) */
+};
+
+/* Weight formats of routed experts (shared experts are always SB_FMT_FP8). */
+enum sb_format {
+  SB_FMT_NVFP4 = 1, /* e2m1 x2 per byte (low nibble first), e4m3 scale per 16 K, fp32 tensor scale */
+  SB_FMT_MXFP4 = 2, /* e2m1 x2 per byte, e8m0 scale per 32 K (the reference's fp4 expert format) */
+  SB_FMT_FP8 = 3    /* e4m3, fp32 scale per 128x128 block */
+};
+
+/* Gate score functions, model.py:571-576 (Gate.forward). */
+enum sb_score { SB_SCORE_SOFTMAX = 0, SB_SCORE_SIGMOID = 1, SB_SCORE_SQRTSOFTPLUS = 2 };
+
+/* Which matrix a tiling call lays out. W13 fuses w1 and w3 ([2I, H], w1 rows then w3 rows, the
+ * reference's bank form, engines/deepseek_v4/v4_moe_grouped.py:382-540); a tile interleaves 8 w1
+ * rows with the same 8 w3 rows so one tensor-core tile yields gate and up values for the same
+ * intermediate index. PLAIN is any other [N, K] matrix (w2, dense projections). */
+enum sb_matrix_kind { SB_MAT_PLAIN = 0, SB_MAT_W13 = 1 };
+
+/* One MoE layer as the forward reads it. All pointers are device pointers; weights are in the
+ * TILED layout produced by sb_tile_weights / sb_tile_scales: 16-row tiles, each stored as the
+ * per-lane tensor-core fragments of consecutive 32-wide K chunks, so a warp streams a tile with
+ * one coalesced 16-byte load per lane per 64 K (fp4) or 32 K (fp8).
+ * Mirrors the state MoE.forward reads, model.py:614-649: self.gate.{weight,bias,tid2eid,
+ * score_func,route_scale,topk}, the expert bank, self.shared_experts, Expert.swiglu_limit. */
+typedef struct sb_moe_layer {
+  int32_t hidden;        /* H (dim): multiple of 128 */
+  int32_t inter;         /* I (moe_inter_dim): multiple of 128 */
+  int32_t n_experts;     /* E routed experts: 1..1024 */
+  int32_t topk;          /* k: 1..16 */
+  int32_t expert_fmt;    /* sb_format */
+  int32_t has_shared;    /* 1: one FP8 shared expert (n_shared_experts == 1) */
+  int32_t score_func;    /* sb_score */
+  int32_t act_pow2;      /* 1: activation scales 2^ceil(log2(amax/448)) (scale_fmt "ue8m0"); 0: amax/448 */
+  float route_scale;
+  float swiglu_limit;    /* 0 disables the clamp */
+  const void* gate_w;    /* bf16 [E, H] */
+  const float* gate_bias;/* fp32 [E] (selection only) or NULL */
+  const int32_t* tid2eid;/* hash routing: int32 [vocab, k], or NULL for score routing */
+  int64_t vocab;
+  /* routed experts, tiled: expert e's w13 at w13 + e * sb_tiled_bytes(fmt, 2I, H), etc. */
+  const void* w13;
+  const void* w13_s;
+  const float* w13_ts;   /* NVFP4: fp32 [E, 2] tensor scales (w1, w3); else NULL */
+  const void* w2;
+  const void* w2_s;
+  const float* w2_ts;    /* NVFP4: fp32 [E] tensor scales; else NULL */
+  /* shared expert (FP8, tiled) */
+  const void* sh_w13;
+  const void* sh_w13_s;
+  const void* sh_w2;
+  const void* sh_w2_s;
+} sb_moe_layer;
+
+/* ── introspection ───────────────────────────────────────────────────────────────────────────── */
+int sb_abi_version(void);
+const char* sb_last_error(void);
+
+/* Bytes of one tiled [N, K] weight matrix, values and scales (identical to the canonical sizes). */
+size_t sb_tiled_bytes(int fmt, int64_t n, int64_t k);
+size_t sb_tiled_scale_bytes(int fmt, int64_t n, int64_t k);
+
+/* ── load-time layout (replaces _relayout_moe / bank_layout, v4_moe_grouped.py:382-540) ───────── */
+/* Canonical -> tiled, for n_mat matrices of [N, K] stored back to back.
+ * src: fp4 packed [n_mat, N, K/2] (low nibble first) or fp8 [n_mat, N, K].  dst: same bytes. */
+int sb_tile_weights(int fmt, int kind, const void* src, void* dst, int64_t n_mat, int64_t n, int64_t k,
+                    void* stream);
+/* src scales: NVFP4 e4m3 [n_mat, N, K/16]; MXFP4 e8m0 [n_mat, N, K/32]; FP8 fp32 [n_mat, N/128, K/128]. */
+int sb_tile_scales(int fmt, int kind, const void* src, void* dst, int64_t n_mat, int64_t n, int64_t k,
+                   void* stream);
+
+/* ── the kernel-level seam (the reference's `kernel` module, kernel.py:105-125, 257-273, 518-536) ── */
+/* act_quant: bf16 x [M, K] -> e4m3 q [M, K] + fp32 s [M, K/128]; pow2 selects scale_fmt "ue8m0". */
+int sb_act_quant(const void* x, int64_t m, int64_t k, int pow2, void* q, float* s, void* stream);
+/* fp8_gemm / fp4_gemm: y bf16 [M, N] = dequant(q, s) @ dequant(W)^T with W tiled (PLAIN kind).
+ * ts: NVFP4 tensor scale (device fp32 [1]) or NULL. */
+int sb_qgemm(int fmt, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
+             const void* q, const float* s, int64_t m, void* y, void* stream);
+
+/* ── the MoE stage forward (MoE.forward, model.py:634-649; Gate.forward :569-589;
+ *    Expert.forward :601-611; grouped decode v4_moe_grouped.py:634-709) ──────────────────────── */
+size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m);
+/* x bf16 [M, H] -> y bf16 [M, H]. input_ids int64 [M] (read only for hash routing; may be NULL
+ * otherwise). Optional outputs (NULL to skip): routing weights fp32 [M, k] and top-k indices
+ * int64 [M, k] exactly as Gate.forward returns them. */
+int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,
+                   void* y, float* out_weights, int64_t* out_indices, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Routing alone (Gate.forward, model.py:569-589): weights fp32 [M, k], indices int64 [M, k]. */
+int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,
+                 float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* Format self-test: decodes a fixed set of e2m1 / e4m3 / e8m0 codes on the device into out
+ * (fp32 [64]) so a test can compare them with the host tables. */
+int sb_selftest_formats(float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SHARD_B200_H */

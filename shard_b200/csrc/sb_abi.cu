@@ -1,0 +1,343 @@
+// extern "C" entry points of libshard_b200.so (declared in include/shard_b200.h).
+//
+// Every entry point validates its shapes and pointers on the host, then enqueues kernels on the
+// caller's stream. None allocates, synchronises or reads device memory on the host.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "../../include/shard_b200.h"
+#include "sb_launch.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return SB_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// The forward's scratch regions, carved from one caller-provided workspace.
+struct Workspace {
+  float* logits;
+  int32_t* topk_idx;
+  float* topk_w;
+  uint8_t* xq;
+  float* xs;
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* active;
+  int32_t* n_active;
+  int32_t* pair_tok;
+  int32_t* pair_slot;
+  uint8_t* hq;
+  float* hs;
+  __nv_bfloat16* o;
+  size_t bytes;
+};
+
+Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
+  Workspace w;
+  const int64_t E = L->n_experts, K = L->topk, H = L->hidden, I = L->inter;
+  const int64_t P = m * K, R = P + m;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  w.logits = (float*)take(sizeof(float) * m * E);
+  w.topk_idx = (int32_t*)take(sizeof(int32_t) * P);
+  w.topk_w = (float*)take(sizeof(float) * P);
+  w.xq = take((size_t)m * H);
+  w.xs = (float*)take(sizeof(float) * m * (H / 128));
+  w.counts = (int32_t*)take(sizeof(int32_t) * E);
+  w.offsets = (int32_t*)take(sizeof(int32_t) * (E + 1));
+  w.active = (int32_t*)take(sizeof(int32_t) * E);
+  w.n_active = (int32_t*)take(sizeof(int32_t));
+  w.pair_tok = (int32_t*)take(sizeof(int32_t) * P);
+  w.pair_slot = (int32_t*)take(sizeof(int32_t) * P);
+  w.hq = take((size_t)R * I);
+  w.hs = (float*)take(sizeof(float) * R * (I / 128));
+  w.o = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * H);
+  w.bytes = off;
+  return w;
+}
+
+int check_layer(const sb_moe_layer* L) {
+  if (!L) return fail(SB_ERR_ARG, "layer is NULL");
+  if (L->hidden <= 0 || L->hidden % 128) return fail(SB_ERR_SHAPE, "hidden=%d must be a positive multiple of 128", L->hidden);
+  if (L->inter <= 0 || L->inter % 128) return fail(SB_ERR_SHAPE, "inter=%d must be a positive multiple of 128", L->inter);
+  if (L->n_experts < 1 || L->n_experts > 1024) return fail(SB_ERR_SHAPE, "n_experts=%d outside 1..1024", L->n_experts);
+  if (L->topk < 1 || L->topk > 16 || L->topk > L->n_experts)
+    return fail(SB_ERR_SHAPE, "topk=%d outside 1..min(16, n_experts)", L->topk);
+  if (L->expert_fmt != SB_FMT_NVFP4 && L->expert_fmt != SB_FMT_MXFP4 && L->expert_fmt != SB_FMT_FP8)
+    return fail(SB_ERR_FORMAT, "expert_fmt=%d unknown", L->expert_fmt);
+  if (L->score_func < 0 || L->score_func > 2) return fail(SB_ERR_ARG, "score_func=%d unknown", L->score_func);
+  if (!L->gate_w) return fail(SB_ERR_ARG, "gate_w is NULL");
+  if (!L->w13 || !L->w13_s || !L->w2 || !L->w2_s) return fail(SB_ERR_ARG, "routed expert bank pointer is NULL");
+  if (L->expert_fmt == SB_FMT_NVFP4 && (!L->w13_ts || !L->w2_ts))
+    return fail(SB_ERR_ARG, "NVFP4 experts need w13_ts and w2_ts");
+  if (L->has_shared && (!L->sh_w13 || !L->sh_w13_s || !L->sh_w2 || !L->sh_w2_s))
+    return fail(SB_ERR_ARG, "shared expert pointer is NULL");
+  if (!aligned16(L->w13) || !aligned16(L->w2) || !aligned16(L->gate_w) ||
+      (L->has_shared && (!aligned16(L->sh_w13) || !aligned16(L->sh_w2))))
+    return fail(SB_ERR_ARG, "weight pointers must be 16-byte aligned");
+  if (L->tid2eid && L->vocab <= 0) return fail(SB_ERR_ARG, "tid2eid given with vocab=%lld", (long long)L->vocab);
+  return SB_OK;
+}
+
+sb::WeightSet routed_set(const sb_moe_layer* L, bool w13) {
+  sb::WeightSet s;
+  const int64_t H = L->hidden, I = L->inter;
+  const int64_t n = w13 ? 2 * I : H, k = w13 ? H : I;
+  s.w = (const uint8_t*)(w13 ? L->w13 : L->w2);
+  s.s = (const uint8_t*)(w13 ? L->w13_s : L->w2_s);
+  s.ts = L->expert_fmt == SB_FMT_NVFP4 ? (w13 ? L->w13_ts : L->w2_ts) : nullptr;
+  s.ts_stride = w13 ? 2 : 1;
+  s.w_stride = sb_tiled_bytes(L->expert_fmt, n, k);
+  s.s_stride = sb_tiled_scale_bytes(L->expert_fmt, n, k);
+  s.fmt = L->expert_fmt;
+  return s;
+}
+
+sb::WeightSet shared_set(const sb_moe_layer* L, bool w13) {
+  sb::WeightSet s;
+  memset(&s, 0, sizeof s);
+  s.w = (const uint8_t*)(w13 ? L->sh_w13 : L->sh_w2);
+  s.s = (const uint8_t*)(w13 ? L->sh_w13_s : L->sh_w2_s);
+  s.fmt = SB_FMT_FP8;
+  return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb_abi_version(void) { return SB_ABI_VERSION; }
+
+const char* sb_last_error(void) { return g_err.c_str(); }
+
+size_t sb_tiled_bytes(int fmt, int64_t n, int64_t k) {
+  if (fmt == SB_FMT_FP8) return (size_t)(n * k);
+  if (fmt == SB_FMT_NVFP4 || fmt == SB_FMT_MXFP4) return (size_t)(n * k / 2);
+  return 0;
+}
+
+size_t sb_tiled_scale_bytes(int fmt, int64_t n, int64_t k) {
+  if (fmt == SB_FMT_NVFP4) return (size_t)(n * (k / 16));
+  if (fmt == SB_FMT_MXFP4) return (size_t)(n * (k / 32));
+  if (fmt == SB_FMT_FP8) return (size_t)((n / 16) * (k / 128) * 8);
+  return 0;
+}
+
+static int check_tile_args(int fmt, int kind, const void* src, const void* dst, int64_t n_mat, int64_t n, int64_t k) {
+  if (!src || !dst) return fail(SB_ERR_ARG, "tile: NULL pointer");
+  if (fmt != SB_FMT_NVFP4 && fmt != SB_FMT_MXFP4 && fmt != SB_FMT_FP8) return fail(SB_ERR_FORMAT, "tile: format %d", fmt);
+  if (kind != SB_MAT_PLAIN && kind != SB_MAT_W13) return fail(SB_ERR_ARG, "tile: kind %d", kind);
+  if (n_mat < 1 || n < 32 || n % 32 || k < 128 || k % 128)
+    return fail(SB_ERR_SHAPE, "tile: need n %% 32 == 0 and k %% 128 == 0 (n=%lld k=%lld)", (long long)n, (long long)k);
+  if (kind == SB_MAT_W13 && (n / 2) % 128)
+    return fail(SB_ERR_SHAPE, "tile: W13 needs the intermediate size n/2 %% 128 == 0 (n=%lld)", (long long)n);
+  return SB_OK;
+}
+
+int sb_tile_weights(int fmt, int kind, const void* src, void* dst, int64_t n_mat, int64_t n, int64_t k, void* stream) {
+  int rc = check_tile_args(fmt, kind, src, dst, n_mat, n, k);
+  if (rc) return rc;
+  if (!aligned16(dst)) return fail(SB_ERR_ARG, "tile: dst must be 16-byte aligned");
+  return cuda_check(sb::launch_tile_weights(fmt, kind, src, dst, n_mat, n, k, (cudaStream_t)stream), "tile_weights");
+}
+
+int sb_tile_scales(int fmt, int kind, const void* src, void* dst, int64_t n_mat, int64_t n, int64_t k, void* stream) {
+  int rc = check_tile_args(fmt, kind, src, dst, n_mat, n, k);
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(dst) & 7u) != 0) return fail(SB_ERR_ARG, "tile: scale dst must be 8-byte aligned");
+  return cuda_check(sb::launch_tile_scales(fmt, kind, src, dst, n_mat, n, k, (cudaStream_t)stream), "tile_scales");
+}
+
+int sb_act_quant(const void* x, int64_t m, int64_t k, int pow2, void* q, float* s, void* stream) {
+  if (!x || !q || !s) return fail(SB_ERR_ARG, "act_quant: NULL pointer");
+  if (m < 0 || k <= 0 || k % 128) return fail(SB_ERR_SHAPE, "act_quant: k=%lld must be a multiple of 128", (long long)k);
+  if (m == 0) return SB_OK;
+  return cuda_check(sb::launch_act_quant(x, m, k, pow2, (uint8_t*)q, s, (cudaStream_t)stream), "act_quant");
+}
+
+int sb_qgemm(int fmt, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k, const void* q,
+             const float* s, int64_t m, void* y, void* stream) {
+  if (!w || !w_s || !q || !s || !y) return fail(SB_ERR_ARG, "qgemm: NULL pointer");
+  if (fmt != SB_FMT_NVFP4 && fmt != SB_FMT_MXFP4 && fmt != SB_FMT_FP8) return fail(SB_ERR_FORMAT, "qgemm: format %d", fmt);
+  if (fmt == SB_FMT_NVFP4 && !ts) return fail(SB_ERR_ARG, "qgemm: NVFP4 needs a tensor scale");
+  if (n < 32 || n % 32 || k < 128 || k % 128 || m < 0 || m > (1 << 24))
+    return fail(SB_ERR_SHAPE, "qgemm: need n %% 32 == 0, k %% 128 == 0 (n=%lld k=%lld m=%lld)", (long long)n,
+                (long long)k, (long long)m);
+  if (!aligned16(w)) return fail(SB_ERR_ARG, "qgemm: weights must be 16-byte aligned");
+  if (m == 0) return SB_OK;
+  sb::GroupedArgs a;
+  memset(&a, 0, sizeof a);
+  a.mode = sb::MODE_DENSE;
+  a.m = (int)m;
+  a.topk = 1;
+  a.n_rows = (int)n;
+  a.k = (int)k;
+  a.has_shared = 1;
+  a.shared.w = (const uint8_t*)w;
+  a.shared.s = (const uint8_t*)w_s;
+  a.shared.ts = ts;
+  a.shared.ts_stride = 1;
+  a.shared.fmt = fmt;
+  a.routed = a.shared;
+  a.bq = (const uint8_t*)q;
+  a.bs = s;
+  a.o = (__nv_bfloat16*)y;
+  a.items_per_expert = (int)((n + 255) / 256);
+  return cuda_check(sb::launch_grouped(a, a.items_per_expert, 0, (cudaStream_t)stream), "qgemm");
+}
+
+size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
+  if (check_layer(layer) != SB_OK || m < 0) return 0;
+  return carve(layer, m < 1 ? 1 : m, nullptr).bytes;
+}
+
+static int route_impl(const sb_moe_layer* L, const void* x, int64_t m, const int64_t* ids, float* out_w,
+                      int64_t* out_idx, const Workspace& w, bool quant, cudaStream_t st) {
+  int rc = cuda_check(sb::launch_gate_logits(x, L->gate_w, w.logits, (int)m, L->n_experts, L->hidden, st), "gate_logits");
+  if (rc) return rc;
+  sb::RouteArgs r;
+  r.logits = w.logits;
+  r.bias = L->gate_bias;
+  r.tid2eid = L->tid2eid;
+  r.input_ids = ids;
+  r.m = (int)m;
+  r.n_experts = L->n_experts;
+  r.topk = L->topk;
+  r.score_func = L->score_func;
+  r.act_pow2 = L->act_pow2;
+  r.hidden = L->hidden;
+  r.route_scale = L->route_scale;
+  r.topk_idx = w.topk_idx;
+  r.topk_w = w.topk_w;
+  r.out_idx = out_idx;
+  r.out_w = out_w;
+  r.x = (const __nv_bfloat16*)x;
+  r.xq = quant ? w.xq : nullptr;
+  r.xs = w.xs;
+  return cuda_check(sb::launch_route(r, st), "route");
+}
+
+int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, float* out_weights,
+                 int64_t* out_indices, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_layer(layer);
+  if (rc) return rc;
+  if (!x) return fail(SB_ERR_ARG, "x is NULL");
+  if (m < 0 || m > (1 << 20)) return fail(SB_ERR_SHAPE, "m=%lld outside 0..2^20", (long long)m);
+  if (m == 0) return SB_OK;
+  if (layer->tid2eid && !input_ids) return fail(SB_ERR_ARG, "hash routing needs input_ids");
+  Workspace w = carve(layer, m, (uint8_t*)workspace);
+  if (!workspace || workspace_bytes < w.bytes)
+    return fail(SB_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, w.bytes);
+  return route_impl(layer, x, m, input_ids, out_weights, out_indices, w, false, (cudaStream_t)stream);
+}
+
+int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
+                   float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_layer(layer);
+  if (rc) return rc;
+  const sb_moe_layer* L = layer;
+  if (!x || !y) return fail(SB_ERR_ARG, "x or y is NULL");
+  if (!aligned16(x) || !aligned16(y)) return fail(SB_ERR_ARG, "x and y must be 16-byte aligned");
+  if (m < 0 || m > (1 << 20)) return fail(SB_ERR_SHAPE, "m=%lld outside 0..2^20", (long long)m);
+  if (m == 0) return SB_OK;
+  if (L->tid2eid && !input_ids) return fail(SB_ERR_ARG, "hash routing needs input_ids");
+  if ((int64_t)m * L->topk > (1 << 22)) return fail(SB_ERR_SHAPE, "m * topk too large");
+  Workspace w = carve(L, m, (uint8_t*)workspace);
+  if (!workspace || workspace_bytes < w.bytes)
+    return fail(SB_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, w.bytes);
+  cudaStream_t st = (cudaStream_t)stream;
+  rc = route_impl(L, x, m, input_ids, out_weights, out_indices, w, true, st);
+  if (rc) return rc;
+  sb::PermuteArgs p;
+  p.topk_idx = w.topk_idx;
+  p.m = (int)m;
+  p.topk = L->topk;
+  p.n_experts = L->n_experts;
+  p.counts = w.counts;
+  p.offsets = w.offsets;
+  p.active = w.active;
+  p.n_active = w.n_active;
+  p.pair_tok = w.pair_tok;
+  p.pair_slot = w.pair_slot;
+  rc = cuda_check(sb::launch_permute(p, st), "permute");
+  if (rc) return rc;
+
+  const int64_t H = L->hidden, I = L->inter, P = m * L->topk;
+  const int64_t max_active = P < L->n_experts ? P : L->n_experts;
+  sb::GroupedArgs g;
+  memset(&g, 0, sizeof g);
+  g.m = (int)m;
+  g.topk = L->topk;
+  g.has_shared = L->has_shared;
+  g.act_pow2 = L->act_pow2;
+  g.swiglu_limit = L->swiglu_limit;
+  g.counts = w.counts;
+  g.offsets = w.offsets;
+  g.active = w.active;
+  g.n_active = w.n_active;
+  g.pair_tok = w.pair_tok;
+  g.pair_slot = w.pair_slot;
+  g.topk_w = w.topk_w;
+  // w13 (+ SwiGLU, + act_quant of h)
+  g.mode = sb::MODE_W13;
+  g.n_rows = (int)(2 * I);
+  g.k = (int)H;
+  g.routed = routed_set(L, true);
+  g.shared = shared_set(L, true);
+  g.bq = w.xq;
+  g.bs = w.xs;
+  g.hq = w.hq;
+  g.hs = w.hs;
+  g.items_per_expert = (int)(I / 128);
+  rc = cuda_check(sb::launch_grouped(g, (int)((max_active + (L->has_shared ? 1 : 0)) * g.items_per_expert), 0, st),
+                  "grouped w13");
+  if (rc) return rc;
+  // w2
+  g.mode = sb::MODE_W2;
+  g.n_rows = (int)H;
+  g.k = (int)I;
+  g.routed = routed_set(L, false);
+  g.shared = shared_set(L, false);
+  g.bq = w.hq;
+  g.bs = w.hs;
+  g.o = w.o;
+  g.items_per_expert = (int)((H + 255) / 256);
+  rc = cuda_check(sb::launch_grouped(g, (int)((max_active + (L->has_shared ? 1 : 0)) * g.items_per_expert), 0, st),
+                  "grouped w2");
+  if (rc) return rc;
+  return cuda_check(sb::launch_combine(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
+                                       (__nv_bfloat16*)y, st),
+                    "combine");
+}
+
+int sb_selftest_formats(float* out, void* stream) {
+  if (!out) return fail(SB_ERR_ARG, "selftest: NULL pointer");
+  return cuda_check(sb::launch_selftest(out, (cudaStream_t)stream), "selftest");
+}
+
+}  // extern "C"

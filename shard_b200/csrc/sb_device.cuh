@@ -1,0 +1,148 @@
+// Device helpers shared by the MoE-stage kernels (sm_100a).
+//
+// Number formats: e2m1 (fp4, two per byte, low nibble = even K), e4m3 (fp8), e8m0 (power-of-two
+// scale byte), bf16 activations, fp32 accumulation. The conversions below go through the CUDA
+// fp4/fp8 intrinsics (cvt.rn.f16x2.e2m1x2 / cvt.rn.f16x2.e4m3x2 on sm_100a), which are exact:
+// every e2m1 and e4m3 value is representable in fp16.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_fp4.h>
+#include <stdint.h>
+
+namespace sb {
+
+constexpr int FMT_NVFP4 = 1;
+constexpr int FMT_MXFP4 = 2;
+constexpr int FMT_FP8 = 3;
+
+constexpr int SCORE_SOFTMAX = 0;
+constexpr int SCORE_SIGMOID = 1;
+constexpr int SCORE_SQRTSOFTPLUS = 2;
+
+// ── conversions ────────────────────────────────────────────────────────────────────────────────
+
+// one byte = two e2m1 codes -> f16x2 (low nibble -> low half)
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+  __half2_raw r = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)(byte & 0xFFu), __NV_E2M1);
+  return (uint32_t)r.x | ((uint32_t)r.y << 16);
+}
+
+// two e4m3 bytes (low byte first) -> f16x2 (low byte -> low half)
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
+  __half2_raw r = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(two & 0xFFFFu), __NV_E4M3);
+  return (uint32_t)r.x | ((uint32_t)r.y << 16);
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint32_t byte) {
+  __half_raw r = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)(byte & 0xFFu), __NV_E4M3);
+  return __half2float(__half(r));
+}
+
+__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
+  return (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+}
+
+// e8m0 byte -> 2^(b-127) (b in [1, 254]; 0 maps to 2^-127 via the subnormal pattern)
+__device__ __forceinline__ float e8m0_to_f32(uint32_t b) {
+  b &= 0xFFu;
+  return b ? __uint_as_float(b << 23) : __uint_as_float(0x00400000u);
+}
+
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// f16x2 with both halves = the low (or high) half of s
+__device__ __forceinline__ uint32_t splat_lo(uint32_t s) { return (s & 0xFFFFu) | (s << 16); }
+__device__ __forceinline__ uint32_t splat_hi(uint32_t s) { return (s >> 16) | (s & 0xFFFF0000u); }
+
+// 2^ceil(log2(x)) for a positive normal x, read off the IEEE bits: the exponent, plus one unless
+// the mantissa is zero. Exact at powers of two, which is the property the activation scale rule
+// (ue8m0) needs.
+__device__ __forceinline__ float pow2_ceil(float x) {
+  uint32_t b = __float_as_uint(x);
+  int e = (int)((b >> 23) & 0xFFu) - 127 + ((b & 0x7FFFFFu) != 0u);
+  e = e < -126 ? -126 : (e > 127 ? 127 : e);
+  return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+
+// per-block activation scale: amax floored at 1e-4, then 2^ceil(log2(amax/448)) or amax/448
+__device__ __forceinline__ float act_scale(float amax, bool pow2) {
+  amax = fmaxf(amax, 1e-4f);
+  float x = amax * (1.0f / 448.0f);
+  return pow2 ? pow2_ceil(x) : x;
+}
+
+__device__ __forceinline__ uint8_t act_q(float v, float s) {
+  float q = __fdiv_rn(v, s);
+  q = fminf(fmaxf(q, -448.0f), 448.0f);
+  return f32_to_e4m3(q);
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+// ── tensor-core fragments (mma.sync, fp32 accumulate) ───────────────────────────────────────────
+// m16n8k16 f16: A rows g / g+8, k {2t,2t+1} and {2t+8,2t+9}; B (k x n) k {2t,2t+1},{2t+8,2t+9}, n = g;
+// C rows g / g+8, cols {2t, 2t+1}   (g = lane/4, t = lane%4)
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// m16n8k32 e4m3: A rows g / g+8, k 4t..4t+3 and 16+4t..; B k 4t.. / 16+4t.., n = g
+__device__ __forceinline__ void mma_e4m3(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// streaming 16-byte weight load: read once, keep it out of L1
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_stream4(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace sb

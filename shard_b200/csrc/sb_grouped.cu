@@ -1,0 +1,642 @@
+// Grouped expert GEMV/GEMM of the MoE stage forward, for the decode/verify regime (few tokens per
+// expert), where the forward is bound by streaming expert weights from HBM.
+//
+// Work is a list of ITEMS, each one CTA-sized piece of one expert's weights: the shared expert's
+// items first, then every active expert's (from the device-side permutation, so the host never
+// learns which experts are active). A persistent grid of 2 CTAs per SM walks the list. An item is
+// 16 row tiles (256 rows) x the whole K; each of the 8 warps streams two 16-row tiles with one
+// coalesced 16-byte load per lane per 64 K (fp4) or 32 K (fp8), converts the e2m1/e4m3 codes to
+// f16 in registers and feeds mma.sync tensor-core fragments, with the item's tokens as the MMA's
+// N dimension (8 per fragment, up to 32 per pass).
+//
+// Arithmetic (the reference's, reassociated only in the fp32 sums):
+//   NVFP4  A = e2m1 * e4m3 scale (exact in f16), per-16 scale folded into the fragment,
+//   MXFP4  A = e2m1, per-32 power-of-two scale applied to the fp32 partial of each 32-chunk,
+//   FP8    A = e4m3 (m16n8k32), 128x128 block scale applied per 128-K block,
+//   B = the e4m3 activation, its per-128 scale applied per 128-K block, fp32 accumulation;
+//   NVFP4 tensor scale in the epilogue.
+// Epilogues:
+//   W13  gate/up -> bf16 each (fp4_gemm's output dtype), clamp, silu(g)*u, * routing weight,
+//        -> bf16 -> per-128 act_quant (e4m3 + scale) of h for the w2 pass   (Expert.forward,
+//        model.py:601-611; act_quant kernel.py:40-125)
+//   W2   bf16 output row per (token, slot), or per token for the shared expert
+//   DENSE a single quantised linear (fp8_gemm / fp4_gemm, kernel.py:257-273, 518-536)
+#include "sb_device.cuh"
+#include "sb_launch.h"
+
+namespace sb {
+
+constexpr int WARPS = 8;
+constexpr int TILES_PER_ITEM = 16;
+constexpr int MAX_PASS = 32;  // tokens per pass (4 fragments of 8)
+
+struct ItemInfo {
+  int shared;   // 1: shared expert / dense
+  int expert;
+  int blk;      // item index within the expert
+  int cnt;      // pairs (tokens) of this expert
+  int base;     // first sorted pair position (routed)
+};
+
+template <int FMT>
+struct Tiling;
+template <>
+struct Tiling<FMT_NVFP4> {
+  static __device__ size_t w_tile(int k) { return (size_t)8 * k; }   // 16 rows * k/2
+  static __device__ size_t s_tile(int k) { return (size_t)k; }       // 16 rows * k/16
+};
+template <>
+struct Tiling<FMT_MXFP4> {
+  static __device__ size_t w_tile(int k) { return (size_t)8 * k; }
+  static __device__ size_t s_tile(int k) { return (size_t)k / 2; }   // 16 rows * k/32
+};
+template <>
+struct Tiling<FMT_FP8> {
+  static __device__ size_t w_tile(int k) { return (size_t)16 * k; }
+  static __device__ size_t s_tile(int k) { return (size_t)(k / 128) * 8; }
+};
+
+// Per-lane B operand for one 32-wide K chunk: raw e4m3 bytes at K {4t..4t+3} and {16+4t..16+4t+3}
+// of the lane's token (g) in fragment c (brow < 0: no token, zeros).
+template <int NCH>
+__device__ __forceinline__ void load_b(const uint8_t* __restrict__ bq, const int (&brow)[NCH], int K, int ch, int t,
+                                       uint32_t (&lo)[NCH], uint32_t (&hi)[NCH]) {
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    if (brow[c] >= 0) {
+      const uint8_t* p = bq + (size_t)brow[c] * K + ch * 32 + 4 * t;
+      lo[c] = *reinterpret_cast<const uint32_t*>(p);
+      hi[c] = *reinterpret_cast<const uint32_t*>(p + 16);
+    } else {
+      lo[c] = 0u;
+      hi[c] = 0u;
+    }
+  }
+}
+
+// Activation scales of the lane's C columns (tokens 2t, 2t+1 of each fragment) for 128-block kb.
+// A missing token gets 1.0 so the running rescale below stays finite (its column is all zero).
+template <int NCH>
+__device__ __forceinline__ void load_sa(const float* __restrict__ bs, const int (&srow)[NCH][2], int nkb, int kb,
+                                        float (&sa)[NCH][2]) {
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int u = 0; u < 2; ++u) sa[c][u] = srow[c][u] >= 0 ? bs[(size_t)srow[c][u] * nkb + kb] : 1.f;
+}
+
+// The two-tile mainloop of one warp over the whole K. On return acc[tile][frag][4] holds
+// sum_k dequant(W) * dequant(B) for rows (g, g+8) x tokens (2t, 2t+1) of each fragment.
+//
+// Per-128-block scales (the activation's, and for FP8 the weight block's) are applied by keeping
+// the running fp32 accumulator in units of the current block's scale: at a block boundary it is
+// multiplied by old_scale / new_scale, and by the last scale at the end. With power-of-two scales
+// (the ue8m0 rule and the FP8 weight blocks here) every such multiply is exact, so this equals
+// summing per-block partials times their scales; it needs one accumulator set instead of two.
+template <int FMT, int NCH>
+__device__ __forceinline__ void mainloop(const uint8_t* __restrict__ wt, const uint8_t* __restrict__ st, int K,
+                                         const uint8_t* __restrict__ bq, const float* __restrict__ bs,
+                                         const int (&brow)[NCH], const int (&srow)[NCH][2],
+                                         float (&acc)[2][NCH][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const size_t wtile = Tiling<FMT>::w_tile(K), stile = Tiling<FMT>::s_tile(K);
+  const int nkb = K / 128;
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[a][c][r] = 0.f;
+  float sa[NCH][2];
+  load_sa<NCH>(bs, srow, nkb, 0, sa);
+  const uint8_t* w0 = wt + lane * 16;
+  const uint8_t* w1 = w0 + wtile;
+
+  if constexpr (FMT == FMT_FP8) {
+    // one 16-byte load per lane per tile per 32 K; 4 steps per 128-block
+    const float2* s0 = reinterpret_cast<const float2*>(st);
+    const float2* s1 = reinterpret_cast<const float2*>(st + stile);
+    float2 sw[2] = {s0[0], s1[0]};
+    const int nsteps = K / 32;
+    uint4 nx0 = ld_stream16(w0), nx1 = ld_stream16(w1);
+    for (int step = 0; step < nsteps; ++step) {
+      const uint4 c0 = nx0, c1 = nx1;
+      if (step + 1 < nsteps) {
+        nx0 = ld_stream16(w0 + (step + 1) * 512);
+        nx1 = ld_stream16(w1 + (step + 1) * 512);
+      }
+      if (step > 0 && (step & 3) == 0) {
+        const int kb = step >> 2;
+        float nsa[NCH][2];
+        load_sa<NCH>(bs, srow, nkb, kb, nsa);
+        const float2 nw0 = s0[kb], nw1 = s1[kb];
+        const float r0x = sw[0].x / nw0.x, r0y = sw[0].y / nw0.y, r1x = sw[1].x / nw1.x, r1y = sw[1].y / nw1.y;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          const float q0 = sa[c][0] / nsa[c][0], q1 = sa[c][1] / nsa[c][1];
+          acc[0][c][0] *= r0x * q0;
+          acc[0][c][1] *= r0x * q1;
+          acc[0][c][2] *= r0y * q0;
+          acc[0][c][3] *= r0y * q1;
+          acc[1][c][0] *= r1x * q0;
+          acc[1][c][1] *= r1x * q1;
+          acc[1][c][2] *= r1y * q0;
+          acc[1][c][3] *= r1y * q1;
+          sa[c][0] = nsa[c][0];
+          sa[c][1] = nsa[c][1];
+        }
+        sw[0] = nw0;
+        sw[1] = nw1;
+      }
+      uint32_t lo[NCH], hi[NCH];
+      load_b<NCH>(bq, brow, K, step, t, lo, hi);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        mma_e4m3(acc[0][c], c0.x, c0.y, c0.z, c0.w, lo[c], hi[c]);
+        mma_e4m3(acc[1][c], c1.x, c1.y, c1.z, c1.w, lo[c], hi[c]);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      acc[0][c][0] *= sw[0].x * sa[c][0];
+      acc[0][c][1] *= sw[0].x * sa[c][1];
+      acc[0][c][2] *= sw[0].y * sa[c][0];
+      acc[0][c][3] *= sw[0].y * sa[c][1];
+      acc[1][c][0] *= sw[1].x * sa[c][0];
+      acc[1][c][1] *= sw[1].x * sa[c][1];
+      acc[1][c][2] *= sw[1].y * sa[c][0];
+      acc[1][c][3] *= sw[1].y * sa[c][1];
+    }
+  } else {
+    // fp4: one 16-byte load per lane per tile per 64 K (two 32-chunks); 2 steps per 128-block
+    constexpr int SB = (FMT == FMT_NVFP4) ? 8 : 4;  // scale bytes per lane per 64 K
+    const uint8_t* s0 = st + g * SB;
+    const uint8_t* s1 = s0 + stile;
+    const int nsteps = K / 64;
+    uint4 nx0 = ld_stream16(w0), nx1 = ld_stream16(w1);
+    uint2 ns0, ns1;
+    if constexpr (FMT == FMT_NVFP4) {
+      ns0 = ld_stream8(s0);
+      ns1 = ld_stream8(s1);
+    } else {
+      ns0 = make_uint2(ld_stream4(s0), 0u);
+      ns1 = make_uint2(ld_stream4(s1), 0u);
+    }
+    for (int step = 0; step < nsteps; ++step) {
+      const uint4 cw[2] = {nx0, nx1};
+      const uint2 cs[2] = {ns0, ns1};
+      if (step + 1 < nsteps) {
+        nx0 = ld_stream16(w0 + (step + 1) * 512);
+        nx1 = ld_stream16(w1 + (step + 1) * 512);
+        if constexpr (FMT == FMT_NVFP4) {
+          ns0 = ld_stream8(s0 + (step + 1) * 64);
+          ns1 = ld_stream8(s1 + (step + 1) * 64);
+        } else {
+          ns0 = make_uint2(ld_stream4(s0 + (step + 1) * 32), 0u);
+          ns1 = make_uint2(ld_stream4(s1 + (step + 1) * 32), 0u);
+        }
+      }
+      if (step > 0 && (step & 1) == 0) {
+        float nsa[NCH][2];
+        load_sa<NCH>(bs, srow, nkb, step >> 1, nsa);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          const float q0 = sa[c][0] / nsa[c][0], q1 = sa[c][1] / nsa[c][1];
+#pragma unroll
+          for (int a = 0; a < 2; ++a) {
+            acc[a][c][0] *= q0;
+            acc[a][c][1] *= q1;
+            acc[a][c][2] *= q0;
+            acc[a][c][3] *= q1;
+          }
+          sa[c][0] = nsa[c][0];
+          sa[c][1] = nsa[c][1];
+        }
+      }
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
+        const int ch = step * 2 + sub;
+        uint32_t lo[NCH], hi[NCH];
+        load_b<NCH>(bq, brow, K, ch, t, lo, hi);
+        uint32_t bA0[NCH], bA1[NCH], bB0[NCH], bB1[NCH];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          bA0[c] = e4m3x2_to_f16x2(lo[c]);
+          bA1[c] = e4m3x2_to_f16x2(lo[c] >> 16);
+          bB0[c] = e4m3x2_to_f16x2(hi[c]);
+          bB1[c] = e4m3x2_to_f16x2(hi[c] >> 16);
+        }
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+          const uint32_t wlo = sub ? cw[a].z : cw[a].x;
+          const uint32_t whi = sub ? cw[a].w : cw[a].y;
+          uint32_t A0 = e2m1x2_to_f16x2(wlo), A1 = e2m1x2_to_f16x2(wlo >> 8);
+          uint32_t A2 = e2m1x2_to_f16x2(wlo >> 16), A3 = e2m1x2_to_f16x2(wlo >> 24);
+          uint32_t B0 = e2m1x2_to_f16x2(whi), B1 = e2m1x2_to_f16x2(whi >> 8);
+          uint32_t B2 = e2m1x2_to_f16x2(whi >> 16), B3 = e2m1x2_to_f16x2(whi >> 24);
+          if constexpr (FMT == FMT_NVFP4) {
+            const uint32_t sc = sub ? cs[a].y : cs[a].x;
+            const uint32_t sA = e4m3x2_to_f16x2(sc), sB = e4m3x2_to_f16x2(sc >> 16);
+            const uint32_t sAl = splat_lo(sA), sAh = splat_hi(sA);
+            const uint32_t sBl = splat_lo(sB), sBh = splat_hi(sB);
+            A0 = hmul2_u32(A0, sAl);
+            A2 = hmul2_u32(A2, sAl);
+            A1 = hmul2_u32(A1, sAh);
+            A3 = hmul2_u32(A3, sAh);
+            B0 = hmul2_u32(B0, sBl);
+            B2 = hmul2_u32(B2, sBl);
+            B1 = hmul2_u32(B1, sBh);
+            B3 = hmul2_u32(B3, sBh);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+              mma_f16(acc[a][c], A0, A1, A2, A3, bA0[c], bA1[c]);
+              mma_f16(acc[a][c], B0, B1, B2, B3, bB0[c], bB1[c]);
+            }
+          } else {
+            const uint32_t sc = (sub ? (cs[a].x >> 16) : cs[a].x) & 0xFFFFu;
+            const float fg = e8m0_to_f32(sc), fg8 = e8m0_to_f32(sc >> 8);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+              float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+              mma_f16(tmp, A0, A1, A2, A3, bA0[c], bA1[c]);
+              mma_f16(tmp, B0, B1, B2, B3, bB0[c], bB1[c]);
+              acc[a][c][0] = fmaf(tmp[0], fg, acc[a][c][0]);
+              acc[a][c][1] = fmaf(tmp[1], fg, acc[a][c][1]);
+              acc[a][c][2] = fmaf(tmp[2], fg8, acc[a][c][2]);
+              acc[a][c][3] = fmaf(tmp[3], fg8, acc[a][c][3]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        acc[a][c][0] *= sa[c][0];
+        acc[a][c][1] *= sa[c][1];
+        acc[a][c][2] *= sa[c][0];
+        acc[a][c][3] *= sa[c][1];
+      }
+  }
+}
+
+__device__ __forceinline__ ItemInfo item_info(const GroupedArgs& a, int item, int n_sh) {
+  ItemInfo it;
+  if (item < n_sh) {
+    it.shared = 1;
+    it.expert = 0;
+    it.blk = item;
+    it.cnt = a.m;
+    it.base = 0;
+  } else {
+    const int r = item - n_sh;
+    it.shared = 0;
+    it.expert = a.active[r / a.items_per_expert];
+    it.blk = r % a.items_per_expert;
+    it.cnt = a.counts[it.expert];
+    it.base = a.offsets[it.expert];
+  }
+  return it;
+}
+
+struct PassSmem {
+  int brow[MAX_PASS];
+  int orow[MAX_PASS];
+  float wgt[MAX_PASS];
+  float amax[WARPS][MAX_PASS];
+  float scale[MAX_PASS];
+};
+
+template <int FMT, int NCH>
+__device__ void run_pass(const GroupedArgs& a, const ItemInfo& it, const WeightSet& ws, int pass_cnt,
+                         PassSmem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int K = a.k;
+  const int tiles_total = a.n_rows / 16;
+  const int tile0 = it.blk * TILES_PER_ITEM + warp * 2;
+  const bool active_warp = tile0 < tiles_total;  // n_rows % 32 == 0: both tiles exist
+  int brow[NCH];
+  int srow[NCH][2];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int ib = c * 8 + g;
+    brow[c] = ib < pass_cnt ? sm.brow[ib] : -1;
+    const int i0 = c * 8 + 2 * t, i1 = i0 + 1;
+    srow[c][0] = i0 < pass_cnt ? sm.brow[i0] : -1;
+    srow[c][1] = i1 < pass_cnt ? sm.brow[i1] : -1;
+  }
+  float acc[2][NCH][4];
+  const int e = it.expert;
+  if (active_warp) {
+    const uint8_t* wt = ws.w + (it.shared ? 0 : (size_t)e * ws.w_stride) + (size_t)tile0 * Tiling<FMT>::w_tile(K);
+    const uint8_t* st = ws.s + (it.shared ? 0 : (size_t)e * ws.s_stride) + (size_t)tile0 * Tiling<FMT>::s_tile(K);
+    mainloop<FMT, NCH>(wt, st, K, a.bq, a.bs, brow, srow, acc);
+  } else {
+#pragma unroll
+    for (int x = 0; x < 2; ++x)
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[x][c][r] = 0.f;
+  }
+  // tensor scales (NVFP4): rows 0-7 / 8-15 of a W13 tile are w1 / w3
+  float ts_lo = 1.f, ts_hi = 1.f;
+  if (FMT == FMT_NVFP4 && ws.ts != nullptr) {
+    const float* tsp = ws.ts + (it.shared ? 0 : (size_t)e * ws.ts_stride);
+    ts_lo = tsp[0];
+    ts_hi = (a.mode == MODE_W13) ? tsp[1] : tsp[0];
+  }
+  if (a.mode == MODE_W13) {
+    // SwiGLU epilogue, then the per-128 quantisation of h over the item's 128 intermediate indices
+    const float lim = a.swiglu_limit;
+    float hv[2][NCH][2];
+    float am[NCH][2];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = c * 8 + 2 * t + u;
+        am[c][u] = 0.f;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          float gv = bf16_round(acc[x][c][u] * ts_lo);
+          float uv = bf16_round(acc[x][c][2 + u] * ts_hi);
+          if (lim > 0.f) {
+            uv = fminf(fmaxf(uv, -lim), lim);
+            gv = fminf(gv, lim);
+          }
+          float h = silu(gv) * uv;
+          if (!it.shared && i < pass_cnt) h = sm.wgt[i] * h;
+          h = bf16_round(h);
+          hv[x][c][u] = h;
+          if (active_warp && i < pass_cnt) am[c][u] = fmaxf(am[c][u], fabsf(h));
+        }
+      }
+    }
+    // max over g (lanes sharing t), then over warps
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float v = am[c][u];
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+        if (g == 0) sm.amax[warp][c * 8 + 2 * t + u] = v;
+      }
+    __syncthreads();
+    if (threadIdx.x < MAX_PASS) {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) v = fmaxf(v, sm.amax[w][threadIdx.x]);
+      const float s = act_scale(v, a.act_pow2 != 0);
+      sm.scale[threadIdx.x] = s;
+      if (threadIdx.x < pass_cnt) a.hs[(size_t)sm.orow[threadIdx.x] * (a.n_rows / 2 / 128) + it.blk] = s;
+    }
+    __syncthreads();
+    if (active_warp) {
+      const int I = a.n_rows / 2;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = c * 8 + 2 * t + u;
+          if (i < pass_cnt) {
+            const float s = sm.scale[i];
+            uint8_t* row = a.hq + (size_t)sm.orow[i] * I;
+#pragma unroll
+            for (int x = 0; x < 2; ++x) row[(tile0 + x) * 8 + g] = act_q(hv[x][c][u], s);
+          }
+        }
+    }
+  } else {
+    if (active_warp) {
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = c * 8 + 2 * t + u;
+          if (i < pass_cnt) {
+            __nv_bfloat16* row = a.o + (size_t)sm.orow[i] * a.n_rows;
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              const int n0 = (tile0 + x) * 16 + g;
+              row[n0] = __float2bfloat16_rn(acc[x][c][u] * ts_lo);
+              row[n0 + 8] = __float2bfloat16_rn(acc[x][c][2 + u] * ts_hi);
+            }
+          }
+        }
+    }
+  }
+}
+
+template <int FMT_R>
+__global__ void __launch_bounds__(256, 2) grouped_kernel(GroupedArgs a) {
+  __shared__ PassSmem sm;
+  const int n_sh = a.has_shared ? a.items_per_expert : 0;
+  const int n_items = n_sh + (a.mode == MODE_DENSE ? 0 : (*a.n_active) * a.items_per_expert);
+  const int P = a.m * a.topk;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const ItemInfo it = item_info(a, item, n_sh);
+    const WeightSet& ws = it.shared ? a.shared : a.routed;
+    const int fmt = it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R;
+    const int pass_max = fmt == FMT_FP8 ? MAX_PASS : 16;
+    for (int pb = 0; pb < it.cnt; pb += pass_max) {
+      const int pass_cnt = min(pass_max, it.cnt - pb);
+      __syncthreads();
+      if (threadIdx.x < pass_cnt) {
+        const int i = pb + threadIdx.x;
+        int brow, orow;
+        float wgt = 1.f;
+        if (it.shared) {
+          if (a.mode == MODE_DENSE) {
+            brow = i;
+            orow = i;
+          } else if (a.mode == MODE_W13) {
+            brow = i;
+            orow = P + i;
+          } else {
+            brow = P + i;
+            orow = P + i;
+          }
+        } else {
+          const int q = it.base + i;
+          const int tok = a.pair_tok[q], slot = a.pair_slot[q];
+          if (a.mode == MODE_W13) {
+            brow = tok;
+            orow = q;
+            wgt = a.topk_w[(size_t)tok * a.topk + slot];
+          } else {
+            brow = q;
+            orow = tok * a.topk + slot;
+          }
+        }
+        sm.brow[threadIdx.x] = brow;
+        sm.orow[threadIdx.x] = orow;
+        sm.wgt[threadIdx.x] = wgt;
+      }
+      __syncthreads();
+      if (fmt == FMT_FP8) {
+        if (pass_cnt <= 8) run_pass<FMT_FP8, 1>(a, it, ws, pass_cnt, sm);
+        else if (pass_cnt <= 16) run_pass<FMT_FP8, 2>(a, it, ws, pass_cnt, sm);
+        else run_pass<FMT_FP8, 4>(a, it, ws, pass_cnt, sm);
+      } else if constexpr (FMT_R != FMT_FP8) {
+        if (pass_cnt <= 8) run_pass<FMT_R, 1>(a, it, ws, pass_cnt, sm);
+        else run_pass<FMT_R, 2>(a, it, ws, pass_cnt, sm);
+      }
+    }
+  }
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+cudaError_t launch_grouped(const GroupedArgs& a, int max_items, int grid_cap, cudaStream_t st) {
+  int grid = 2 * num_sms();
+  if (grid_cap > 0 && grid > grid_cap) grid = grid_cap;
+  if (grid > max_items) grid = max_items;
+  if (grid < 1) grid = 1;
+  switch (a.routed.fmt) {
+    case FMT_NVFP4: grouped_kernel<FMT_NVFP4><<<grid, 256, 0, st>>>(a); break;
+    case FMT_MXFP4: grouped_kernel<FMT_MXFP4><<<grid, 256, 0, st>>>(a); break;
+    default: grouped_kernel<FMT_FP8><<<grid, 256, 0, st>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+// y[t] = bf16( sum over t's slots in ascending expert id of o[t*K + slot] (fp32), + shared o[P + t] )
+// A slot whose expert a later slot of the same token names again is dropped (the reference's
+// `y[idx] +=` with repeated indices keeps only the last write; v4_moe_grouped.py:98-118).
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ o,
+                                                      const int32_t* __restrict__ topk_idx, int m, int K, int h,
+                                                      int has_shared, __nv_bfloat16* __restrict__ y) {
+  const int t = blockIdx.x;
+  __shared__ int order[16];
+  __shared__ int n_keep;
+  if (threadIdx.x == 0) {
+    int ids[16], slots[16], n = 0;
+    for (int j = 0; j < K; ++j) {
+      const int e = topk_idx[(size_t)t * K + j];
+      bool later = false;
+      for (int j2 = j + 1; j2 < K; ++j2) later |= topk_idx[(size_t)t * K + j2] == e;
+      if (later) continue;
+      int p = n++;
+      while (p > 0 && ids[p - 1] > e) {
+        ids[p] = ids[p - 1];
+        slots[p] = slots[p - 1];
+        --p;
+      }
+      ids[p] = e;
+      slots[p] = j;
+    }
+    for (int j = 0; j < n; ++j) order[j] = slots[j];
+    n_keep = n;
+  }
+  __syncthreads();
+  const int P = m * K;
+  const int nk = n_keep;
+  for (int v = threadIdx.x; v < h / 8; v += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+    for (int j = 0; j < nk; ++j) {
+      const uint4 r = *reinterpret_cast<const uint4*>(o + ((size_t)t * K + order[j]) * h + v * 8);
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(p[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    if (has_shared) {
+      const uint4 r = *reinterpret_cast<const uint4*>(o + ((size_t)P + t) * h + v * 8);
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(p[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    uint4 out;
+    __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) op[q] = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+    *reinterpret_cast<uint4*>(y + (size_t)t * h + v * 8) = out;
+  }
+}
+
+cudaError_t launch_combine(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h, int has_shared,
+                           __nv_bfloat16* y, cudaStream_t st) {
+  combine_kernel<<<m, 256, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
+  return cudaGetLastError();
+}
+
+// Standalone act_quant (the kernel seam): one warp per (row, 128-block).
+__global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t m, int64_t k, int pow2,
+                                 uint8_t* __restrict__ q, float* __restrict__ s) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nb = k / 128;
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (w >= m * nb) return;
+  const int64_t r = w / nb, b = w % nb;
+  const uint2 raw = *reinterpret_cast<const uint2*>(x + r * k + b * 128 + lane * 4);
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
+  float am = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
+  am = warp_max(am);
+  const float sc = act_scale(am, pow2 != 0);
+  const uint32_t v = (uint32_t)act_q(f0.x, sc) | ((uint32_t)act_q(f0.y, sc) << 8) |
+                     ((uint32_t)act_q(f1.x, sc) << 16) | ((uint32_t)act_q(f1.y, sc) << 24);
+  *reinterpret_cast<uint32_t*>(q + r * k + b * 128 + lane * 4) = v;
+  if (lane == 0) s[r * nb + b] = sc;
+}
+
+cudaError_t launch_act_quant(const void* x, int64_t m, int64_t k, int pow2, uint8_t* q, float* s, cudaStream_t st) {
+  const int64_t warps = m * (k / 128);
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  act_quant_kernel<<<(unsigned)blocks, 256, 0, st>>>((const __nv_bfloat16*)x, m, k, pow2, q, s);
+  return cudaGetLastError();
+}
+
+// Decodes fixed code sets with the same conversions the GEMV kernels use:
+// out[0:16] e2m1 codes 0..15, out[16:32] e4m3 codes {0x00..0x0f step 1 | a spread}, out[32:40]
+// e8m0 codes, out[40:48] pow2_ceil of fixed inputs, out[48:56] e4m3 round-trip of fixed inputs.
+__global__ void selftest_kernel(float* out) {
+  if (threadIdx.x != 0) return;
+  for (int c = 0; c < 16; c += 2) {
+    const uint32_t h2 = e2m1x2_to_f16x2((uint32_t)c | ((uint32_t)(c + 1) << 4));
+    out[c] = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+    out[c + 1] = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+  }
+  const uint8_t e4[16] = {0x00, 0x01, 0x07, 0x08, 0x30, 0x38, 0x3c, 0x40, 0x7e, 0x80, 0xb8, 0xfe, 0x11, 0x22, 0x55, 0x66};
+  for (int i = 0; i < 16; i += 2) {
+    const uint32_t h2 = e4m3x2_to_f16x2((uint32_t)e4[i] | ((uint32_t)e4[i + 1] << 8));
+    out[16 + i] = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+    out[16 + i + 1] = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+  }
+  const uint32_t e8[8] = {127, 126, 128, 120, 134, 1, 254, 100};
+  for (int i = 0; i < 8; ++i) out[32 + i] = e8m0_to_f32(e8[i]);
+  const float px[8] = {1.0f, 1.5f, 0.75f, 448.0f / 448.0f, 3.0e-3f, 2.0f, 1.0e-4f / 448.0f, 0.1f};
+  for (int i = 0; i < 8; ++i) out[40 + i] = pow2_ceil(px[i]);
+  const float qx[8] = {0.1f, -3.3f, 447.0f, 17.0f, 0.0009765625f, -0.3f, 250.0f, 1.0f / 3.0f};
+  for (int i = 0; i < 8; ++i) out[48 + i] = e4m3_to_f32(f32_to_e4m3(qx[i]));
+  for (int i = 56; i < 64; ++i) out[i] = 0.f;
+}
+
+cudaError_t launch_selftest(float* out, cudaStream_t st) {
+  selftest_kernel<<<1, 32, 0, st>>>(out);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

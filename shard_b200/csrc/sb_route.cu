@@ -1,0 +1,295 @@
+// Routing and token permutation of the MoE stage forward.
+//
+//   gate_logits_kernel   logits[M, E] = fp32(x) . fp32(W_gate)^T            (Gate.forward, model.py:570)
+//   route_kernel         score, selection bias, sorted top-k, weights renormalised and scaled
+//                        (model.py:571-589), hash routing through tid2eid (model.py:581-582), and
+//                        the per-128 e4m3 quantisation of x for the expert GEMVs (act_quant,
+//                        kernel.py:40-125)
+//   permute_kernel       per-expert (token, slot) lists in ascending expert id, tokens ascending
+//                        within an expert; the list of active experts; all on the device, so the
+//                        forward never drains to the host (the reference's bincount().tolist(),
+//                        model.py:639, is the sync this replaces)
+#include "sb_device.cuh"
+#include "sb_launch.h"
+
+namespace sb {
+
+// One warp per expert row, 8 tokens per CTA column: each warp streams its W row once (16-byte
+// loads) and multiplies it against 8 token rows (L1/L2 resident). bf16 x bf16 products are exact
+// in fp32, so only the summation order differs from the reference's fp32 F.linear.
+__global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ w,
+                                                          float* __restrict__ logits, int m, int e_total,
+                                                          int h) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + warp;
+  const int t0 = blockIdx.y * 8;
+  if (e >= e_total) return;
+  const int nt = min(8, m - t0);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)e * h);
+  const int nv = h / 8;
+  for (int v = lane; v < nv; v += 32) {
+    const uint4 wv = __ldg(wr + v);
+    const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    float wf[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(wp[q]);
+      wf[2 * q] = f.x;
+      wf[2 * q + 1] = f.y;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < nt) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + j) * h) + v);
+        const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(xp[q]);
+          acc[j] = fmaf(f.x, wf[2 * q], acc[j]);
+          acc[j] = fmaf(f.y, wf[2 * q + 1], acc[j]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float s = warp_sum(acc[j]);
+    if (lane == 0 && j < nt) logits[(size_t)(t0 + j) * e_total + e] = s;
+  }
+}
+
+constexpr int MAX_E_PER_LANE = 32;  // E <= 1024
+
+// One warp per token. Warp w of the CTA handles token blockIdx.x * 4 + w: top-k on lane-strided
+// scores, then the token's act_quant (all 128-blocks of x[t]).
+__global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + warp;
+  if (t >= a.m) return;
+  const int E = a.n_experts;
+  const float* lg = a.logits + (size_t)t * E;
+  float sc[MAX_E_PER_LANE];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+    const int e = lane + 32 * i;
+    sc[i] = e < E ? lg[e] : -INFINITY;
+    mx = fmaxf(mx, sc[i]);
+  }
+  if (a.score_func == SCORE_SOFTMAX) {
+    mx = warp_max(mx);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+      const int e = lane + 32 * i;
+      sc[i] = e < E ? expf(sc[i] - mx) : 0.f;
+      s += sc[i];
+    }
+    s = warp_sum(s);
+#pragma unroll
+    for (int i = 0; i < MAX_E_PER_LANE; ++i) sc[i] = __fdiv_rn(sc[i], s);
+  } else if (a.score_func == SCORE_SIGMOID) {
+#pragma unroll
+    for (int i = 0; i < MAX_E_PER_LANE; ++i) sc[i] = __fdiv_rn(1.0f, 1.0f + expf(-sc[i]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+      const float l = sc[i];
+      const float sp = l > 20.f ? l : log1pf(expf(l));
+      sc[i] = sqrtf(sp);
+    }
+  }
+  const int K = a.topk;
+  int sel[16];
+  float wsel[16];
+  if (a.tid2eid != nullptr) {
+    // hash routing: the ids come from the table, weights still from the unbiased scores
+    const int64_t id = a.input_ids[t];
+    for (int j = 0; j < K; ++j) {
+      int e = a.tid2eid[id * K + j];
+      e = e < 0 ? 0 : (e >= E ? E - 1 : e);  // the host validates the table; this only keeps
+      sel[j] = e;                             // a corrupt one from indexing out of bounds
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAX_E_PER_LANE; ++i)
+        if (lane + 32 * i == e) mine = sc[i];
+      wsel[j] = __shfl_sync(0xffffffffu, mine, e & 31);
+    }
+  } else {
+    float bsel[MAX_E_PER_LANE];
+#pragma unroll
+    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+      const int e = lane + 32 * i;
+      bsel[i] = e < E ? sc[i] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
+    }
+    unsigned taken = 0u;  // bit i: this lane's slot i already selected
+    for (int j = 0; j < K; ++j) {
+      float bv = -INFINITY;
+      int be = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && !(taken & (1u << i)) && (bsel[i] > bv || (bsel[i] == bv && e < be))) {
+          bv = bsel[i];
+          be = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+        if (ov > bv || (ov == bv && oe < be)) {
+          bv = ov;
+          be = oe;
+        }
+      }
+      if (be >= E) be = j;  // only reachable with NaN scores; keeps every id in range
+      sel[j] = be;
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAX_E_PER_LANE; ++i)
+        if (lane + 32 * i == be) {
+          mine = sc[i];
+          taken |= (1u << i);
+        }
+      wsel[j] = __shfl_sync(0xffffffffu, mine, be & 31);
+    }
+  }
+  if (a.score_func != SCORE_SOFTMAX) {
+    float s = 0.f;
+    for (int j = 0; j < K; ++j) s += wsel[j];
+    for (int j = 0; j < K; ++j) wsel[j] = __fdiv_rn(wsel[j], s);
+  }
+  for (int j = 0; j < K; ++j) wsel[j] *= a.route_scale;
+  if (lane == 0) {
+    for (int j = 0; j < K; ++j) {
+      a.topk_idx[(size_t)t * K + j] = sel[j];
+      a.topk_w[(size_t)t * K + j] = wsel[j];
+      if (a.out_idx) a.out_idx[(size_t)t * K + j] = sel[j];
+      if (a.out_w) a.out_w[(size_t)t * K + j] = wsel[j];
+    }
+  }
+  // act_quant of x[t]: one 128-block per warp iteration, 4 values per lane
+  if (a.xq != nullptr) {
+    const __nv_bfloat16* xr = a.x + (size_t)t * a.hidden;
+    for (int b = 0; b < a.hidden / 128; ++b) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(xr + b * 128 + lane * 4);
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
+      float am = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
+      am = warp_max(am);
+      const float s = act_scale(am, a.act_pow2);
+      const uint32_t q = (uint32_t)act_q(f0.x, s) | ((uint32_t)act_q(f0.y, s) << 8) |
+                         ((uint32_t)act_q(f1.x, s) << 16) | ((uint32_t)act_q(f1.y, s) << 24);
+      *reinterpret_cast<uint32_t*>(a.xq + (size_t)t * a.hidden + b * 128 + lane * 4) = q;
+      if (lane == 0) a.xs[(size_t)t * (a.hidden / 128) + b] = s;
+    }
+  }
+}
+
+// Single CTA. counts -> exclusive offsets -> stable placement (pair p = t*K + j, ascending p
+// within each expert, i.e. ascending token) -> active expert list. Deterministic.
+__global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
+  extern __shared__ int smem[];
+  int* cnt = smem;                   // [E]
+  int* cursor = smem + a.n_experts;  // [E]
+  __shared__ int warp_tot[32];
+  const int E = a.n_experts, P = a.m * a.topk;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) atomicAdd(&cnt[a.topk_idx[p]], 1);
+  __syncthreads();
+  // exclusive scan of cnt over E (E <= 1024 = blockDim), and of the active flags
+  const int e = threadIdx.x;
+  const int c = e < E ? cnt[e] : 0;
+  const int flag = c > 0 ? 1 : 0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = c, fincl = flag;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    const int fv = __shfl_up_sync(0xffffffffu, fincl, o);
+    if (lane >= o) {
+      incl += v;
+      fincl += fv;
+    }
+  }
+  __shared__ int warp_ftot[32];
+  if (lane == 31) {
+    warp_tot[warp] = incl;
+    warp_ftot[warp] = fincl;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int v = warp_tot[lane], fv = warp_ftot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      const int fu = __shfl_up_sync(0xffffffffu, fv, o);
+      if (lane >= o) {
+        v += u;
+        fv += fu;
+      }
+    }
+    warp_tot[lane] = v;
+    warp_ftot[lane] = fv;
+  }
+  __syncthreads();
+  const int base = warp > 0 ? warp_tot[warp - 1] : 0;
+  const int fbase = warp > 0 ? warp_ftot[warp - 1] : 0;
+  if (e < E) {
+    const int off = base + incl - c;
+    a.offsets[e] = off;
+    a.counts[e] = c;
+    cursor[e] = off;
+    if (flag) a.active[fbase + fincl - 1] = e;
+    if (e == E - 1) {
+      a.offsets[E] = base + incl;
+      *a.n_active = fbase + fincl;
+    }
+  }
+  __syncthreads();
+  // stable placement by one warp, 32 pairs at a time in ascending p
+  if (warp == 0) {
+    for (int p0 = 0; p0 < P; p0 += 32) {
+      const int p = p0 + lane;
+      const int ex = p < P ? a.topk_idx[p] : -1 - lane;
+      const unsigned same = __match_any_sync(0xffffffffu, ex);
+      const int rank = __popc(same & ((1u << lane) - 1u));
+      const int leader = __ffs(same) - 1;
+      int pos = 0;
+      if (p < P) pos = cursor[ex] + rank;
+      __syncwarp();
+      if (p < P && lane == leader) cursor[ex] += __popc(same);
+      __syncwarp();
+      if (p < P) {
+        a.pair_tok[pos] = p / a.topk;
+        a.pair_slot[pos] = p % a.topk;
+      }
+    }
+  }
+}
+
+cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int m, int e, int h,
+                               cudaStream_t st) {
+  dim3 grid((e + 7) / 8, (m + 7) / 8);
+  gate_logits_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w, logits, m, e, h);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
+  route_kernel<<<(a.m + 3) / 4, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t st) {
+  const size_t smem = (size_t)2 * a.n_experts * sizeof(int);
+  permute_kernel<<<1, 1024, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

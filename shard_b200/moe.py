@@ -1,0 +1,281 @@
+"""The MoE stage forward on the B200, behind the reference's own operator seam.
+
+`MoELayer` holds one layer's weights in HBM in the tiled layout and runs the forward through the
+C ABI (route -> permute -> grouped w13 + SwiGLU + act_quant -> grouped w2 -> combine), all on the
+caller's stream with no host sync.
+
+`install(mod)` rebinds `mod.MoE.forward` of the reference model module (the vendored model.py,
+loaded by engines/deepseek_v4/v4_ref_cpu.load_ref) exactly as the reference's own levers do
+(engines/deepseek_v4/v4_moe_grouped.py:736-755, v4_moe_decode.py:71-94): it captures the forward in
+place as the fallback, marks itself to refuse double installs, and declines (with a tally, like
+`_decline`, v4_moe_grouped.py:607-620) only what it does not claim: world_size > 1 (the reference
+all-reduces the routed sum across ranks, model.py:646-647) and modules whose tensors are not on a
+CUDA device. Everything else it claims, including multi-token verify chunks, prefill and hash
+layers. If the CUDA library is missing on a CUDA module it raises instead of falling back.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from . import formats as F
+from ._lib import SbMoeLayer, check, lib, ptr, stream_ptr
+
+_SCORE = _lib.SCORE
+
+
+def _u8(t):
+    return t.contiguous().view(torch.uint8)
+
+
+def tile(fmt: int, kind: int, w: torch.Tensor, s: torch.Tensor, n_mat: int, n: int, k: int):
+    """Canonical [n_mat, N, K] weights (+ scales) on the device -> tiled (values, scales)."""
+    L = lib()
+    dev = w.device
+    wt = torch.empty(n_mat * L.sb_tiled_bytes(fmt, n, k), dtype=torch.uint8, device=dev)
+    st = torch.empty(n_mat * L.sb_tiled_scale_bytes(fmt, n, k), dtype=torch.uint8, device=dev)
+    sp = stream_ptr()
+    check(L.sb_tile_weights(fmt, kind, ptr(_u8(w)), ptr(wt), n_mat, n, k, sp), "sb_tile_weights")
+    src_s = s.contiguous().float() if fmt == F.FMT_FP8 else _u8(s)
+    check(L.sb_tile_scales(fmt, kind, ptr(src_s), ptr(st), n_mat, n, k, sp), "sb_tile_scales")
+    return wt, st
+
+
+class MoELayer:
+    """One MoE layer resident on a B200, in the layout the forward streams.
+
+    Canonical inputs (the reference's bank form, v4_moe_grouped.py:382-540), all on the device:
+      gate_w bf16 [E, H]; gate_bias fp32 [E] or None; tid2eid int32 [vocab, k] or None
+      w13: fp4 uint8 [E, 2I, H/2] | fp8 uint8 [E, 2I, H]   (w1 rows then w3 rows)
+      w13_s: nvfp4 e4m3 [E, 2I, H/16] | mxfp4 e8m0 [E, 2I, H/32] | fp8 fp32 [E, 2I/128, H/128]
+      w13_ts fp32 [E, 2] (NVFP4), w2 / w2_s / w2_ts likewise for [E, H, I]
+      shared: (w13 e4m3 [2I, H], w13_s fp32 [2I/128, H/128], w2 e4m3 [H, I], w2_s fp32) or None
+    """
+
+    def __init__(self, *, hidden, inter, n_experts, topk, expert_fmt, gate_w, gate_bias=None, tid2eid=None,
+                 score_func="sigmoid", route_scale=1.0, swiglu_limit=0.0, act_pow2=True,
+                 w13, w13_s, w13_ts=None, w2, w2_s, w2_ts=None, shared=None, tiled=False):
+        self.hidden, self.inter, self.n_experts, self.topk = hidden, inter, n_experts, topk
+        self.expert_fmt = expert_fmt
+        self.device = gate_w.device
+        self.gate_w = gate_w.contiguous().to(torch.bfloat16)
+        self.gate_bias = None if gate_bias is None else gate_bias.contiguous().float()
+        self.tid2eid = None if tid2eid is None else tid2eid.contiguous().to(torch.int32)
+        e, h, i = n_experts, hidden, inter
+        if tiled:
+            self.w13, self.w13_s, self.w2, self.w2_s = w13, w13_s, w2, w2_s
+        else:
+            self.w13, self.w13_s = tile(expert_fmt, _lib.MAT_W13, w13, w13_s, e, 2 * i, h)
+            self.w2, self.w2_s = tile(expert_fmt, _lib.MAT_PLAIN, w2, w2_s, e, h, i)
+        self.w13_ts = None if w13_ts is None else w13_ts.contiguous().float()
+        self.w2_ts = None if w2_ts is None else w2_ts.contiguous().float()
+        self.shared = None
+        if shared is not None:
+            if tiled:
+                self.shared = shared
+            else:
+                s13, s13s, s2, s2s = shared
+                a, b = tile(F.FMT_FP8, _lib.MAT_W13, s13, s13s, 1, 2 * i, h)
+                c, d = tile(F.FMT_FP8, _lib.MAT_PLAIN, s2, s2s, 1, h, i)
+                self.shared = (a, b, c, d)
+        self.desc = SbMoeLayer()
+        d = self.desc
+        d.hidden, d.inter, d.n_experts, d.topk = h, i, e, topk
+        d.expert_fmt = expert_fmt
+        d.has_shared = 1 if self.shared is not None else 0
+        d.score_func = _SCORE[score_func]
+        d.act_pow2 = 1 if act_pow2 else 0
+        d.route_scale = float(route_scale)
+        d.swiglu_limit = float(swiglu_limit)
+        d.gate_w = ptr(self.gate_w)
+        d.gate_bias = ptr(self.gate_bias)
+        d.tid2eid = ptr(self.tid2eid)
+        d.vocab = 0 if self.tid2eid is None else self.tid2eid.shape[0]
+        d.w13, d.w13_s, d.w13_ts = ptr(self.w13), ptr(self.w13_s), ptr(self.w13_ts)
+        d.w2, d.w2_s, d.w2_ts = ptr(self.w2), ptr(self.w2_s), ptr(self.w2_ts)
+        if self.shared is not None:
+            d.sh_w13, d.sh_w13_s, d.sh_w2, d.sh_w2_s = (ptr(t) for t in self.shared)
+        self._ws = None
+        self.score_func, self.route_scale, self.swiglu_limit, self.act_pow2 = score_func, route_scale, swiglu_limit, act_pow2
+
+    # ── scratch ───────────────────────────────────────────────────────────────────────────────
+    def workspace_bytes(self, m: int) -> int:
+        n = lib().sb_moe_workspace_bytes(ctypes.byref(self.desc), m)
+        if n == 0:
+            check(-2, "sb_moe_workspace_bytes")
+        return n
+
+    def reserve(self, m: int):
+        """Pre-size the workspace for up to m tokens (do this before capturing a CUDA graph)."""
+        need = self.workspace_bytes(m)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def weight_bytes(self) -> int:
+        ts = [self.gate_w, self.w13, self.w13_s, self.w2, self.w2_s]
+        ts += [t for t in (self.gate_bias, self.w13_ts, self.w2_ts) if t is not None]
+        ts += list(self.shared or ())
+        return sum(t.numel() * t.element_size() for t in ts)
+
+    # ── forward ───────────────────────────────────────────────────────────────────────────────
+    def forward(self, x: torch.Tensor, input_ids: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                routing: bool = False, stream=None):
+        """x bf16 [M, H] (cuda) -> y bf16 [M, H]; with routing=True also (weights fp32 [M,k], indices int64 [M,k])."""
+        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] == self.hidden
+        x = x.contiguous()
+        m = x.shape[0]
+        y = out if out is not None else torch.empty_like(x)
+        ws = self.reserve(m)
+        w = idx = None
+        if routing:
+            w = torch.empty(m, self.topk, dtype=torch.float32, device=x.device)
+            idx = torch.empty(m, self.topk, dtype=torch.int64, device=x.device)
+        ids = None
+        if self.tid2eid is not None:
+            ids = input_ids.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
+        check(lib().sb_moe_forward(ctypes.byref(self.desc), ptr(x), m, ptr(ids), ptr(y), ptr(w), ptr(idx),
+                                   ptr(ws), ws.numel(), stream_ptr(stream)), "sb_moe_forward")
+        if routing:
+            return y, w, idx
+        return y
+
+    __call__ = forward
+
+    def route(self, x: torch.Tensor, input_ids: Optional[torch.Tensor] = None):
+        """Gate.forward alone: (weights fp32 [M, k], indices int64 [M, k])."""
+        x = x.contiguous()
+        m = x.shape[0]
+        ws = self.reserve(m)
+        w = torch.empty(m, self.topk, dtype=torch.float32, device=x.device)
+        idx = torch.empty(m, self.topk, dtype=torch.int64, device=x.device)
+        ids = None
+        if self.tid2eid is not None:
+            ids = input_ids.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
+        check(lib().sb_moe_route(ctypes.byref(self.desc), ptr(x), m, ptr(ids), ptr(w), ptr(idx), ptr(ws),
+                                 ws.numel(), stream_ptr()), "sb_moe_route")
+        return w, idx
+
+
+# ── building a layer from the reference's own MoE module ─────────────────────────────────────────
+
+def _scale_to_f32_pow2(s: torch.Tensor) -> torch.Tensor:
+    """A reference fp8 weight scale (e8m0 or fp32) -> fp32."""
+    if s.dtype == torch.float8_e8m0fnu:
+        return F.e8m0_decode(s.view(torch.uint8))
+    return s.float()
+
+
+def _expert_format(lin) -> int:
+    w = lin.weight
+    if w.dtype == torch.float4_e2m1fn_x2 or (w.dtype == torch.uint8 and w.shape[1] * 2 == lin.in_features):
+        return F.FMT_NVFP4 if lin.weight.scale.dtype == torch.float8_e4m3fn else F.FMT_MXFP4
+    if w.dtype == torch.float8_e4m3fn:
+        return F.FMT_FP8
+    raise NotImplementedError(f"expert weight dtype {w.dtype} has no B200 kernel")
+
+
+def layer_from_module(moe, act_pow2: bool) -> MoELayer:
+    """Lay a reference `MoE` module (model.py:614-632) out as a MoELayer on its device.
+
+    Reads exactly what MoE.forward reads: gate weight/bias/tid2eid/score_func/route_scale/topk,
+    each routed Expert's w1/w3/w2 (weight, scale, and for NVFP4 a `tensor_scale` attribute), the
+    shared expert, and swiglu_limit."""
+    gate = moe.gate
+    lo, hi = moe.experts_start_idx, moe.experts_end_idx
+    experts = [moe.experts[j] for j in range(lo, hi)]
+    fmt = _expert_format(experts[0].w1)
+    e = len(experts)
+
+    def stack(kind):
+        ws, ss, ts = [], [], []
+        for ex in experts:
+            lins = (ex.w1, ex.w3) if kind == "w13" else (ex.w2,)
+            ws.append(torch.cat([_u8(l.weight) for l in lins]))
+            if fmt == F.FMT_FP8:
+                ss.append(torch.cat([_scale_to_f32_pow2(l.weight.scale) for l in lins]))
+            else:
+                ss.append(torch.cat([_u8(l.weight.scale) for l in lins]))
+            ts.append(torch.tensor([float(getattr(l.weight, "tensor_scale", 1.0)) for l in lins]))
+        return torch.stack(ws), torch.stack(ss), torch.stack(ts).to(ws[0].device)
+
+    w13, w13_s, w13_ts = stack("w13")
+    w2, w2_s, w2_ts = stack("w2")
+    sh = moe.shared_experts
+    shared = (torch.cat([_u8(sh.w1.weight), _u8(sh.w3.weight)]),
+              torch.cat([_scale_to_f32_pow2(sh.w1.weight.scale), _scale_to_f32_pow2(sh.w3.weight.scale)]),
+              _u8(sh.w2.weight), _scale_to_f32_pow2(sh.w2.weight.scale))
+    return MoELayer(
+        hidden=moe.dim, inter=experts[0].w1.out_features, n_experts=e, topk=gate.topk, expert_fmt=fmt,
+        gate_w=gate.weight.detach(), gate_bias=None if gate.bias is None else gate.bias.detach(),
+        tid2eid=gate.tid2eid.detach() if gate.hash else None, score_func=gate.score_func,
+        route_scale=gate.route_scale, swiglu_limit=experts[0].swiglu_limit, act_pow2=act_pow2,
+        w13=w13, w13_s=w13_s, w13_ts=w13_ts if fmt == F.FMT_NVFP4 else None,
+        w2=w2, w2_s=w2_s, w2_ts=w2_ts.reshape(e) if fmt == F.FMT_NVFP4 else None, shared=shared)
+
+
+# ── the operator seam ──────────────────────────────────────────────────────────────────────────
+
+_REF_FORWARD = None
+_MOD = None
+
+
+def _decline(moe, why, x, input_ids):
+    tally = getattr(moe, "_b200_declined", None)
+    if tally is None:
+        tally = moe._b200_declined = {}
+    tally[why] = tally.get(why, 0) + 1
+    return _REF_FORWARD(moe, x, input_ids)
+
+
+def b200_moe_forward(self, x, input_ids):
+    """MoE.forward(self, x [b,s,dim] bf16, input_ids [b,s] int64) -> [b,s,dim] bf16 on the B200."""
+    world = int(getattr(_MOD, "world_size", 1) or 1)
+    if world > 1:
+        return _decline(self, "world_size>1", x, input_ids)
+    if not x.is_cuda:
+        return _decline(self, "not-on-cuda", x, input_ids)
+    layer = getattr(self, "_b200_layer", None)
+    if layer is None:
+        layer = self._b200_layer = layer_from_module(self, act_pow2=getattr(_MOD, "scale_fmt", None) is not None)
+    shape = x.shape
+    y = layer.forward(x.reshape(-1, self.dim).to(torch.bfloat16), input_ids)
+    self._b200_steps = getattr(self, "_b200_steps", 0) + 1
+    return y.to(x.dtype).view(shape)
+
+
+def install(mod) -> bool:
+    """Rebind mod.MoE.forward to the B200 forward; the previous forward becomes the fallback.
+    Idempotent. Fails loudly if a CUDA device is present but the library is not."""
+    global _REF_FORWARD, _MOD
+    if getattr(mod.MoE.forward, "_b200", False):
+        return False
+    if torch.cuda.is_available():
+        lib()                     # raises if libshard_b200.so is missing: no silent fallback
+    _REF_FORWARD = mod.MoE.forward
+    _MOD = mod
+    b200_moe_forward._b200 = True
+    mod.MoE.forward = b200_moe_forward
+    return True
+
+
+def uninstall(mod) -> bool:
+    global _REF_FORWARD
+    if not getattr(mod.MoE.forward, "_b200", False):
+        return False
+    mod.MoE.forward = _REF_FORWARD
+    _REF_FORWARD = None
+    return True
+
+
+def coverage(module):
+    """{layer_id: (steps on the B200, {decline reason: count})} for every MoE under `module`."""
+    out = {}
+    for m in module.modules() if hasattr(module, "modules") else [module]:
+        if hasattr(m, "experts") and hasattr(m, "experts_start_idx"):
+            out[getattr(m, "layer_id", len(out))] = (getattr(m, "_b200_steps", 0),
+                                                     dict(getattr(m, "_b200_declined", {})))
+    return out

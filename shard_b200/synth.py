@@ -161,3 +161,98 @@ def tensor_sha(*ts) -> str:
         h.update(t.view(torch.uint8).numpy().tobytes() if t.dtype != torch.float32
                  else t.numpy().tobytes())
     return h.hexdigest()
+
+
+# ── device layers ─────────────────────────────────────────────────────────────────────────────
+
+def _random_canonical(fmt, n_mat, n, k, device, gen):
+    """Valid random canonical bytes (values and scales) for experts whose values no test reads."""
+    if fmt == F.FMT_FP8:
+        w = torch.randint(0, 255, (n_mat, n, k), dtype=torch.uint8, device=device, generator=gen)
+        w = torch.where((w & 0x7F) == 0x7F, w ^ 1, w)
+        s = torch.ldexp(torch.ones(n_mat, n // 128, k // 128, device=device),
+                        torch.randint(-8, -4, (n_mat, n // 128, k // 128), device=device, generator=gen))
+        return w, s
+    w = torch.randint(0, 256, (n_mat, n, k // 2), dtype=torch.uint8, device=device, generator=gen)
+    if fmt == F.FMT_NVFP4:
+        s = torch.randint(0x20, 0x38, (n_mat, n, k // 16), dtype=torch.uint8, device=device, generator=gen)
+    else:
+        s = torch.randint(118, 124, (n_mat, n, k // 32), dtype=torch.uint8, device=device, generator=gen)
+    return w, s
+
+
+def _normal_expert_on_device(cfg, layer, expert, fmt, device):
+    """N(0, 0.02) draws quantised on the device (fast path for benchmark layers)."""
+    h, i = cfg.hidden, cfg.inter
+    g = _gen(device, cfg.seed, layer, expert, "dev")
+    w1 = (torch.randn(i, h, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    w3 = (torch.randn(i, h, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(h, i, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    p1, s1, t1 = _quant(fmt, w1)
+    p3, s3, t3 = _quant(fmt, w3)
+    p2, s2, t2 = _quant(fmt, w2)
+    return ExpertWeights(torch.cat([p1, p3]), torch.cat([s1, s3]),
+                         torch.tensor([t1, t3], dtype=torch.float32, device=device),
+                         p2, s2, torch.tensor([t2], dtype=torch.float32, device=device))
+
+
+def device_layer(cfg: MoEConfig, layer: int = 0, device="cuda", seeded=None, fill="random", act_pow2=True):
+    """A MoELayer on `device` for config `cfg`.
+
+    seeded: expert ids generated from their CPU-seeded draws (the bytes the oracle and the golden
+            vectors use); None means all of them.
+    fill:   how the other experts are made: "random" (valid random bytes, for experts no check
+            reads) or "normal" (N(0, 0.02) drawn and quantised on the device, for benchmarks).
+    The shared expert and the gate are always the seeded ones."""
+    from .moe import MoELayer
+    e, h, i, fmt = cfg.n_experts, cfg.hidden, cfg.inter, cfg.expert_fmt
+    seeded = set(range(e)) if seeded is None else set(int(v) for v in seeded)
+    gw, gb = make_gate(cfg, layer)
+    if fmt == F.FMT_FP8:
+        w13 = torch.empty(e, 2 * i, h, dtype=torch.uint8, device=device)
+        w13_s = torch.empty(e, 2 * i // 128, h // 128, dtype=torch.float32, device=device)
+        w2 = torch.empty(e, h, i, dtype=torch.uint8, device=device)
+        w2_s = torch.empty(e, h // 128, i // 128, dtype=torch.float32, device=device)
+    else:
+        g = 16 if fmt == F.FMT_NVFP4 else 32
+        w13 = torch.empty(e, 2 * i, h // 2, dtype=torch.uint8, device=device)
+        w13_s = torch.empty(e, 2 * i, h // g, dtype=torch.uint8, device=device)
+        w2 = torch.empty(e, h, i // 2, dtype=torch.uint8, device=device)
+        w2_s = torch.empty(e, h, i // g, dtype=torch.uint8, device=device)
+    w13_ts = torch.ones(e, 2, dtype=torch.float32, device=device)
+    w2_ts = torch.ones(e, dtype=torch.float32, device=device)
+    rest = [x for x in range(e) if x not in seeded]
+    if rest and fill == "random":
+        gen = _gen(device, cfg.seed, layer, "filler")
+        a, b = _random_canonical(fmt, len(rest), 2 * i, h, device, gen)
+        c, d = _random_canonical(fmt, len(rest), h, i, device, gen)
+        idx = torch.tensor(rest, device=device)
+        w13[idx], w13_s[idx], w2[idx], w2_s[idx] = a, b, c, d
+        if fmt == F.FMT_NVFP4:
+            w13_ts[idx] = 1e-3
+            w2_ts[idx] = 1e-3
+        del a, b, c, d
+    for x in range(e):
+        if x in seeded:
+            ew = make_expert(cfg, layer, x)
+        elif fill == "normal":
+            ew = _normal_expert_on_device(cfg, layer, x, fmt, device)
+        else:
+            continue
+        w13[x].copy_(ew.w13)
+        w13_s[x].copy_(ew.w13_s)
+        w2[x].copy_(ew.w2)
+        w2_s[x].copy_(ew.w2_s)
+        w13_ts[x].copy_(ew.w13_ts)
+        w2_ts[x].copy_(ew.w2_ts.reshape(()))
+    shared = None
+    if cfg.n_shared:
+        sh = make_expert(cfg, layer, -1, F.FMT_FP8)
+        shared = tuple(t.to(device) for t in (sh.w13, sh.w13_s, sh.w2, sh.w2_s))
+    lay = MoELayer(hidden=h, inter=i, n_experts=e, topk=cfg.topk, expert_fmt=fmt, gate_w=gw.to(device),
+                   gate_bias=gb.to(device), score_func=cfg.score_func, route_scale=cfg.route_scale,
+                   swiglu_limit=cfg.swiglu_limit, act_pow2=act_pow2, w13=w13, w13_s=w13_s,
+                   w13_ts=w13_ts if fmt == F.FMT_NVFP4 else None, w2=w2, w2_s=w2_s,
+                   w2_ts=w2_ts if fmt == F.FMT_NVFP4 else None, shared=shared)
+    del w13, w13_s, w2, w2_s
+    return lay
