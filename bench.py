@@ -1,0 +1,413 @@
+"""MoE stage forward benchmark on B200 (see --help).
+
+Workload (all N): the V4-Flash-shaped MoE layer of config c1 (H=4096, 256 routed experts top-8,
+I=2048, NVFP4 routed experts, FP8 128x128 shared expert, sigmoid router), verify chunks of M=16
+tokens, 6 distinct layers per GPU. At N GPUs the 6N-layer stack is pipeline-partitioned into
+contiguous 6-layer blocks, one per rank (N=8 is config c2's 48 layers), with NCCL send/recv of the
+bf16 activations between stages and 8 chunks streamed per step. Per-GPU work is fixed: weak scaling.
+
+  value   = token-layers per second over the whole job: chunks * M tokens * layers / time, with
+            the inputs already in HBM (one layer's MoE forward on M tokens = M token-layers; at N=1
+            this is the single-layer c1 tokens/s at M=16).
+  e2e     = the same through the public API with host buffers: every chunk is copied in from pinned
+            host memory on stage 0 and its output read back to the host on the last stage.
+  roofline = the grouped expert kernel (the w13 and w2 launches) on the headline workload, from CUDA
+            events around its launches: algorithmic bytes (distinct routed experts' NVFP4 weights
+            and scales + the shared expert) / time, against MEASURED_PEAKS.json's HBM copy figure.
+  cpu_baseline = the CPU oracle (numpy restatement of the reference MoE.forward) on a sample of the
+            same workload on the host cores.
+
+--impl reference times that CPU path alone (rank 0), as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HEADLINE_M = 16
+LAYERS_PER_GPU = 6
+CHUNKS_PER_STEP = 8
+METRIC = "MoE stage tokens/s (token-layers/s), verify M=16, c1/c2 V4-Flash MoE layer"
+UNIT = "tokens/s"
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+# ── peaks ────────────────────────────────────────────────────────────────────────────────────────
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ── clocks ───────────────────────────────────────────────────────────────────────────────────────
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, path):
+        self.path = path
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self, gpus):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) < 9:
+                    continue
+                try:
+                    idx = int(p[0])
+                except ValueError:
+                    continue
+                if idx not in gpus:
+                    continue
+                try:
+                    sm.append(float(p[1]))
+                    smax.append(float(p[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, p[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ── workload ─────────────────────────────────────────────────────────────────────────────────────
+
+def build_layers(rank, n_layers, device):
+    from shard_b200 import synth as S
+    cfg = S.CONFIGS["c1"]
+    layers = []
+    for j in range(n_layers):
+        layers.append(S.device_layer(cfg, layer=rank * n_layers + j, device=device, seeded=[], fill="normal"))
+    return cfg, layers
+
+
+def chunk_inputs(cfg, n, device, seed_step=0):
+    from shard_b200 import synth as S
+    xs = []
+    for j in range(n):
+        x, _ = S.make_inputs(cfg, HEADLINE_M, step=seed_step * 1000 + j)
+        xs.append(x.to(device))
+    return xs
+
+
+def algorithmic_bytes(cfg, idx_list, m):
+    """Per-forward algorithmic bytes: distinct routed experts + shared + gate + x in / y out."""
+    from shard_b200 import formats as F
+    h, i = cfg.hidden, cfg.inter
+    per_e = F.weight_bytes(cfg.expert_fmt, 2 * i, h) + F.weight_bytes(cfg.expert_fmt, h, i)
+    shared = F.weight_bytes(F.FMT_FP8, 2 * i, h) + F.weight_bytes(F.FMT_FP8, h, i) if cfg.n_shared else 0
+    gate = cfg.n_experts * h * 2
+    out = []
+    for idx in idx_list:
+        d = len(np.unique(idx))
+        grouped = d * per_e + shared
+        out.append((grouped, grouped + gate + 2 * m * h * 2))
+    return out
+
+
+def time_grouped(layers, cfg, m, reps=3):
+    """CUDA events around the grouped kernel's launches (w13 + w2) of each layer, per forward."""
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize()
+    rows = []
+    xs = chunk_inputs(cfg, reps * len(layers), layers[0].device, seed_step=7)
+    k = 0
+    for r in range(reps):
+        for lay in layers:
+            y, idx, t = lay.forward_profiled(xs[k], evs)
+            k += 1
+            torch.cuda.synchronize()
+            rows.append((idx.cpu().numpy(), t))
+    return rows
+
+
+def cpu_oracle_sample(cfg, n_tokens=2, layer=0, reps=1):
+    """The CPU oracle on a bounded sample: n_tokens tokens of one c1 layer, all host threads."""
+    from oracle import moe_oracle as O
+    from shard_b200 import formats as F
+    from shard_b200 import synth as S
+    x, _ = S.make_inputs(cfg, HEADLINE_M, step=0)
+    x = x[:n_tokens].float().numpy()
+    gw, gb = S.make_gate(cfg, layer)
+    _, idx, _ = O.gate(x, gw.float().numpy(), gb.numpy(), cfg.score_func, cfg.route_scale, cfg.topk)
+    cache = {}
+    for e in sorted(set(idx.ravel().tolist())):
+        ew = S.make_expert(cfg, layer, e)
+        cache[e] = tuple(t.numpy() for t in (ew.w13, ew.w13_s, ew.w13_ts, ew.w2, ew.w2_s, ew.w2_ts))
+    sh = S.make_expert(cfg, layer, -1, F.FMT_FP8)
+    lay = O.OracleLayer(hidden=cfg.hidden, inter=cfg.inter, topk=cfg.topk, score_func=cfg.score_func,
+                        route_scale=cfg.route_scale, swiglu_limit=cfg.swiglu_limit, expert_fmt=cfg.expert_fmt,
+                        gate_w=gw.float().numpy(), gate_b=gb.numpy(), expert=lambda e: cache[e],
+                        shared=tuple(t.numpy() for t in (sh.w13, sh.w13_s, sh.w13_ts, sh.w2, sh.w2_s, sh.w2_ts)))
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.moe_forward(lay, x, workers=cores)
+        ts.append(time.perf_counter() - t0)
+    return n_tokens / min(ts), cores, f"c1 layer {layer}, {n_tokens} of the M={HEADLINE_M} chunk's tokens, " \
+        f"{len(cache)} routed experts + shared, numpy fp32 dequant-then-matmul"
+
+
+# ── arms ─────────────────────────────────────────────────────────────────────────────────────────
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    from shard_b200 import synth as S
+    cfg = S.CONFIGS["c1"]
+    vals = []
+    for s in range(args.warmup + args.steps):
+        v, cores, sample = cpu_oracle_sample(cfg, n_tokens=1, layer=s % LAYERS_PER_GPU)
+        if s >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) NVFP4 weights, N(0,1) bf16 tokens)",
+            "config": {"workload": "c1 MoE layer, 1 token per step (bounded CPU sample)", "m": HEADLINE_M},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_gpu(args, rank, world, local_rank):
+    import torch.distributed as dist
+    from shard_b200.pipeline import Pipeline, StageStack
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    cfg, layers = build_layers(rank, LAYERS_PER_GPU, device)
+    pipe = Pipeline(StageStack(layers), HEADLINE_M, cfg.hidden, rank, world, device)
+    C = CHUNKS_PER_STEP
+    xs_dev = chunk_inputs(cfg, C, device) if rank == 0 else None
+    outs_dev = [torch.empty(HEADLINE_M, cfg.hidden, dtype=torch.bfloat16, device=device) for _ in range(C)] \
+        if rank == world - 1 else None
+    for lay in layers:
+        lay.reserve(HEADLINE_M)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(step_fn, steps, warmup):
+        for _ in range(warmup):
+            step_fn()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step_fn()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / 1000.0)
+
+    # device-resident value
+    def step_dev():
+        pipe.run(C, xs_dev, outs_dev)
+
+    clk = ClockSampler(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
+                                    f"clocks_bench_r{rank}.csv"))
+    with clk:
+        t = timed(step_dev, args.steps, args.warmup)
+    tok_layers = args.steps * C * HEADLINE_M * LAYERS_PER_GPU * world
+    value = tok_layers / t
+
+    # end to end: pinned host in, pinned host out, through the public API
+    xs_host = [x.cpu().pin_memory() for x in xs_dev] if rank == 0 else None
+    outs_host = [torch.empty(HEADLINE_M, cfg.hidden, dtype=torch.bfloat16).pin_memory() for _ in range(C)] \
+        if rank == world - 1 else None
+    stage_in = [torch.empty(HEADLINE_M, cfg.hidden, dtype=torch.bfloat16, device=device) for _ in range(C)] \
+        if rank == 0 else None
+
+    def step_e2e():
+        if rank == 0:
+            for j in range(C):
+                stage_in[j].copy_(xs_host[j], non_blocking=True)
+        pipe.run(C, stage_in, outs_host)
+
+    t_e2e = timed(step_e2e, args.steps, max(args.warmup, 3))
+    e2e_value = tok_layers / t_e2e
+    bytes_io = C * HEADLINE_M * cfg.hidden * 2
+
+    # roofline of the grouped kernel on this rank's layers (rank 0 reports)
+    roof = None
+    sweep = {}
+    if rank == 0:
+        rows = time_grouped(layers, cfg, HEADLINE_M, reps=2)
+        peak, kind = hbm_peak()
+        nb = algorithmic_bytes(cfg, [r[0] for r in rows], HEADLINE_M)
+        g_bytes = sum(b[0] for b in nb) / len(nb)
+        g_time = sum(r[1]["grouped"] for r in rows) / len(rows)
+        f_bytes = sum(b[1] for b in nb) / len(nb)
+        f_time = sum(r[1]["total"] for r in rows) / len(rows)
+        roof = {"kernel": "grouped_kernel (w13 + w2 launches)", "bound": "hbm",
+                "achieved": g_bytes / g_time / 1e9, "peak": peak, "unit": "GB/s",
+                "frac": g_bytes / g_time / 1e9 / peak, "traffic": None,
+                "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback",
+                "algorithmic_bytes_per_forward": g_bytes, "grouped_us_per_forward": g_time * 1e6,
+                "forward_us": f_time * 1e6, "forward_frac": f_bytes / f_time / 1e9 / peak,
+                "phase_us": {k: sum(r[1][k] for r in rows) / len(rows) * 1e6
+                             for k in ("route", "permute", "w13", "w2", "combine")}}
+        if world == 1 and not args.no_sweep:
+            sweep = m_sweep(layers, cfg)
+    clocks = clk.summary(set(range(world)) if world > 1 else {local_rank}) if rank == 0 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, sample = cpu_oracle_sample(cfg, n_tokens=2)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": t / args.steps * 1000.0, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4",
+                "data": "synthetic (seeded N(0,0.02) weights quantised NVFP4 / FP8, N(0,1) bf16 tokens)",
+                "config": {"workload": f"c1 MoE layer x {LAYERS_PER_GPU} per GPU, pipeline over {world} GPU(s) "
+                                       f"({LAYERS_PER_GPU * world} layers; N=8 is c2's 48), M={HEADLINE_M} chunks",
+                           "m": HEADLINE_M, "layers_per_gpu": LAYERS_PER_GPU, "chunks_per_step": C,
+                           "hidden": cfg.hidden, "experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
+                           "routed_fmt": "nvfp4", "shared_fmt": "fp8-128x128",
+                           "l2": "no flush: each step streams >1 GB of distinct expert weights per layer (L2 126 MB)",
+                           "parallelism": f"pp{world}"},
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": bytes_io,
+                        "d2h_bytes_per_step": bytes_io},
+                "gpu_launches": args.steps * C * LAYERS_PER_GPU * 6 * world,
+                "roofline": roof, "cpu_baseline": cpu, "clocks": clocks, "sweep": sweep}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def m_sweep(layers, cfg):
+    """c1 at M in {1, 8, 32, 64}: tokens/s per layer and the grouped kernel's HBM fraction."""
+    peak, _ = hbm_peak()
+    out = {}
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in evs:
+        e.record()
+    from shard_b200 import synth as S
+    for m in (1, 8, 32, 64):
+        xs = [S.make_inputs(cfg, m, step=500 + j)[0].to(layers[0].device) for j in range(len(layers))]
+        for lay in layers:
+            lay.reserve(m)
+        for lay, x in zip(layers, xs):
+            lay.forward(x)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            for lay, x in zip(layers, xs):
+                lay.forward(x)
+        e1.record()
+        torch.cuda.synchronize()
+        t_fwd = e0.elapsed_time(e1) / 1000.0 / (reps * len(layers))
+        rows = []
+        for lay, x in zip(layers, xs):
+            y, idx, t = lay.forward_profiled(x, evs)
+            torch.cuda.synchronize()
+            rows.append((idx.cpu().numpy(), t))
+        nb = algorithmic_bytes(cfg, [r[0] for r in rows], m)
+        g = sum(b[0] for b in nb) / sum(r[1]["grouped"] for r in rows) / 1e9
+        f = sum(b[1] for b in nb) / len(nb) / t_fwd / 1e9
+        out[f"c1_m{m}"] = {"tokens_per_s": m / t_fwd, "forward_us": t_fwd * 1e6, "grouped_gbs": g,
+                           "grouped_frac": g / peak, "forward_gbs": f, "forward_frac": f / peak}
+    return out
+
+
+def main():
+    global LAYERS_PER_GPU
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS_PER_GPU,
+                    help="layers per GPU (a smaller stack is the small case for ncu captures)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    LAYERS_PER_GPU = args.layers
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    import datetime
+    import torch.distributed as dist
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

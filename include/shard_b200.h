@@ -56,7 +56,7 @@ enum sb_matrix_kind { SB_MAT_PLAIN = 0, SB_MAT_W13 = 1 };
  * Mirrors the state MoE.forward reads, model.py:614-649: self.gate.{weight,bias,tid2eid,
  * score_func,route_scale,topk}, the expert bank, self.shared_experts, Expert.swiglu_limit. */
 typedef struct sb_moe_layer {
-  int32_t hidden;        /* H (dim): multiple of 128 */
+  int32_t hidden;        /* H (dim): multiple of 256 */
   int32_t inter;         /* I (moe_inter_dim): multiple of 128 */
   int32_t n_experts;     /* E routed experts: 1..1024 */
   int32_t topk;          /* k: 1..16 */
@@ -118,6 +118,13 @@ size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m);
 int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,
                    void* y, float* out_weights, int64_t* out_indices, void* workspace,
                    size_t workspace_bytes, void* stream);
+
+/* sb_moe_forward that also records up to six CUDA events (cudaEvent_t, NULL entries skipped) on
+ * the stream: before routing, after routing, after the permutation, after the grouped w13 pass,
+ * after the grouped w2 pass, after the combine. For per-phase timing; same results. */
+int sb_moe_forward_profiled(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,
+                            void* y, float* out_weights, int64_t* out_indices, void* workspace,
+                            size_t workspace_bytes, void* stream, void* const* events);
 
 /* Routing alone (Gate.forward, model.py:569-589): weights fp32 [M, k], indices int64 [M, k]. */
 int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,

@@ -50,6 +50,8 @@ SIGNATURES = {
     "sb_qgemm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "sb_moe_workspace_bytes": (_sz, [ctypes.POINTER(SbMoeLayer), _i64]),
     "sb_moe_forward": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "sb_moe_forward_profiled": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp,
+                                        ctypes.POINTER(_vp)]),
     "sb_moe_route": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sb_selftest_formats": (_int, [_vp, _vp]),
 }

@@ -63,7 +63,8 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
     off += align256(bytes);
     return p;
   };
-  w.logits = (float*)take(sizeof(float) * m * E);
+  // partial gate logits, one [M, E] slab per 512- (or 256-) wide K split
+  w.logits = (float*)take(sizeof(float) * m * E * (H / (H % 512 == 0 ? 512 : 256)));
   w.topk_idx = (int32_t*)take(sizeof(int32_t) * P);
   w.topk_w = (float*)take(sizeof(float) * P);
   w.xq = take((size_t)m * H);
@@ -83,7 +84,7 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
 
 int check_layer(const sb_moe_layer* L) {
   if (!L) return fail(SB_ERR_ARG, "layer is NULL");
-  if (L->hidden <= 0 || L->hidden % 128) return fail(SB_ERR_SHAPE, "hidden=%d must be a positive multiple of 128", L->hidden);
+  if (L->hidden <= 0 || L->hidden % 256) return fail(SB_ERR_SHAPE, "hidden=%d must be a positive multiple of 256", L->hidden);
   if (L->inter <= 0 || L->inter % 128) return fail(SB_ERR_SHAPE, "inter=%d must be a positive multiple of 128", L->inter);
   if (L->n_experts < 1 || L->n_experts > 1024) return fail(SB_ERR_SHAPE, "n_experts=%d outside 1..1024", L->n_experts);
   if (L->topk < 1 || L->topk > 16 || L->topk > L->n_experts)
@@ -256,8 +257,13 @@ int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int6
   return route_impl(layer, x, m, input_ids, out_weights, out_indices, w, false, (cudaStream_t)stream);
 }
 
-int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
-                   float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes, void* stream) {
+static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
+                        float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes,
+                        void* stream, void* const* events) {
+  cudaStream_t st = (cudaStream_t)stream;
+  auto mark = [&](int i) {
+    if (events && events[i]) cudaEventRecord((cudaEvent_t)events[i], st);
+  };
   int rc = check_layer(layer);
   if (rc) return rc;
   const sb_moe_layer* L = layer;
@@ -270,9 +276,10 @@ int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const in
   Workspace w = carve(L, m, (uint8_t*)workspace);
   if (!workspace || workspace_bytes < w.bytes)
     return fail(SB_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, w.bytes);
-  cudaStream_t st = (cudaStream_t)stream;
+  mark(0);
   rc = route_impl(L, x, m, input_ids, out_weights, out_indices, w, true, st);
   if (rc) return rc;
+  mark(1);
   sb::PermuteArgs p;
   p.topk_idx = w.topk_idx;
   p.m = (int)m;
@@ -286,6 +293,7 @@ int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const in
   p.pair_slot = w.pair_slot;
   rc = cuda_check(sb::launch_permute(p, st), "permute");
   if (rc) return rc;
+  mark(2);
 
   const int64_t H = L->hidden, I = L->inter, P = m * L->topk;
   const int64_t max_active = P < L->n_experts ? P : L->n_experts;
@@ -317,6 +325,7 @@ int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const in
   rc = cuda_check(sb::launch_grouped(g, (int)((max_active + (L->has_shared ? 1 : 0)) * g.items_per_expert), 0, st),
                   "grouped w13");
   if (rc) return rc;
+  mark(3);
   // w2
   g.mode = sb::MODE_W2;
   g.n_rows = (int)H;
@@ -330,9 +339,26 @@ int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const in
   rc = cuda_check(sb::launch_grouped(g, (int)((max_active + (L->has_shared ? 1 : 0)) * g.items_per_expert), 0, st),
                   "grouped w2");
   if (rc) return rc;
-  return cuda_check(sb::launch_combine(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
-                                       (__nv_bfloat16*)y, st),
-                    "combine");
+  mark(4);
+  rc = cuda_check(sb::launch_combine(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
+                                     (__nv_bfloat16*)y, st),
+                  "combine");
+  if (rc) return rc;
+  mark(5);
+  return SB_OK;
+}
+
+int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
+                   float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(layer, x, m, input_ids, y, out_weights, out_indices, workspace, workspace_bytes, stream,
+                      nullptr);
+}
+
+int sb_moe_forward_profiled(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
+                            float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes,
+                            void* stream, void* const* events) {
+  return forward_impl(layer, x, m, input_ids, y, out_weights, out_indices, workspace, workspace_bytes, stream,
+                      events);
 }
 
 int sb_selftest_formats(float* out, void* stream) {

@@ -37,6 +37,24 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
   return (uint32_t)r.x | ((uint32_t)r.y << 16);
 }
 
+// four bytes of e2m1 pairs -> four f16x2 (byte i -> r_i), one cvt per byte, no repacking
+__device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(w));
+}
+
+// four e4m3 bytes -> two f16x2 (bytes 0,1 -> d0; bytes 2,3 -> d1)
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& d0, uint32_t& d1) {
+  asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %2;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n"
+      " cvt.rn.f16x2.e4m3x2 %1, hi;\n}"
+      : "=r"(d0), "=r"(d1)
+      : "r"(w));
+}
+
 __device__ __forceinline__ float e4m3_to_f32(uint32_t byte) {
   __half_raw r = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)(byte & 0xFFu), __NV_E4M3);
   return __half2float(__half(r));
@@ -57,8 +75,9 @@ __device__ __forceinline__ float bf16_round(float v) {
 }
 
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
 // f16x2 with both halves = the low (or high) half of s
@@ -95,7 +114,7 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 // C rows g / g+8, cols {2t, 2t+1}   (g = lane/4, t = lane%4)
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -105,7 +124,7 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
 // m16n8k32 e4m3: A rows g / g+8, k 4t..4t+3 and 16+4t..; B k 4t.. / 16+4t.., n = g
 __device__ __forceinline__ void mma_e4m3(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -115,7 +134,7 @@ __device__ __forceinline__ void mma_e4m3(float (&c)[4], uint32_t a0, uint32_t a1
 // streaming 16-byte weight load: read once, keep it out of L1
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
@@ -123,13 +142,13 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
 
 __device__ __forceinline__ uint2 ld_stream8(const void* p) {
   uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
 }
 
 __device__ __forceinline__ uint32_t ld_stream4(const void* p) {
   uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
   return v;
 }
 

@@ -168,40 +168,42 @@ __device__ __forceinline__ void mainloop(const uint8_t* __restrict__ wt, const u
       acc[1][c][3] *= sw[1].y * sa[c][1];
     }
   } else {
-    // fp4: one 16-byte load per lane per tile per 64 K (two 32-chunks); 2 steps per 128-block
+    // fp4: one 16-byte load per lane per tile per 64 K (two 32-chunks); 2 steps per 128-block.
+    // Weights and scales are prefetched two steps ahead in registers.
     constexpr int SB = (FMT == FMT_NVFP4) ? 8 : 4;  // scale bytes per lane per 64 K
     const uint8_t* s0 = st + g * SB;
     const uint8_t* s1 = s0 + stile;
     const int nsteps = K / 64;
-    uint4 nx0 = ld_stream16(w0), nx1 = ld_stream16(w1);
-    uint2 ns0, ns1;
-    if constexpr (FMT == FMT_NVFP4) {
-      ns0 = ld_stream8(s0);
-      ns1 = ld_stream8(s1);
-    } else {
-      ns0 = make_uint2(ld_stream4(s0), 0u);
-      ns1 = make_uint2(ld_stream4(s1), 0u);
-    }
-    for (int step = 0; step < nsteps; ++step) {
-      const uint4 cw[2] = {nx0, nx1};
-      const uint2 cs[2] = {ns0, ns1};
-      if (step + 1 < nsteps) {
-        nx0 = ld_stream16(w0 + (step + 1) * 512);
-        nx1 = ld_stream16(w1 + (step + 1) * 512);
-        if constexpr (FMT == FMT_NVFP4) {
-          ns0 = ld_stream8(s0 + (step + 1) * 64);
-          ns1 = ld_stream8(s1 + (step + 1) * 64);
-        } else {
-          ns0 = make_uint2(ld_stream4(s0 + (step + 1) * 32), 0u);
-          ns1 = make_uint2(ld_stream4(s1 + (step + 1) * 32), 0u);
-        }
+    const uint8_t* bp[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) bp[c] = brow[c] >= 0 ? bq + (size_t)brow[c] * K + 4 * t : nullptr;
+    uint4 wq[2][2];   // [slot][tile]
+    uint2 sq[2][2];
+    auto fetch = [&](int step, int slot) {
+      wq[slot][0] = ld_stream16(w0 + step * 512);
+      wq[slot][1] = ld_stream16(w1 + step * 512);
+      if constexpr (FMT == FMT_NVFP4) {
+        sq[slot][0] = ld_stream8(s0 + step * 64);
+        sq[slot][1] = ld_stream8(s1 + step * 64);
+      } else {
+        sq[slot][0] = make_uint2(ld_stream4(s0 + step * 32), 0u);
+        sq[slot][1] = make_uint2(ld_stream4(s1 + step * 32), 0u);
       }
+    };
+    fetch(0, 0);
+    if (nsteps > 1) fetch(1, 1);
+#pragma unroll 2
+    for (int step = 0; step < nsteps; ++step) {
+      const int slot = step & 1;
+      const uint4 cw[2] = {wq[slot][0], wq[slot][1]};
+      const uint2 cs[2] = {sq[slot][0], sq[slot][1]};
+      if (step + 2 < nsteps) fetch(step + 2, slot);
       if (step > 0 && (step & 1) == 0) {
         float nsa[NCH][2];
         load_sa<NCH>(bs, srow, nkb, step >> 1, nsa);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
-          const float q0 = sa[c][0] / nsa[c][0], q1 = sa[c][1] / nsa[c][1];
+          const float q0 = sa[c][0] * __frcp_rn(nsa[c][0]), q1 = sa[c][1] * __frcp_rn(nsa[c][1]);
 #pragma unroll
           for (int a = 0; a < 2; ++a) {
             acc[a][c][0] *= q0;
@@ -216,29 +218,28 @@ __device__ __forceinline__ void mainloop(const uint8_t* __restrict__ wt, const u
 #pragma unroll
       for (int sub = 0; sub < 2; ++sub) {
         const int ch = step * 2 + sub;
-        uint32_t lo[NCH], hi[NCH];
-        load_b<NCH>(bq, brow, K, ch, t, lo, hi);
         uint32_t bA0[NCH], bA1[NCH], bB0[NCH], bB1[NCH];
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
-          bA0[c] = e4m3x2_to_f16x2(lo[c]);
-          bA1[c] = e4m3x2_to_f16x2(lo[c] >> 16);
-          bB0[c] = e4m3x2_to_f16x2(hi[c]);
-          bB1[c] = e4m3x2_to_f16x2(hi[c] >> 16);
+          uint32_t lo = 0u, hi = 0u;
+          if (bp[c] != nullptr) {
+            lo = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32);
+            hi = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32 + 16);
+          }
+          e4m3x4_to_f16x2x2(lo, bA0[c], bA1[c]);
+          e4m3x4_to_f16x2x2(hi, bB0[c], bB1[c]);
         }
 #pragma unroll
         for (int a = 0; a < 2; ++a) {
-          const uint32_t wlo = sub ? cw[a].z : cw[a].x;
-          const uint32_t whi = sub ? cw[a].w : cw[a].y;
-          uint32_t A0 = e2m1x2_to_f16x2(wlo), A1 = e2m1x2_to_f16x2(wlo >> 8);
-          uint32_t A2 = e2m1x2_to_f16x2(wlo >> 16), A3 = e2m1x2_to_f16x2(wlo >> 24);
-          uint32_t B0 = e2m1x2_to_f16x2(whi), B1 = e2m1x2_to_f16x2(whi >> 8);
-          uint32_t B2 = e2m1x2_to_f16x2(whi >> 16), B3 = e2m1x2_to_f16x2(whi >> 24);
+          uint32_t A0, A1, A2, A3, B0, B1, B2, B3;
+          e2m1x8_to_f16x2x4(sub ? cw[a].z : cw[a].x, A0, A1, A2, A3);
+          e2m1x8_to_f16x2x4(sub ? cw[a].w : cw[a].y, B0, B1, B2, B3);
           if constexpr (FMT == FMT_NVFP4) {
+            // scale bytes of this chunk: [s(g,grp0), s(g+8,grp0), s(g,grp1), s(g+8,grp1)]
             const uint32_t sc = sub ? cs[a].y : cs[a].x;
-            const uint32_t sA = e4m3x2_to_f16x2(sc), sB = e4m3x2_to_f16x2(sc >> 16);
-            const uint32_t sAl = splat_lo(sA), sAh = splat_hi(sA);
-            const uint32_t sBl = splat_lo(sB), sBh = splat_hi(sB);
+            uint32_t sAl, sAh, sBl, sBh;
+            e4m3x4_to_f16x2x2(__byte_perm(sc, 0u, 0x1100), sAl, sAh);
+            e4m3x4_to_f16x2x2(__byte_perm(sc, 0u, 0x3322), sBl, sBh);
             A0 = hmul2_u32(A0, sAl);
             A2 = hmul2_u32(A2, sAl);
             A1 = hmul2_u32(A1, sAh);
@@ -516,18 +517,21 @@ cudaError_t launch_grouped(const GroupedArgs& a, int max_items, int grid_cap, cu
 // y[t] = bf16( sum over t's slots in ascending expert id of o[t*K + slot] (fp32), + shared o[P + t] )
 // A slot whose expert a later slot of the same token names again is dropped (the reference's
 // `y[idx] +=` with repeated indices keeps only the last write; v4_moe_grouped.py:98-118).
-__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ o,
+__global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16* __restrict__ o,
                                                       const int32_t* __restrict__ topk_idx, int m, int K, int h,
                                                       int has_shared, __nv_bfloat16* __restrict__ y) {
   const int t = blockIdx.x;
   __shared__ int order[16];
   __shared__ int n_keep;
   if (threadIdx.x == 0) {
-    int ids[16], slots[16], n = 0;
+    int all[16], ids[16], slots[16], n = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) all[j] = j < K ? topk_idx[(size_t)t * K + j] : -1;
     for (int j = 0; j < K; ++j) {
-      const int e = topk_idx[(size_t)t * K + j];
+      const int e = all[j];
       bool later = false;
-      for (int j2 = j + 1; j2 < K; ++j2) later |= topk_idx[(size_t)t * K + j2] == e;
+#pragma unroll
+      for (int j2 = 0; j2 < 16; ++j2) later |= (j2 > j && j2 < K && all[j2] == e);
       if (later) continue;
       int p = n++;
       while (p > 0 && ids[p - 1] > e) {
@@ -544,23 +548,20 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
   __syncthreads();
   const int P = m * K;
   const int nk = n_keep;
-  for (int v = threadIdx.x; v < h / 8; v += blockDim.x) {
-    float acc[8];
+  const int v = blockIdx.y * blockDim.x + threadIdx.x;  // one 8-element vector per thread
+  if (v >= h / 8) return;
+  uint4 r[17];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-    for (int j = 0; j < nk; ++j) {
-      const uint4 r = *reinterpret_cast<const uint4*>(o + ((size_t)t * K + order[j]) * h + v * 8);
-      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&r);
+  for (int j = 0; j < 16; ++j)
+    if (j < nk) r[j] = *reinterpret_cast<const uint4*>(o + ((size_t)t * K + order[j]) * h + v * 8);
+  if (has_shared) r[16] = *reinterpret_cast<const uint4*>(o + ((size_t)P + t) * h + v * 8);
+  float acc[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __bfloat1622float2(p[q]);
-        acc[2 * q] += f.x;
-        acc[2 * q + 1] += f.y;
-      }
-    }
-    if (has_shared) {
-      const uint4 r = *reinterpret_cast<const uint4*>(o + ((size_t)P + t) * h + v * 8);
-      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&r);
+  for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 17; ++j) {
+    if ((j < 16 && j < nk) || (j == 16 && has_shared)) {
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&r[j]);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float2 f = __bfloat1622float2(p[q]);
@@ -568,17 +569,18 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
         acc[2 * q + 1] += f.y;
       }
     }
-    uint4 out;
-    __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&out);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) op[q] = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
-    *reinterpret_cast<uint4*>(y + (size_t)t * h + v * 8) = out;
   }
+  uint4 out;
+  __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) op[q] = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+  *reinterpret_cast<uint4*>(y + (size_t)t * h + v * 8) = out;
 }
 
 cudaError_t launch_combine(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h, int has_shared,
                            __nv_bfloat16* y, cudaStream_t st) {
-  combine_kernel<<<m, 256, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
+  dim3 grid(m, (h / 8 + 127) / 128);
+  combine_kernel<<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
   return cudaGetLastError();
 }
 

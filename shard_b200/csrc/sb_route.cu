@@ -14,72 +14,136 @@
 
 namespace sb {
 
-// One warp per expert row, 8 tokens per CTA column: each warp streams its W row once (16-byte
-// loads) and multiplies it against 8 token rows (L1/L2 resident). bf16 x bf16 products are exact
-// in fp32, so only the summation order differs from the reference's fp32 F.linear.
+// Split-K gate GEMV. CTA (e-group of 8 experts, K-split s of 512, token group of 32): each warp takes
+// one expert row's 512-wide K slice (1 KB, two 16-byte loads per lane, issued before any math) and
+// dots it with the slice of every token of the group (L1/L2 resident). Partial logits go to
+// part[s][t][e]; route_kernel adds the splits in ascending s, so the sum order is fixed. bf16 x bf16
+// products are exact in fp32; only the summation order differs from the reference's fp32 F.linear.
+constexpr int GATE_TOKENS = 32;
+
+// K-split width of the gate GEMV: 512 when H allows it, else 256 (H % 256 == 0 is required).
+__host__ __device__ inline int gate_ksplit(int h) { return h % 512 == 0 ? 512 : 256; }
+
 __global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ w,
-                                                          float* __restrict__ logits, int m, int e_total,
+                                                          float* __restrict__ part, int m, int e_total,
                                                           int h) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * 8 + warp;
-  const int t0 = blockIdx.y * 8;
+  const int ks = blockIdx.y;
+  const int t0 = blockIdx.z * GATE_TOKENS;
   if (e >= e_total) return;
-  const int nt = min(8, m - t0);
-  float acc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-  const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)e * h);
-  const int nv = h / 8;
-  for (int v = lane; v < nv; v += 32) {
-    const uint4 wv = __ldg(wr + v);
-    const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wv);
-    float wf[8];
+  const int nt = min(GATE_TOKENS, m - t0);
+  const int kspl = gate_ksplit(h);
+  const bool two = kspl == 512;
+  const int k0 = ks * kspl;
+  const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)e * h + k0);
+  const uint4 wv0 = __ldg(wr + lane);
+  const uint4 wv1 = two ? __ldg(wr + 32 + lane) : make_uint4(0u, 0u, 0u, 0u);
+  float wf[16];
+  {
+    const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&wv0);
+    const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&wv1);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const float2 f = __bfloat1622float2(wp[q]);
-      wf[2 * q] = f.x;
-      wf[2 * q + 1] = f.y;
+      const float2 a = __bfloat1622float2(p0[q]), b = __bfloat1622float2(p1[q]);
+      wf[2 * q] = a.x;
+      wf[2 * q + 1] = a.y;
+      wf[8 + 2 * q] = b.x;
+      wf[8 + 2 * q + 1] = b.y;
+    }
+  }
+  float* out = part + ((size_t)ks * m + t0) * e_total + e;
+  for (int j0 = 0; j0 < nt; j0 += 8) {
+    uint4 xv0[8], xv1[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j0 + j < nt) {
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)(t0 + j0 + j) * h + k0);
+        xv0[j] = __ldg(xr + lane);
+        xv1[j] = two ? __ldg(xr + 32 + lane) : make_uint4(0u, 0u, 0u, 0u);
+      }
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      if (j < nt) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + j) * h) + v);
-        const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
+      float acc = 0.f;
+      if (j0 + j < nt) {
+        const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&xv0[j]);
+        const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&xv1[j]);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float2 f = __bfloat1622float2(xp[q]);
-          acc[j] = fmaf(f.x, wf[2 * q], acc[j]);
-          acc[j] = fmaf(f.y, wf[2 * q + 1], acc[j]);
+          const float2 a = __bfloat1622float2(p0[q]), b = __bfloat1622float2(p1[q]);
+          acc = fmaf(a.x, wf[2 * q], acc);
+          acc = fmaf(a.y, wf[2 * q + 1], acc);
+          acc = fmaf(b.x, wf[8 + 2 * q], acc);
+          acc = fmaf(b.y, wf[8 + 2 * q + 1], acc);
         }
       }
+      acc = warp_sum(acc);
+      if (lane == 0 && j0 + j < nt) out[(size_t)(j0 + j) * e_total] = acc;
     }
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float s = warp_sum(acc[j]);
-    if (lane == 0 && j < nt) logits[(size_t)(t0 + j) * e_total + e] = s;
   }
 }
 
 constexpr int MAX_E_PER_LANE = 32;  // E <= 1024
 
-// One warp per token. Warp w of the CTA handles token blockIdx.x * 4 + w: top-k on lane-strided
-// scores, then the token's act_quant (all 128-blocks of x[t]).
+// One CTA per token: the 4 warps quantise x[t] (act_quant, one 128-block per warp-iteration, loads
+// issued up front), then warp 0 does the top-k on lane-strided scores.
+__device__ __forceinline__ void quant_row(const RouteArgs& a, int t, int warp, int lane) {
+  const __nv_bfloat16* xr = a.x + (size_t)t * a.hidden;
+  const int nb = a.hidden / 128;
+  for (int b0 = warp; b0 < nb; b0 += 16) {
+    uint2 raw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int b = b0 + 4 * u;
+      if (b < nb) raw[u] = *reinterpret_cast<const uint2*>(xr + b * 128 + lane * 4);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int b = b0 + 4 * u;
+      if (b < nb) {
+        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
+        const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
+        float am = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
+        am = warp_max(am);
+        const float s = act_scale(am, a.act_pow2);
+        const uint32_t q = (uint32_t)act_q(f0.x, s) | ((uint32_t)act_q(f0.y, s) << 8) |
+                           ((uint32_t)act_q(f1.x, s) << 16) | ((uint32_t)act_q(f1.y, s) << 24);
+        *reinterpret_cast<uint32_t*>(a.xq + (size_t)t * a.hidden + b * 128 + lane * 4) = q;
+        if (lane == 0) a.xs[(size_t)t * nb + b] = s;
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + warp;
+  const int t = blockIdx.x;
   if (t >= a.m) return;
+  if (a.xq != nullptr) quant_row(a, t, warp, lane);
+  if (warp != 0) return;
   const int E = a.n_experts;
-  const float* lg = a.logits + (size_t)t * E;
+  const int nsplit = a.hidden / gate_ksplit(a.hidden);
   float sc[MAX_E_PER_LANE];
   float mx = -INFINITY;
+  // logit = split 0 + split 1 + ... in ascending split order; the loads of one split are
+  // independent of each other, so each split costs one memory latency, not one per expert
 #pragma unroll
   for (int i = 0; i < MAX_E_PER_LANE; ++i) {
     const int e = lane + 32 * i;
-    sc[i] = e < E ? lg[e] : -INFINITY;
-    mx = fmaxf(mx, sc[i]);
+    sc[i] = e < E ? a.logits[(size_t)t * E + e] : -INFINITY;
   }
+  for (int ks = 1; ks < nsplit; ++ks) {
+    const float* pk = a.logits + ((size_t)ks * a.m + t) * E;
+#pragma unroll
+    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E) sc[i] += pk[e];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MAX_E_PER_LANE; ++i) mx = fmaxf(mx, sc[i]);
   if (a.score_func == SCORE_SOFTMAX) {
     mx = warp_max(mx);
     float s = 0.f;
@@ -173,22 +237,6 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
       if (a.out_w) a.out_w[(size_t)t * K + j] = wsel[j];
     }
   }
-  // act_quant of x[t]: one 128-block per warp iteration, 4 values per lane
-  if (a.xq != nullptr) {
-    const __nv_bfloat16* xr = a.x + (size_t)t * a.hidden;
-    for (int b = 0; b < a.hidden / 128; ++b) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(xr + b * 128 + lane * 4);
-      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
-      float am = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
-      am = warp_max(am);
-      const float s = act_scale(am, a.act_pow2);
-      const uint32_t q = (uint32_t)act_q(f0.x, s) | ((uint32_t)act_q(f0.y, s) << 8) |
-                         ((uint32_t)act_q(f1.x, s) << 16) | ((uint32_t)act_q(f1.y, s) << 24);
-      *reinterpret_cast<uint32_t*>(a.xq + (size_t)t * a.hidden + b * 128 + lane * 4) = q;
-      if (lane == 0) a.xs[(size_t)t * (a.hidden / 128) + b] = s;
-    }
-  }
 }
 
 // Single CTA. counts -> exclusive offsets -> stable placement (pair p = t*K + j, ascending p
@@ -276,13 +324,13 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
 
 cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int m, int e, int h,
                                cudaStream_t st) {
-  dim3 grid((e + 7) / 8, (m + 7) / 8);
+  dim3 grid((e + 7) / 8, h / gate_ksplit(h), (m + GATE_TOKENS - 1) / GATE_TOKENS);
   gate_logits_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w, logits, m, e, h);
   return cudaGetLastError();
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
-  route_kernel<<<(a.m + 3) / 4, 128, 0, st>>>(a);
+  route_kernel<<<a.m, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
 

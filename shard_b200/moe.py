@@ -145,6 +145,29 @@ class MoELayer:
 
     __call__ = forward
 
+    def forward_profiled(self, x: torch.Tensor, events, input_ids: Optional[torch.Tensor] = None):
+        """forward() with CUDA events between its launches (six torch.cuda.Event(enable_timing=True),
+        each already recorded once so it exists). Synchronises; returns (y, top-k indices,
+        {phase: seconds}) with phases route, permute, w13, w2, combine, grouped (= w13 + w2), total."""
+        x = x.contiguous()
+        m = x.shape[0]
+        y = torch.empty_like(x)
+        ws = self.reserve(m)
+        idx = torch.empty(m, self.topk, dtype=torch.int64, device=x.device)
+        ids = None
+        if self.tid2eid is not None:
+            ids = input_ids.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
+        handles = (ctypes.c_void_p * 6)(*[ctypes.c_void_p(e.cuda_event) for e in events])
+        check(lib().sb_moe_forward_profiled(ctypes.byref(self.desc), ptr(x), m, ptr(ids), ptr(y), None, ptr(idx),
+                                            ptr(ws), ws.numel(), stream_ptr(), handles),
+              "sb_moe_forward_profiled")
+        events[5].synchronize()
+        ms = [events[i].elapsed_time(events[i + 1]) / 1000.0 for i in range(5)]
+        t = {"route": ms[0], "permute": ms[1], "w13": ms[2], "w2": ms[3], "combine": ms[4]}
+        t["grouped"] = ms[2] + ms[3]
+        t["total"] = sum(ms)
+        return y, idx, t
+
     def route(self, x: torch.Tensor, input_ids: Optional[torch.Tensor] = None):
         """Gate.forward alone: (weights fp32 [M, k], indices int64 [M, k])."""
         x = x.contiguous()
