@@ -36,6 +36,7 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 // The forward's scratch regions, carved from one caller-provided workspace.
 struct Workspace {
+  int32_t* err;      // offset 0: device error flag (cleared by every forward; 1 = a bounded wait gave up)
   float* logits;
   int32_t* topk_idx;
   float* topk_w;
@@ -63,6 +64,7 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
     off += align256(bytes);
     return p;
   };
+  w.err = (int32_t*)take(sizeof(int32_t));
   // partial gate logits, one [M, E] slab per 512- (or 256-) wide K split
   w.logits = (float*)take(sizeof(float) * m * E * (H / (H % 512 == 0 ? 512 : 256)));
   w.topk_idx = (int32_t*)take(sizeof(int32_t) * P);
@@ -291,6 +293,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.n_active = w.n_active;
   p.pair_tok = w.pair_tok;
   p.pair_slot = w.pair_slot;
+  p.err = w.err;
   rc = cuda_check(sb::launch_permute(p, st), "permute");
   if (rc) return rc;
   mark(2);
@@ -311,6 +314,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   g.pair_tok = w.pair_tok;
   g.pair_slot = w.pair_slot;
   g.topk_w = w.topk_w;
+  g.err = w.err;
   // w13 (+ SwiGLU, + act_quant of h)
   g.mode = sb::MODE_W13;
   g.n_rows = (int)(2 * I);

@@ -30,6 +30,22 @@ constexpr int WARPS = 8;
 constexpr int TILES_PER_ITEM = 16;
 constexpr int MAX_PASS = 32;  // tokens per pass (4 fragments of 8)
 
+// Per-warp weight ring in shared memory, filled by bulk async copies (cp.async.bulk, the TMA
+// engine's non-tensor form) that complete on one mbarrier per stage. A stage is 1 KB of each of
+// the warp's two tiles (128 K of fp4, 64 K of fp8) plus, for fp4, the matching scale bytes.
+constexpr int STAGES = 4;
+constexpr int STAGE_W = 2048;
+constexpr int STAGE_BYTES = STAGE_W + 256;
+constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+constexpr int DYN_SMEM = WARPS * RING_BYTES + WARPS * STAGES * 8;
+
+struct WarpRing {
+  uint8_t* buf;     // STAGES * STAGE_BYTES
+  uint32_t bar0;    // shared address of the first of STAGES mbarriers (8 bytes apart)
+  uint32_t count;   // stages consumed so far by this warp (selects slot and phase)
+  bool bad;         // a wait timed out: stop streaming
+};
+
 struct ItemInfo {
   int shared;   // 1: shared expert / dense
   int expert;
@@ -56,24 +72,6 @@ struct Tiling<FMT_FP8> {
   static __device__ size_t s_tile(int k) { return (size_t)(k / 128) * 8; }
 };
 
-// Per-lane B operand for one 32-wide K chunk: raw e4m3 bytes at K {4t..4t+3} and {16+4t..16+4t+3}
-// of the lane's token (g) in fragment c (brow < 0: no token, zeros).
-template <int NCH>
-__device__ __forceinline__ void load_b(const uint8_t* __restrict__ bq, const int (&brow)[NCH], int K, int ch, int t,
-                                       uint32_t (&lo)[NCH], uint32_t (&hi)[NCH]) {
-#pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    if (brow[c] >= 0) {
-      const uint8_t* p = bq + (size_t)brow[c] * K + ch * 32 + 4 * t;
-      lo[c] = *reinterpret_cast<const uint32_t*>(p);
-      hi[c] = *reinterpret_cast<const uint32_t*>(p + 16);
-    } else {
-      lo[c] = 0u;
-      hi[c] = 0u;
-    }
-  }
-}
-
 // Activation scales of the lane's C columns (tokens 2t, 2t+1 of each fragment) for 128-block kb.
 // A missing token gets 1.0 so the running rescale below stays finite (its column is all zero).
 template <int NCH>
@@ -85,8 +83,15 @@ __device__ __forceinline__ void load_sa(const float* __restrict__ bs, const int 
     for (int u = 0; u < 2; ++u) sa[c][u] = srow[c][u] >= 0 ? bs[(size_t)srow[c][u] * nkb + kb] : 1.f;
 }
 
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
 // The two-tile mainloop of one warp over the whole K. On return acc[tile][frag][4] holds
 // sum_k dequant(W) * dequant(B) for rows (g, g+8) x tokens (2t, 2t+1) of each fragment.
+//
+// Weights stream through the warp's shared-memory ring: lane 0 keeps STAGES stages of bulk copies in
+// flight, every lane reads its fragment bytes from shared memory.
 //
 // Per-128-block scales (the activation's, and for FP8 the weight block's) are applied by keeping
 // the running fp32 accumulator in units of the current block's scale: at a block boundary it is
@@ -97,43 +102,69 @@ template <int FMT, int NCH>
 __device__ __forceinline__ void mainloop(const uint8_t* __restrict__ wt, const uint8_t* __restrict__ st, int K,
                                          const uint8_t* __restrict__ bq, const float* __restrict__ bs,
                                          const int (&brow)[NCH], const int (&srow)[NCH][2],
-                                         float (&acc)[2][NCH][4]) {
+                                         float (&acc)[2][NCH][4], WarpRing& ring, int* err) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const size_t wtile = Tiling<FMT>::w_tile(K), stile = Tiling<FMT>::s_tile(K);
   const int nkb = K / 128;
+  constexpr int SBS = FMT == FMT_NVFP4 ? 128 : (FMT == FMT_MXFP4 ? 64 : 0);  // scale bytes per tile per stage
+  const int nst = FMT == FMT_FP8 ? K / 64 : K / 128;
 #pragma unroll
   for (int a = 0; a < 2; ++a)
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
 #pragma unroll
       for (int r = 0; r < 4; ++r) acc[a][c][r] = 0.f;
+  if (ring.bad) return;
   float sa[NCH][2];
   load_sa<NCH>(bs, srow, nkb, 0, sa);
-  const uint8_t* w0 = wt + lane * 16;
-  const uint8_t* w1 = w0 + wtile;
+  const uint8_t* bp[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) bp[c] = brow[c] >= 0 ? bq + (size_t)brow[c] * K + 4 * t : nullptr;
 
+  auto issue = [&](int j) {
+    const uint32_t slot = (ring.count + j) % STAGES;
+    uint8_t* dst = ring.buf + slot * STAGE_BYTES;
+    const uint32_t bar = ring.bar0 + slot * 8;
+    mbar_expect_tx(bar, STAGE_W + 2 * SBS);
+    bulk_g2s(smem_addr(dst), wt + (size_t)j * 1024, 1024, bar);
+    bulk_g2s(smem_addr(dst + 1024), wt + wtile + (size_t)j * 1024, 1024, bar);
+    if constexpr (SBS > 0) {
+      bulk_g2s(smem_addr(dst + STAGE_W), st + (size_t)j * SBS, SBS, bar);
+      bulk_g2s(smem_addr(dst + STAGE_W + SBS), st + stile + (size_t)j * SBS, SBS, bar);
+    }
+  };
+  if (lane == 0)
+    for (int j = 0; j < (nst < STAGES ? nst : STAGES); ++j) issue(j);
+  __syncwarp();
+
+  float2 sw[2] = {make_float2(1.f, 1.f), make_float2(1.f, 1.f)};
   if constexpr (FMT == FMT_FP8) {
-    // one 16-byte load per lane per tile per 32 K; 4 steps per 128-block
-    const float2* s0 = reinterpret_cast<const float2*>(st);
-    const float2* s1 = reinterpret_cast<const float2*>(st + stile);
-    float2 sw[2] = {s0[0], s1[0]};
-    const int nsteps = K / 32;
-    uint4 nx0 = ld_stream16(w0), nx1 = ld_stream16(w1);
-    for (int step = 0; step < nsteps; ++step) {
-      const uint4 c0 = nx0, c1 = nx1;
-      if (step + 1 < nsteps) {
-        nx0 = ld_stream16(w0 + (step + 1) * 512);
-        nx1 = ld_stream16(w1 + (step + 1) * 512);
-      }
-      if (step > 0 && (step & 3) == 0) {
-        const int kb = step >> 2;
+    sw[0] = reinterpret_cast<const float2*>(st)[0];
+    sw[1] = reinterpret_cast<const float2*>(st + stile)[0];
+  }
+  int j = 0;
+  for (; j < nst; ++j) {
+    const uint32_t slot = (ring.count + j) % STAGES, par = ((ring.count + j) / STAGES) & 1u;
+    const bool ok = __any_sync(0xffffffffu, mbar_wait(ring.bar0 + slot * 8, par));
+    if (!ok) {
+      if (lane == 0) atomicExch(err, 1);
+      ring.bad = true;
+      break;
+    }
+    const uint8_t* sbuf = ring.buf + slot * STAGE_BYTES;
+    if constexpr (FMT == FMT_FP8) {
+      // stage j = K [64j, 64j + 64): two m16n8k32 steps; a new 128-block starts at even j
+      if (j > 0 && (j & 1) == 0) {
+        const int kb = j >> 1;
         float nsa[NCH][2];
         load_sa<NCH>(bs, srow, nkb, kb, nsa);
-        const float2 nw0 = s0[kb], nw1 = s1[kb];
-        const float r0x = sw[0].x / nw0.x, r0y = sw[0].y / nw0.y, r1x = sw[1].x / nw1.x, r1y = sw[1].y / nw1.y;
+        const float2 nw0 = reinterpret_cast<const float2*>(st)[kb];
+        const float2 nw1 = reinterpret_cast<const float2*>(st + stile)[kb];
+        const float r0x = sw[0].x * __frcp_rn(nw0.x), r0y = sw[0].y * __frcp_rn(nw0.y);
+        const float r1x = sw[1].x * __frcp_rn(nw1.x), r1y = sw[1].y * __frcp_rn(nw1.y);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
-          const float q0 = sa[c][0] / nsa[c][0], q1 = sa[c][1] / nsa[c][1];
+          const float q0 = sa[c][0] * __frcp_rn(nsa[c][0]), q1 = sa[c][1] * __frcp_rn(nsa[c][1]);
           acc[0][c][0] *= r0x * q0;
           acc[0][c][1] *= r0x * q1;
           acc[0][c][2] *= r0y * q0;
@@ -148,59 +179,27 @@ __device__ __forceinline__ void mainloop(const uint8_t* __restrict__ wt, const u
         sw[0] = nw0;
         sw[1] = nw1;
       }
-      uint32_t lo[NCH], hi[NCH];
-      load_b<NCH>(bq, brow, K, step, t, lo, hi);
 #pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-        mma_e4m3(acc[0][c], c0.x, c0.y, c0.z, c0.w, lo[c], hi[c]);
-        mma_e4m3(acc[1][c], c1.x, c1.y, c1.z, c1.w, lo[c], hi[c]);
+      for (int q = 0; q < 2; ++q) {
+        const int ch = j * 2 + q;
+        const uint4 c0 = lds128(sbuf + q * 512 + lane * 16);
+        const uint4 c1 = lds128(sbuf + 1024 + q * 512 + lane * 16);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t lo = 0u, hi = 0u;
+          if (bp[c] != nullptr) {
+            lo = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32);
+            hi = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32 + 16);
+          }
+          mma_e4m3(acc[0][c], c0.x, c0.y, c0.z, c0.w, lo, hi);
+          mma_e4m3(acc[1][c], c1.x, c1.y, c1.z, c1.w, lo, hi);
+        }
       }
-    }
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      acc[0][c][0] *= sw[0].x * sa[c][0];
-      acc[0][c][1] *= sw[0].x * sa[c][1];
-      acc[0][c][2] *= sw[0].y * sa[c][0];
-      acc[0][c][3] *= sw[0].y * sa[c][1];
-      acc[1][c][0] *= sw[1].x * sa[c][0];
-      acc[1][c][1] *= sw[1].x * sa[c][1];
-      acc[1][c][2] *= sw[1].y * sa[c][0];
-      acc[1][c][3] *= sw[1].y * sa[c][1];
-    }
-  } else {
-    // fp4: one 16-byte load per lane per tile per 64 K (two 32-chunks); 2 steps per 128-block.
-    // Weights and scales are prefetched two steps ahead in registers.
-    constexpr int SB = (FMT == FMT_NVFP4) ? 8 : 4;  // scale bytes per lane per 64 K
-    const uint8_t* s0 = st + g * SB;
-    const uint8_t* s1 = s0 + stile;
-    const int nsteps = K / 64;
-    const uint8_t* bp[NCH];
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) bp[c] = brow[c] >= 0 ? bq + (size_t)brow[c] * K + 4 * t : nullptr;
-    uint4 wq[2][2];   // [slot][tile]
-    uint2 sq[2][2];
-    auto fetch = [&](int step, int slot) {
-      wq[slot][0] = ld_stream16(w0 + step * 512);
-      wq[slot][1] = ld_stream16(w1 + step * 512);
-      if constexpr (FMT == FMT_NVFP4) {
-        sq[slot][0] = ld_stream8(s0 + step * 64);
-        sq[slot][1] = ld_stream8(s1 + step * 64);
-      } else {
-        sq[slot][0] = make_uint2(ld_stream4(s0 + step * 32), 0u);
-        sq[slot][1] = make_uint2(ld_stream4(s1 + step * 32), 0u);
-      }
-    };
-    fetch(0, 0);
-    if (nsteps > 1) fetch(1, 1);
-#pragma unroll 2
-    for (int step = 0; step < nsteps; ++step) {
-      const int slot = step & 1;
-      const uint4 cw[2] = {wq[slot][0], wq[slot][1]};
-      const uint2 cs[2] = {sq[slot][0], sq[slot][1]};
-      if (step + 2 < nsteps) fetch(step + 2, slot);
-      if (step > 0 && (step & 1) == 0) {
+    } else {
+      // stage j = 128-block j: two 64-K steps of two 32-K chunks each
+      if (j > 0) {
         float nsa[NCH][2];
-        load_sa<NCH>(bs, srow, nkb, step >> 1, nsa);
+        load_sa<NCH>(bs, srow, nkb, j, nsa);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           const float q0 = sa[c][0] * __frcp_rn(nsa[c][0]), q1 = sa[c][1] * __frcp_rn(nsa[c][1]);
@@ -216,60 +215,101 @@ __device__ __forceinline__ void mainloop(const uint8_t* __restrict__ wt, const u
         }
       }
 #pragma unroll
-      for (int sub = 0; sub < 2; ++sub) {
-        const int ch = step * 2 + sub;
-        uint32_t bA0[NCH], bA1[NCH], bB0[NCH], bB1[NCH];
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          uint32_t lo = 0u, hi = 0u;
-          if (bp[c] != nullptr) {
-            lo = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32);
-            hi = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32 + 16);
-          }
-          e4m3x4_to_f16x2x2(lo, bA0[c], bA1[c]);
-          e4m3x4_to_f16x2x2(hi, bB0[c], bB1[c]);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const uint4 cw[2] = {lds128(sbuf + h2 * 512 + lane * 16), lds128(sbuf + 1024 + h2 * 512 + lane * 16)};
+        uint2 cs[2];
+        if constexpr (FMT == FMT_NVFP4) {
+          cs[0] = lds64(sbuf + STAGE_W + h2 * 64 + g * 8);
+          cs[1] = lds64(sbuf + STAGE_W + SBS + h2 * 64 + g * 8);
+        } else {
+          cs[0] = make_uint2(lds32(sbuf + STAGE_W + h2 * 32 + g * 4), 0u);
+          cs[1] = make_uint2(lds32(sbuf + STAGE_W + SBS + h2 * 32 + g * 4), 0u);
         }
 #pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          uint32_t A0, A1, A2, A3, B0, B1, B2, B3;
-          e2m1x8_to_f16x2x4(sub ? cw[a].z : cw[a].x, A0, A1, A2, A3);
-          e2m1x8_to_f16x2x4(sub ? cw[a].w : cw[a].y, B0, B1, B2, B3);
-          if constexpr (FMT == FMT_NVFP4) {
-            // scale bytes of this chunk: [s(g,grp0), s(g+8,grp0), s(g,grp1), s(g+8,grp1)]
-            const uint32_t sc = sub ? cs[a].y : cs[a].x;
-            uint32_t sAl, sAh, sBl, sBh;
-            e4m3x4_to_f16x2x2(__byte_perm(sc, 0u, 0x1100), sAl, sAh);
-            e4m3x4_to_f16x2x2(__byte_perm(sc, 0u, 0x3322), sBl, sBh);
-            A0 = hmul2_u32(A0, sAl);
-            A2 = hmul2_u32(A2, sAl);
-            A1 = hmul2_u32(A1, sAh);
-            A3 = hmul2_u32(A3, sAh);
-            B0 = hmul2_u32(B0, sBl);
-            B2 = hmul2_u32(B2, sBl);
-            B1 = hmul2_u32(B1, sBh);
-            B3 = hmul2_u32(B3, sBh);
+        for (int sub = 0; sub < 2; ++sub) {
+          const int ch = (j * 2 + h2) * 2 + sub;
+          uint32_t bA0[NCH], bA1[NCH], bB0[NCH], bB1[NCH];
 #pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-              mma_f16(acc[a][c], A0, A1, A2, A3, bA0[c], bA1[c]);
-              mma_f16(acc[a][c], B0, B1, B2, B3, bB0[c], bB1[c]);
+          for (int c = 0; c < NCH; ++c) {
+            uint32_t lo = 0u, hi = 0u;
+            if (bp[c] != nullptr) {
+              lo = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32);
+              hi = *reinterpret_cast<const uint32_t*>(bp[c] + ch * 32 + 16);
             }
-          } else {
-            const uint32_t sc = (sub ? (cs[a].x >> 16) : cs[a].x) & 0xFFFFu;
-            const float fg = e8m0_to_f32(sc), fg8 = e8m0_to_f32(sc >> 8);
+            e4m3x4_to_f16x2x2(lo, bA0[c], bA1[c]);
+            e4m3x4_to_f16x2x2(hi, bB0[c], bB1[c]);
+          }
 #pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-              float tmp[4] = {0.f, 0.f, 0.f, 0.f};
-              mma_f16(tmp, A0, A1, A2, A3, bA0[c], bA1[c]);
-              mma_f16(tmp, B0, B1, B2, B3, bB0[c], bB1[c]);
-              acc[a][c][0] = fmaf(tmp[0], fg, acc[a][c][0]);
-              acc[a][c][1] = fmaf(tmp[1], fg, acc[a][c][1]);
-              acc[a][c][2] = fmaf(tmp[2], fg8, acc[a][c][2]);
-              acc[a][c][3] = fmaf(tmp[3], fg8, acc[a][c][3]);
+          for (int a = 0; a < 2; ++a) {
+            uint32_t A0, A1, A2, A3, B0, B1, B2, B3;
+            e2m1x8_to_f16x2x4(sub ? cw[a].z : cw[a].x, A0, A1, A2, A3);
+            e2m1x8_to_f16x2x4(sub ? cw[a].w : cw[a].y, B0, B1, B2, B3);
+            if constexpr (FMT == FMT_NVFP4) {
+              // scale bytes of this chunk: [s(g,grp0), s(g+8,grp0), s(g,grp1), s(g+8,grp1)]
+              const uint32_t sc = sub ? cs[a].y : cs[a].x;
+              uint32_t sAl, sAh, sBl, sBh;
+              e4m3x4_to_f16x2x2(__byte_perm(sc, 0u, 0x1100), sAl, sAh);
+              e4m3x4_to_f16x2x2(__byte_perm(sc, 0u, 0x3322), sBl, sBh);
+              A0 = hmul2_u32(A0, sAl);
+              A2 = hmul2_u32(A2, sAl);
+              A1 = hmul2_u32(A1, sAh);
+              A3 = hmul2_u32(A3, sAh);
+              B0 = hmul2_u32(B0, sBl);
+              B2 = hmul2_u32(B2, sBl);
+              B1 = hmul2_u32(B1, sBh);
+              B3 = hmul2_u32(B3, sBh);
+#pragma unroll
+              for (int c = 0; c < NCH; ++c) {
+                mma_f16(acc[a][c], A0, A1, A2, A3, bA0[c], bA1[c]);
+                mma_f16(acc[a][c], B0, B1, B2, B3, bB0[c], bB1[c]);
+              }
+            } else {
+              const uint32_t sc = (sub ? (cs[a].x >> 16) : cs[a].x) & 0xFFFFu;
+              const float fg = e8m0_to_f32(sc), fg8 = e8m0_to_f32(sc >> 8);
+#pragma unroll
+              for (int c = 0; c < NCH; ++c) {
+                float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+                mma_f16(tmp, A0, A1, A2, A3, bA0[c], bA1[c]);
+                mma_f16(tmp, B0, B1, B2, B3, bB0[c], bB1[c]);
+                acc[a][c][0] = fmaf(tmp[0], fg, acc[a][c][0]);
+                acc[a][c][1] = fmaf(tmp[1], fg, acc[a][c][1]);
+                acc[a][c][2] = fmaf(tmp[2], fg8, acc[a][c][2]);
+                acc[a][c][3] = fmaf(tmp[3], fg8, acc[a][c][3]);
+              }
             }
           }
         }
       }
     }
+    __syncwarp();
+    if (lane == 0 && j + STAGES < nst) {
+      fence_proxy_async_smem();  // this warp's reads of the slot are ordered before the refill
+      issue(j + STAGES);
+    }
+  }
+  if (ring.bad) {
+    // drain: wait (bounded) for the copies this warp still has in flight, then stop
+    const int last = (j + STAGES < nst ? j + STAGES : nst);
+    for (int k = j; k < last; ++k) {
+      const uint32_t slot = (ring.count + k) % STAGES, par = ((ring.count + k) / STAGES) & 1u;
+      (void)mbar_wait(ring.bar0 + slot * 8, par);
+    }
+    return;
+  }
+  ring.count += nst;
+  if constexpr (FMT == FMT_FP8) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      acc[0][c][0] *= sw[0].x * sa[c][0];
+      acc[0][c][1] *= sw[0].x * sa[c][1];
+      acc[0][c][2] *= sw[0].y * sa[c][0];
+      acc[0][c][3] *= sw[0].y * sa[c][1];
+      acc[1][c][0] *= sw[1].x * sa[c][0];
+      acc[1][c][1] *= sw[1].x * sa[c][1];
+      acc[1][c][2] *= sw[1].y * sa[c][0];
+      acc[1][c][3] *= sw[1].y * sa[c][1];
+    }
+  } else {
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
 #pragma unroll
@@ -311,7 +351,7 @@ struct PassSmem {
 
 template <int FMT, int NCH>
 __device__ void run_pass(const GroupedArgs& a, const ItemInfo& it, const WeightSet& ws, int pass_cnt,
-                         PassSmem& sm) {
+                         PassSmem& sm, WarpRing& ring) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int K = a.k;
   const int tiles_total = a.n_rows / 16;
@@ -332,7 +372,7 @@ __device__ void run_pass(const GroupedArgs& a, const ItemInfo& it, const WeightS
   if (active_warp) {
     const uint8_t* wt = ws.w + (it.shared ? 0 : (size_t)e * ws.w_stride) + (size_t)tile0 * Tiling<FMT>::w_tile(K);
     const uint8_t* st = ws.s + (it.shared ? 0 : (size_t)e * ws.s_stride) + (size_t)tile0 * Tiling<FMT>::s_tile(K);
-    mainloop<FMT, NCH>(wt, st, K, a.bq, a.bs, brow, srow, acc);
+    mainloop<FMT, NCH>(wt, st, K, a.bq, a.bs, brow, srow, acc, ring, a.err);
   } else {
 #pragma unroll
     for (int x = 0; x < 2; ++x)
@@ -432,17 +472,37 @@ __device__ void run_pass(const GroupedArgs& a, const ItemInfo& it, const WeightS
   }
 }
 
+// error flag of launches that have no workspace (the dense sb_qgemm path)
+__device__ int g_dense_err = 0;
+
 template <int FMT_R>
 __global__ void __launch_bounds__(256, 2) grouped_kernel(GroupedArgs a) {
+  if (a.err == nullptr) a.err = &g_dense_err;
   __shared__ PassSmem sm;
+  extern __shared__ __align__(128) uint8_t dyn[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WarpRing ring;
+  ring.buf = dyn + warp * RING_BYTES;
+  ring.bar0 = smem_addr(dyn + WARPS * RING_BYTES) + warp * STAGES * 8;
+  ring.count = 0;
+  ring.bad = false;
+  if (lane == 0) {
+    for (int s2 = 0; s2 < STAGES; ++s2) mbar_init(ring.bar0 + s2 * 8, 1);
+    mbar_init_fence();
+  }
+  __syncwarp();
   const int n_sh = a.has_shared ? a.items_per_expert : 0;
   const int n_items = n_sh + (a.mode == MODE_DENSE ? 0 : (*a.n_active) * a.items_per_expert);
   const int P = a.m * a.topk;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    __syncthreads();
+    if (*reinterpret_cast<volatile int*>(a.err) != 0) break;  // a warp gave up waiting: stop everywhere
     const ItemInfo it = item_info(a, item, n_sh);
     const WeightSet& ws = it.shared ? a.shared : a.routed;
     const int fmt = it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R;
-    const int pass_max = fmt == FMT_FP8 ? MAX_PASS : 16;
+    // 32 tokens per pass only in the FP8 kernel: inside the fp4 kernels the shared expert's FP8
+    // path keeps to 16 so the kernel stays within 128 registers
+    const int pass_max = (fmt == FMT_FP8 && FMT_R == FMT_FP8) ? MAX_PASS : 16;
     for (int pb = 0; pb < it.cnt; pb += pass_max) {
       const int pass_cnt = min(pass_max, it.cnt - pb);
       __syncthreads();
@@ -479,12 +539,12 @@ __global__ void __launch_bounds__(256, 2) grouped_kernel(GroupedArgs a) {
       }
       __syncthreads();
       if (fmt == FMT_FP8) {
-        if (pass_cnt <= 8) run_pass<FMT_FP8, 1>(a, it, ws, pass_cnt, sm);
-        else if (pass_cnt <= 16) run_pass<FMT_FP8, 2>(a, it, ws, pass_cnt, sm);
-        else run_pass<FMT_FP8, 4>(a, it, ws, pass_cnt, sm);
+        if (pass_cnt <= 8) run_pass<FMT_FP8, 1>(a, it, ws, pass_cnt, sm, ring);
+        else if (FMT_R != FMT_FP8 || pass_cnt <= 16) run_pass<FMT_FP8, 2>(a, it, ws, pass_cnt, sm, ring);
+        else if constexpr (FMT_R == FMT_FP8) run_pass<FMT_FP8, 4>(a, it, ws, pass_cnt, sm, ring);
       } else if constexpr (FMT_R != FMT_FP8) {
-        if (pass_cnt <= 8) run_pass<FMT_R, 1>(a, it, ws, pass_cnt, sm);
-        else run_pass<FMT_R, 2>(a, it, ws, pass_cnt, sm);
+        if (pass_cnt <= 8) run_pass<FMT_R, 1>(a, it, ws, pass_cnt, sm, ring);
+        else run_pass<FMT_R, 2>(a, it, ws, pass_cnt, sm, ring);
       }
     }
   }
@@ -501,17 +561,28 @@ int num_sms() {
   return n;
 }
 
+template <int F>
+static cudaError_t launch_one(const GroupedArgs& a, int grid, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(grouped_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_SMEM);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  grouped_kernel<F><<<grid, 256, DYN_SMEM, st>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_grouped(const GroupedArgs& a, int max_items, int grid_cap, cudaStream_t st) {
   int grid = 2 * num_sms();
   if (grid_cap > 0 && grid > grid_cap) grid = grid_cap;
   if (grid > max_items) grid = max_items;
   if (grid < 1) grid = 1;
   switch (a.routed.fmt) {
-    case FMT_NVFP4: grouped_kernel<FMT_NVFP4><<<grid, 256, 0, st>>>(a); break;
-    case FMT_MXFP4: grouped_kernel<FMT_MXFP4><<<grid, 256, 0, st>>>(a); break;
-    default: grouped_kernel<FMT_FP8><<<grid, 256, 0, st>>>(a); break;
+    case FMT_NVFP4: return launch_one<FMT_NVFP4>(a, grid, st);
+    case FMT_MXFP4: return launch_one<FMT_MXFP4>(a, grid, st);
+    default: return launch_one<FMT_FP8>(a, grid, st);
   }
-  return cudaGetLastError();
 }
 
 // y[t] = bf16( sum over t's slots in ascending expert id of o[t*K + slot] (fp32), + shared o[P + t] )

@@ -33,6 +33,7 @@ struct PermuteArgs {
   int32_t* n_active; // [1]
   int32_t* pair_tok; // [M*K]
   int32_t* pair_slot;// [M*K]
+  int32_t* err;      // cleared here, before the grouped kernels run
 };
 
 // One family of tiled weight matrices (one per expert, or a single matrix).
@@ -70,6 +71,7 @@ struct GroupedArgs {
   float* hs;           // W13 out: h scales (stride I/128)
   __nv_bfloat16* o;    // W2 / DENSE out (bf16), row stride n_rows
   int items_per_expert;
+  int* err;            // device flag: set to 1 if a bounded wait gave up (must start at 0)
 };
 
 cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int m, int e, int h, cudaStream_t st);

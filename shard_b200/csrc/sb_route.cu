@@ -85,10 +85,15 @@ __global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* _
   }
 }
 
-constexpr int MAX_E_PER_LANE = 32;  // E <= 1024
+// (value, expert) ordering of the top-k: larger value first, lower expert id on ties
+__device__ __forceinline__ bool before(float va, int ea, float vb, int eb) {
+  return va > vb || (va == vb && ea < eb);
+}
 
 // One CTA per token: the 4 warps quantise x[t] (act_quant, one 128-block per warp-iteration, loads
-// issued up front), then warp 0 does the top-k on lane-strided scores.
+// issued up front), then warp 0 routes. SPL = expert slots per lane (E <= 32 * SPL): every lane
+// sorts its slots once (bitonic network, biased score descending, ties to the lower id), then k
+// rounds of a warp-wide argmax over the lanes' current heads pick the top-k in order.
 __device__ __forceinline__ void quant_row(const RouteArgs& a, int t, int warp, int lane) {
   const __nv_bfloat16* xr = a.x + (size_t)t * a.hidden;
   const int nb = a.hidden / 128;
@@ -117,6 +122,7 @@ __device__ __forceinline__ void quant_row(const RouteArgs& a, int t, int warp, i
   }
 }
 
+template <int SPL>
 __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
@@ -125,46 +131,44 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
   if (warp != 0) return;
   const int E = a.n_experts;
   const int nsplit = a.hidden / gate_ksplit(a.hidden);
-  float sc[MAX_E_PER_LANE];
-  float mx = -INFINITY;
-  // logit = split 0 + split 1 + ... in ascending split order; the loads of one split are
-  // independent of each other, so each split costs one memory latency, not one per expert
+  // logits: split 0 + split 1 + ... in ascending split order (one memory latency per split)
+  float sc[SPL];
 #pragma unroll
-  for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+  for (int i = 0; i < SPL; ++i) {
     const int e = lane + 32 * i;
     sc[i] = e < E ? a.logits[(size_t)t * E + e] : -INFINITY;
   }
   for (int ks = 1; ks < nsplit; ++ks) {
     const float* pk = a.logits + ((size_t)ks * a.m + t) * E;
 #pragma unroll
-    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+    for (int i = 0; i < SPL; ++i) {
       const int e = lane + 32 * i;
       if (e < E) sc[i] += pk[e];
     }
   }
-#pragma unroll
-  for (int i = 0; i < MAX_E_PER_LANE; ++i) mx = fmaxf(mx, sc[i]);
   if (a.score_func == SCORE_SOFTMAX) {
-    mx = warp_max(mx);
-    float s = 0.f;
+    float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+    for (int i = 0; i < SPL; ++i) mx = fmaxf(mx, sc[i]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < SPL; ++i) {
       const int e = lane + 32 * i;
       sc[i] = e < E ? expf(sc[i] - mx) : 0.f;
-      s += sc[i];
+      sum += sc[i];
     }
-    s = warp_sum(s);
+    sum = warp_sum(sum);
 #pragma unroll
-    for (int i = 0; i < MAX_E_PER_LANE; ++i) sc[i] = __fdiv_rn(sc[i], s);
+    for (int i = 0; i < SPL; ++i) sc[i] = __fdiv_rn(sc[i], sum);
   } else if (a.score_func == SCORE_SIGMOID) {
 #pragma unroll
-    for (int i = 0; i < MAX_E_PER_LANE; ++i) sc[i] = __fdiv_rn(1.0f, 1.0f + expf(-sc[i]));
+    for (int i = 0; i < SPL; ++i) sc[i] = __fdiv_rn(1.0f, 1.0f + expf(-sc[i]));
   } else {
 #pragma unroll
-    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+    for (int i = 0; i < SPL; ++i) {
       const float l = sc[i];
-      const float sp = l > 20.f ? l : log1pf(expf(l));
-      sc[i] = sqrtf(sp);
+      sc[i] = sqrtf(l > 20.f ? l : log1pf(expf(l)));
     }
   }
   const int K = a.topk;
@@ -173,69 +177,106 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
   if (a.tid2eid != nullptr) {
     // hash routing: the ids come from the table, weights still from the unbiased scores
     const int64_t id = a.input_ids[t];
-    for (int j = 0; j < K; ++j) {
-      int e = a.tid2eid[id * K + j];
-      e = e < 0 ? 0 : (e >= E ? E - 1 : e);  // the host validates the table; this only keeps
-      sel[j] = e;                             // a corrupt one from indexing out of bounds
-      float mine = 0.f;
 #pragma unroll
-      for (int i = 0; i < MAX_E_PER_LANE; ++i)
-        if (lane + 32 * i == e) mine = sc[i];
-      wsel[j] = __shfl_sync(0xffffffffu, mine, e & 31);
+    for (int j = 0; j < 16; ++j) {
+      if (j < K) {
+        int e = a.tid2eid[id * K + j];
+        e = e < 0 ? 0 : (e >= E ? E - 1 : e);  // the host validates the table; this only keeps
+        sel[j] = e;                             // a corrupt one from indexing out of bounds
+        float mine = 0.f;
+#pragma unroll
+        for (int i = 0; i < SPL; ++i)
+          if (lane + 32 * i == e) mine = sc[i];
+        wsel[j] = __shfl_sync(0xffffffffu, mine, e & 31);
+      }
     }
   } else {
-    float bsel[MAX_E_PER_LANE];
+    // lane-local (biased value, expert, unbiased score), sorted once
+    float bv[SPL], uv[SPL];
+    int be[SPL];
 #pragma unroll
-    for (int i = 0; i < MAX_E_PER_LANE; ++i) {
+    for (int i = 0; i < SPL; ++i) {
       const int e = lane + 32 * i;
-      bsel[i] = e < E ? sc[i] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
+      bv[i] = e < E ? sc[i] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
+      be[i] = e < E ? e : 0x7fffffff;
+      uv[i] = sc[i];
     }
-    unsigned taken = 0u;  // bit i: this lane's slot i already selected
-    for (int j = 0; j < K; ++j) {
-      float bv = -INFINITY;
-      int be = 0x7fffffff;
 #pragma unroll
-      for (int i = 0; i < MAX_E_PER_LANE; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E && !(taken & (1u << i)) && (bsel[i] > bv || (bsel[i] == bv && e < be))) {
-          bv = bsel[i];
-          be = e;
+    for (int k2 = 2; k2 <= SPL; k2 <<= 1)
+#pragma unroll
+      for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1)
+#pragma unroll
+        for (int i = 0; i < SPL; ++i) {
+          const int l = i ^ j2;
+          if (l > i) {
+            const bool desc = (i & k2) == 0;
+            const bool swap = desc ? before(bv[l], be[l], bv[i], be[i]) : before(bv[i], be[i], bv[l], be[l]);
+            if (swap) {
+              const float tv = bv[i], tu = uv[i];
+              const int te = be[i];
+              bv[i] = bv[l];
+              uv[i] = uv[l];
+              be[i] = be[l];
+              bv[l] = tv;
+              uv[l] = tu;
+              be[l] = te;
+            }
+          }
+        }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j < K) {
+        float v = bv[0];
+        int e = be[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+          const int oe = __shfl_xor_sync(0xffffffffu, e, o);
+          if (before(ov, oe, v, e)) {
+            v = ov;
+            e = oe;
+          }
+        }
+        if (e >= E) e = j;  // only reachable with NaN scores; keeps every id in range
+        sel[j] = e;
+        const float mine = be[0] == e ? uv[0] : 0.f;
+        wsel[j] = __shfl_sync(0xffffffffu, mine, e & 31);
+        if (be[0] == e) {  // the owner pops its head
+#pragma unroll
+          for (int i = 0; i + 1 < SPL; ++i) {
+            bv[i] = bv[i + 1];
+            be[i] = be[i + 1];
+            uv[i] = uv[i + 1];
+          }
+          bv[SPL - 1] = -INFINITY;
+          be[SPL - 1] = 0x7fffffff;
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-        if (ov > bv || (ov == bv && oe < be)) {
-          bv = ov;
-          be = oe;
-        }
-      }
-      if (be >= E) be = j;  // only reachable with NaN scores; keeps every id in range
-      sel[j] = be;
-      float mine = 0.f;
-#pragma unroll
-      for (int i = 0; i < MAX_E_PER_LANE; ++i)
-        if (lane + 32 * i == be) {
-          mine = sc[i];
-          taken |= (1u << i);
-        }
-      wsel[j] = __shfl_sync(0xffffffffu, mine, be & 31);
     }
   }
   if (a.score_func != SCORE_SOFTMAX) {
     float s = 0.f;
-    for (int j = 0; j < K; ++j) s += wsel[j];
-    for (int j = 0; j < K; ++j) wsel[j] = __fdiv_rn(wsel[j], s);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < K) s += wsel[j];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < K) wsel[j] = __fdiv_rn(wsel[j], s);
   }
-  for (int j = 0; j < K; ++j) wsel[j] *= a.route_scale;
-  if (lane == 0) {
-    for (int j = 0; j < K; ++j) {
-      a.topk_idx[(size_t)t * K + j] = sel[j];
-      a.topk_w[(size_t)t * K + j] = wsel[j];
-      if (a.out_idx) a.out_idx[(size_t)t * K + j] = sel[j];
-      if (a.out_w) a.out_w[(size_t)t * K + j] = wsel[j];
-    }
+  if (lane < K) {
+    float w = 0.f;
+    int e = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j == lane) {
+        w = wsel[j];
+        e = sel[j];
+      }
+    w *= a.route_scale;
+    a.topk_idx[(size_t)t * K + lane] = e;
+    a.topk_w[(size_t)t * K + lane] = w;
+    if (a.out_idx) a.out_idx[(size_t)t * K + lane] = e;
+    if (a.out_w) a.out_w[(size_t)t * K + lane] = w;
   }
 }
 
@@ -247,6 +288,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   int* cursor = smem + a.n_experts;  // [E]
   __shared__ int warp_tot[32];
   const int E = a.n_experts, P = a.m * a.topk;
+  if (threadIdx.x == 0 && a.err) *a.err = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) atomicAdd(&cnt[a.topk_idx[p]], 1);
@@ -330,7 +372,13 @@ cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int 
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
-  route_kernel<<<a.m, 128, 0, st>>>(a);
+  const int spl = (a.n_experts + 31) / 32;
+  if (spl <= 1) route_kernel<1><<<a.m, 128, 0, st>>>(a);
+  else if (spl <= 2) route_kernel<2><<<a.m, 128, 0, st>>>(a);
+  else if (spl <= 4) route_kernel<4><<<a.m, 128, 0, st>>>(a);
+  else if (spl <= 8) route_kernel<8><<<a.m, 128, 0, st>>>(a);
+  else if (spl <= 16) route_kernel<16><<<a.m, 128, 0, st>>>(a);
+  else route_kernel<32><<<a.m, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -115,6 +115,13 @@ class MoELayer:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
+    def device_error(self) -> int:
+        """The forward's device error flag (workspace offset 0): 0, or 1 if a kernel's bounded wait on
+        its own bulk copies gave up. Reading it synchronises with the device."""
+        if self._ws is None:
+            return 0
+        return int(self._ws[:4].view(torch.int32).item())
+
     def weight_bytes(self) -> int:
         ts = [self.gate_w, self.w13, self.w13_s, self.w2, self.w2_s]
         ts += [t for t in (self.gate_bias, self.w13_ts, self.w2_ts) if t is not None]

@@ -104,6 +104,7 @@ def test_forward_matches_reference_golden(name):
     yref = O.bf16_from_bits(g["y_bits"])
     err = O.max_rel_err(_np(y), yref)
     assert err < TOL, f"{name}: max rel err {err:.3e}"
+    assert lay.device_error() == 0
 
 
 @pytest.mark.parametrize("name", ["c0_nvfp4_m8", "c0_mxfp4_m8", "small_fp8_noshared_m16", "v4route_nvfp4_m8"])
@@ -137,6 +138,7 @@ def test_full_size_forward(cname, m):
         alone = lay.forward(x[t:t + 1].cuda(), ids[t:t + 1].cuda())
         assert torch.equal(alone, y[t:t + 1]), "a token's output must not depend on its batch"
     assert torch.isfinite(y.float()).all()
+    assert lay.device_error() == 0
 
 
 def test_merged_chunks_equal_unmerged():
