@@ -329,6 +329,7 @@ def run_gpu(args, rank, world, local_rank):
                            "m": HEADLINE_M, "layers_per_gpu": LAYERS_PER_GPU, "chunks_per_step": C,
                            "hidden": cfg.hidden, "experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
                            "routed_fmt": "nvfp4", "shared_fmt": "fp8-128x128",
+                           "kernels": "tcgen05" if layers[0].layout == 1 else "mma.sync",
                            "l2": "no flush: each step streams >1 GB of distinct expert weights per layer (L2 126 MB)",
                            "parallelism": f"pp{world}"},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": bytes_io,
@@ -387,7 +388,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS_PER_GPU,
                     help="layers per GPU (a smaller stack is the small case for ncu captures)")
+    ap.add_argument("--layout", choices=["tc", "fragment"], default=None,
+                    help="weight layout / kernel family (default: the library default)")
     args = ap.parse_args()
+    if args.layout is not None:
+        import shard_b200.moe as sbm
+        from shard_b200 import _lib
+        sbm.DEFAULT_LAYOUT = _lib.LAYOUT_TC if args.layout == "tc" else _lib.LAYOUT_FRAGMENT
     args.warmup = max(args.warmup, 3)
     LAYERS_PER_GPU = args.layers
     world = env_int("WORLD_SIZE", 1)

@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define SB_ABI_VERSION 1
+#define SB_ABI_VERSION 3
 
 enum sb_status {
   SB_OK = 0,
@@ -48,6 +48,16 @@ enum sb_score { SB_SCORE_SOFTMAX = 0, SB_SCORE_SIGMOID = 1, SB_SCORE_SQRTSOFTPLU
  * rows with the same 8 w3 rows so one tensor-core tile yields gate and up values for the same
  * intermediate index. PLAIN is any other [N, K] matrix (w2, dense projections). */
 enum sb_matrix_kind { SB_MAT_PLAIN = 0, SB_MAT_W13 = 1 };
+
+/* Weight layouts (the forward's two kernel families).
+ *  SB_LAYOUT_FRAGMENT  16-row tiles of mma.sync register fragments (grouped_kernel).
+ *  SB_LAYOUT_TC        128-row blocks x 128-K stages for tcgen05 (one TMA box per stage): fp4 values
+ *                      [128 rows][64 B], FP8 values [128 rows][128 B], NVFP4 scales [128 rows][8 B], MXFP4
+ *                      scales [128 rows][4 B], FP8 scales [4] fp32 (block scale of rows 0-63, of rows
+ *                      64-127, two zero pads). A W13 block holds 64 w1 rows then the same 64 w3 rows.
+ *                      Pass the layout OR'ed into `kind` of the tiling calls (e.g. SB_MAT_W13 | SB_KIND_TC). */
+enum sb_layout { SB_LAYOUT_FRAGMENT = 0, SB_LAYOUT_TC = 1 };
+#define SB_KIND_TC 4
 
 /* One MoE layer as the forward reads it. All pointers are device pointers; weights are in the
  * TILED layout produced by sb_tile_weights / sb_tile_scales: 16-row tiles, each stored as the
@@ -82,6 +92,7 @@ typedef struct sb_moe_layer {
   const void* sh_w13_s;
   const void* sh_w2;
   const void* sh_w2_s;
+  int32_t layout;        /* sb_layout of every weight above */
 } sb_moe_layer;
 
 /* ── introspection ───────────────────────────────────────────────────────────────────────────── */
@@ -90,7 +101,7 @@ const char* sb_last_error(void);
 
 /* Bytes of one tiled [N, K] weight matrix, values and scales (identical to the canonical sizes). */
 size_t sb_tiled_bytes(int fmt, int64_t n, int64_t k);
-size_t sb_tiled_scale_bytes(int fmt, int64_t n, int64_t k);
+size_t sb_tiled_scale_bytes(int fmt, int kind, int64_t n, int64_t k);
 
 /* ── load-time layout (replaces _relayout_moe / bank_layout, v4_moe_grouped.py:382-540) ───────── */
 /* Canonical -> tiled, for n_mat matrices of [N, K] stored back to back.
@@ -104,10 +115,13 @@ int sb_tile_scales(int fmt, int kind, const void* src, void* dst, int64_t n_mat,
 /* ── the kernel-level seam (the reference's `kernel` module, kernel.py:105-125, 257-273, 518-536) ── */
 /* act_quant: bf16 x [M, K] -> e4m3 q [M, K] + fp32 s [M, K/128]; pow2 selects scale_fmt "ue8m0". */
 int sb_act_quant(const void* x, int64_t m, int64_t k, int pow2, void* q, float* s, void* stream);
-/* fp8_gemm / fp4_gemm: y bf16 [M, N] = dequant(q, s) @ dequant(W)^T with W tiled (PLAIN kind).
- * ts: NVFP4 tensor scale (device fp32 [1]) or NULL. */
-int sb_qgemm(int fmt, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
-             const void* q, const float* s, int64_t m, void* y, void* stream);
+/* fp8_gemm / fp4_gemm: y bf16 [M, N] = dequant(q, s) @ dequant(W)^T with W tiled (PLAIN kind, `layout`).
+ * ts: NVFP4 tensor scale (device fp32 [1]) or NULL. The tensor-core layout needs a workspace of
+ * sb_qgemm_workspace_bytes() (the activation panel); the fragment layout needs none (0, NULL ok). */
+size_t sb_qgemm_workspace_bytes(int fmt, int layout, int64_t n, int64_t k, int64_t m);
+int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
+             const void* q, const float* s, int64_t m, void* y, void* workspace, size_t workspace_bytes,
+             void* stream);
 
 /* ── the MoE stage forward (MoE.forward, model.py:634-649; Gate.forward :569-589;
  *    Expert.forward :601-611; grouped decode v4_moe_grouped.py:634-709) ──────────────────────── */

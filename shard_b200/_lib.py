@@ -15,8 +15,11 @@ SB_OK = 0
 STATUS = {0: "SB_OK", -1: "SB_ERR_ARG", -2: "SB_ERR_SHAPE", -3: "SB_ERR_FORMAT", -4: "SB_ERR_WORKSPACE",
           -5: "SB_ERR_CUDA", -6: "SB_ERR_UNSUPPORTED"}
 
+ABI_VERSION = 3
 SCORE = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 MAT_PLAIN, MAT_W13 = 0, 1
+KIND_TC = 4                      # OR'ed into a tiling kind: the tensor-core (tcgen05) layout
+LAYOUT_FRAGMENT, LAYOUT_TC = 0, 1
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -35,6 +38,7 @@ class SbMoeLayer(ctypes.Structure):
         ("gate_w", _vp), ("gate_bias", _vp), ("tid2eid", _vp), ("vocab", ctypes.c_int64),
         ("w13", _vp), ("w13_s", _vp), ("w13_ts", _vp), ("w2", _vp), ("w2_s", _vp), ("w2_ts", _vp),
         ("sh_w13", _vp), ("sh_w13_s", _vp), ("sh_w2", _vp), ("sh_w2_s", _vp),
+        ("layout", ctypes.c_int32),
     ]
 
 
@@ -43,11 +47,12 @@ SIGNATURES = {
     "sb_abi_version": (_int, []),
     "sb_last_error": (ctypes.c_char_p, []),
     "sb_tiled_bytes": (_sz, [_int, _i64, _i64]),
-    "sb_tiled_scale_bytes": (_sz, [_int, _i64, _i64]),
+    "sb_tiled_scale_bytes": (_sz, [_int, _int, _i64, _i64]),
     "sb_tile_weights": (_int, [_int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     "sb_tile_scales": (_int, [_int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     "sb_act_quant": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _vp]),
-    "sb_qgemm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
+    "sb_qgemm_workspace_bytes": (_sz, [_int, _int, _i64, _i64, _i64]),
+    "sb_qgemm": (_int, [_int, _int, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _sz, _vp]),
     "sb_moe_workspace_bytes": (_sz, [ctypes.POINTER(SbMoeLayer), _i64]),
     "sb_moe_forward": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sb_moe_forward_profiled": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp,
@@ -74,8 +79,8 @@ def lib():
             f = getattr(L, name)
             f.restype = res
             f.argtypes = args
-        if L.sb_abi_version() != 1:
-            raise ShardB200Error(f"ABI version mismatch: library {L.sb_abi_version()}, binding 1")
+        if L.sb_abi_version() != ABI_VERSION:
+            raise ShardB200Error(f"ABI version mismatch: library {L.sb_abi_version()}, binding {ABI_VERSION}")
         _LIB = L
     return _LIB
 

@@ -51,8 +51,23 @@ struct Workspace {
   uint8_t* hq;
   float* hs;
   __nv_bfloat16* o;
+  __nv_bfloat16* hbf;  // tensor-core layout: h in bf16 (quantised per 128 K into the w2 panel)
+  int32_t* pass_off;   // tensor-core layout: first pass of each active slot
+  uint8_t* bpanel;     // tensor-core layout: B tiles of every (pass, stage)
+  float* apanel;       //                     and their row scales
+  int n_sh_pass;
   size_t bytes;
 };
+
+// Tensor-core layout: passes of the shared expert (FP8, 16 tokens each).
+int64_t shared_passes(const sb_moe_layer* L, int64_t m) { return L->has_shared ? (m + 15) / 16 : 0; }
+
+// Upper bound of the passes of one grouped launch: sum over experts of ceil(count / pass_max)
+// <= P / pass_max + (active experts).
+int64_t max_passes(const sb_moe_layer* L, int64_t m) {
+  const int64_t P = m * L->topk, E = L->n_experts;
+  return shared_passes(L, m) + P / sb::tc_pass_max(L->expert_fmt) + (P < E ? P : E);
+}
 
 Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   Workspace w;
@@ -77,9 +92,16 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   w.n_active = (int32_t*)take(sizeof(int32_t));
   w.pair_tok = (int32_t*)take(sizeof(int32_t) * P);
   w.pair_slot = (int32_t*)take(sizeof(int32_t) * P);
-  w.hq = take((size_t)R * I);
-  w.hs = (float*)take(sizeof(float) * R * (I / 128));
+  const bool tc = L->layout == SB_LAYOUT_TC;
+  w.hq = take(tc ? 0 : (size_t)R * I);
+  w.hs = (float*)take(tc ? 0 : sizeof(float) * R * (I / 128));
   w.o = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * H);
+  w.hbf = (__nv_bfloat16*)take(tc ? sizeof(__nv_bfloat16) * R * I : 0);
+  w.pass_off = (int32_t*)take(tc ? sizeof(int32_t) * (E + 1) : 0);
+  const int64_t panel_tiles = tc ? max_passes(L, m) * ((H > I ? H : I) / 128) : 0;
+  w.bpanel = take((size_t)panel_tiles * 2048);
+  w.apanel = (float*)take((size_t)panel_tiles * 16 * sizeof(float));
+  w.n_sh_pass = (int)shared_passes(L, m);
   w.bytes = off;
   return w;
 }
@@ -104,6 +126,7 @@ int check_layer(const sb_moe_layer* L) {
       (L->has_shared && (!aligned16(L->sh_w13) || !aligned16(L->sh_w2))))
     return fail(SB_ERR_ARG, "weight pointers must be 16-byte aligned");
   if (L->tid2eid && L->vocab <= 0) return fail(SB_ERR_ARG, "tid2eid given with vocab=%lld", (long long)L->vocab);
+  if (L->layout != SB_LAYOUT_FRAGMENT && L->layout != SB_LAYOUT_TC) return fail(SB_ERR_ARG, "layout=%d unknown", L->layout);
   return SB_OK;
 }
 
@@ -116,7 +139,7 @@ sb::WeightSet routed_set(const sb_moe_layer* L, bool w13) {
   s.ts = L->expert_fmt == SB_FMT_NVFP4 ? (w13 ? L->w13_ts : L->w2_ts) : nullptr;
   s.ts_stride = w13 ? 2 : 1;
   s.w_stride = sb_tiled_bytes(L->expert_fmt, n, k);
-  s.s_stride = sb_tiled_scale_bytes(L->expert_fmt, n, k);
+  s.s_stride = sb_tiled_scale_bytes(L->expert_fmt, L->layout == SB_LAYOUT_TC ? SB_KIND_TC : 0, n, k);
   s.fmt = L->expert_fmt;
   return s;
 }
@@ -144,20 +167,22 @@ size_t sb_tiled_bytes(int fmt, int64_t n, int64_t k) {
   return 0;
 }
 
-size_t sb_tiled_scale_bytes(int fmt, int64_t n, int64_t k) {
+size_t sb_tiled_scale_bytes(int fmt, int kind, int64_t n, int64_t k) {
   if (fmt == SB_FMT_NVFP4) return (size_t)(n * (k / 16));
   if (fmt == SB_FMT_MXFP4) return (size_t)(n * (k / 32));
-  if (fmt == SB_FMT_FP8) return (size_t)((n / 16) * (k / 128) * 8);
+  if (fmt == SB_FMT_FP8) return (kind & SB_KIND_TC) ? (size_t)((n / 128) * (k / 128) * 16) : (size_t)((n / 16) * (k / 128) * 8);
   return 0;
 }
 
 static int check_tile_args(int fmt, int kind, const void* src, const void* dst, int64_t n_mat, int64_t n, int64_t k) {
   if (!src || !dst) return fail(SB_ERR_ARG, "tile: NULL pointer");
   if (fmt != SB_FMT_NVFP4 && fmt != SB_FMT_MXFP4 && fmt != SB_FMT_FP8) return fail(SB_ERR_FORMAT, "tile: format %d", fmt);
-  if (kind != SB_MAT_PLAIN && kind != SB_MAT_W13) return fail(SB_ERR_ARG, "tile: kind %d", kind);
+  if ((kind & 3) != SB_MAT_PLAIN && (kind & 3) != SB_MAT_W13) return fail(SB_ERR_ARG, "tile: kind %d", kind);
+  if ((kind & SB_KIND_TC) && (n < 128 || n % 128))
+    return fail(SB_ERR_SHAPE, "tile: the tensor-core layout needs n %% 128 == 0 (n=%lld)", (long long)n);
   if (n_mat < 1 || n < 32 || n % 32 || k < 128 || k % 128)
     return fail(SB_ERR_SHAPE, "tile: need n %% 32 == 0 and k %% 128 == 0 (n=%lld k=%lld)", (long long)n, (long long)k);
-  if (kind == SB_MAT_W13 && (n / 2) % 128)
+  if ((kind & 3) == SB_MAT_W13 && (n / 2) % 128)
     return fail(SB_ERR_SHAPE, "tile: W13 needs the intermediate size n/2 %% 128 == 0 (n=%lld)", (long long)n);
   return SB_OK;
 }
@@ -166,6 +191,8 @@ int sb_tile_weights(int fmt, int kind, const void* src, void* dst, int64_t n_mat
   int rc = check_tile_args(fmt, kind, src, dst, n_mat, n, k);
   if (rc) return rc;
   if (!aligned16(dst)) return fail(SB_ERR_ARG, "tile: dst must be 16-byte aligned");
+  if (kind & SB_KIND_TC)
+    return cuda_check(sb::launch_tc_tile(fmt, kind & 3, false, src, dst, n_mat, n, k, (cudaStream_t)stream), "tile_weights");
   return cuda_check(sb::launch_tile_weights(fmt, kind, src, dst, n_mat, n, k, (cudaStream_t)stream), "tile_weights");
 }
 
@@ -173,6 +200,8 @@ int sb_tile_scales(int fmt, int kind, const void* src, void* dst, int64_t n_mat,
   int rc = check_tile_args(fmt, kind, src, dst, n_mat, n, k);
   if (rc) return rc;
   if ((reinterpret_cast<uintptr_t>(dst) & 7u) != 0) return fail(SB_ERR_ARG, "tile: scale dst must be 8-byte aligned");
+  if (kind & SB_KIND_TC)
+    return cuda_check(sb::launch_tc_tile(fmt, kind & 3, true, src, dst, n_mat, n, k, (cudaStream_t)stream), "tile_scales");
   return cuda_check(sb::launch_tile_scales(fmt, kind, src, dst, n_mat, n, k, (cudaStream_t)stream), "tile_scales");
 }
 
@@ -183,8 +212,31 @@ int sb_act_quant(const void* x, int64_t m, int64_t k, int pow2, void* q, float* 
   return cuda_check(sb::launch_act_quant(x, m, k, pow2, (uint8_t*)q, s, (cudaStream_t)stream), "act_quant");
 }
 
-int sb_qgemm(int fmt, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k, const void* q,
-             const float* s, int64_t m, void* y, void* stream) {
+// Dense tensor-core GEMM scratch: error flag, then the B panel of ceil(m / pass_max) passes.
+static size_t qgemm_ws(int fmt, int layout, int64_t k, int64_t m, uint8_t* base, int** err, uint8_t** bpanel,
+                       float** apanel) {
+  if (layout != SB_LAYOUT_TC) return 0;
+  const int64_t pm = sb::tc_pass_max(fmt);
+  const int64_t tiles = ((m + pm - 1) / pm) * (k / 128);
+  size_t off = 0;
+  if (err) *err = base ? (int*)(base + off) : nullptr;
+  off += 256;
+  if (bpanel) *bpanel = base ? base + off : nullptr;
+  off += align256((size_t)tiles * 2048);
+  if (apanel) *apanel = base ? (float*)(base + off) : nullptr;
+  off += align256((size_t)tiles * 16 * sizeof(float));
+  return off;
+}
+
+size_t sb_qgemm_workspace_bytes(int fmt, int layout, int64_t n, int64_t k, int64_t m) {
+  (void)n;
+  if (k < 128 || k % 128 || m < 0) return 0;
+  return qgemm_ws(fmt, layout, k, m < 1 ? 1 : m, nullptr, nullptr, nullptr, nullptr);
+}
+
+int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
+             const void* q, const float* s, int64_t m, void* y, void* workspace, size_t workspace_bytes,
+             void* stream) {
   if (!w || !w_s || !q || !s || !y) return fail(SB_ERR_ARG, "qgemm: NULL pointer");
   if (fmt != SB_FMT_NVFP4 && fmt != SB_FMT_MXFP4 && fmt != SB_FMT_FP8) return fail(SB_ERR_FORMAT, "qgemm: format %d", fmt);
   if (fmt == SB_FMT_NVFP4 && !ts) return fail(SB_ERR_ARG, "qgemm: NVFP4 needs a tensor scale");
@@ -210,6 +262,45 @@ int sb_qgemm(int fmt, const void* w, const void* w_s, const float* ts, int64_t n
   a.bq = (const uint8_t*)q;
   a.bs = s;
   a.o = (__nv_bfloat16*)y;
+  if (layout == SB_LAYOUT_TC) {
+    if (n % 128) return fail(SB_ERR_SHAPE, "qgemm: the tensor-core layout needs n %% 128 == 0");
+    int* err = nullptr;
+    uint8_t* bpanel = nullptr;
+    float* apanel = nullptr;
+    const size_t need = qgemm_ws(fmt, layout, k, m, (uint8_t*)workspace, &err, &bpanel, &apanel);
+    if (!workspace || workspace_bytes < need)
+      return fail(SB_ERR_WORKSPACE, "qgemm: workspace %zu bytes < %zu needed", workspace_bytes, need);
+    if (!aligned16(q)) return fail(SB_ERR_ARG, "qgemm: activations must be 16-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = cuda_check(cudaMemsetAsync(err, 0, sizeof(int), st), "qgemm");
+    if (rc) return rc;
+    const int pm = sb::tc_pass_max(fmt);
+    sb::PanelArgs pa;
+    memset(&pa, 0, sizeof pa);
+    pa.mode = sb::MODE_DENSE;
+    pa.m = (int)m;
+    pa.topk = 1;
+    pa.k = (int)k;
+    pa.has_shared = 1;
+    pa.n_sh_pass = (int)((m + pm - 1) / pm);
+    pa.nv_shared = fmt == SB_FMT_NVFP4;
+    pa.xq = (const uint8_t*)q;
+    pa.xs = s;
+    pa.bpanel = bpanel;
+    pa.apanel = apanel;
+    rc = cuda_check(sb::launch_tc_panel(pa, 1, st), "qgemm panel");
+    if (rc) return rc;
+    sb::TcPlan plan;
+    plan.bpanel = bpanel;
+    plan.apanel = apanel;
+    plan.pass_off = nullptr;
+    plan.n_sh_pass = pa.n_sh_pass;
+    a.shared.s_stride = 0;
+    a.routed = a.shared;
+    a.err = err;
+    a.items_per_expert = (int)(n / 128);
+    return cuda_check(sb::launch_tc_grouped(a, plan, a.items_per_expert, st), "qgemm");
+  }
   a.items_per_expert = (int)((n + 255) / 256);
   return cuda_check(sb::launch_grouped(a, a.items_per_expert, 0, (cudaStream_t)stream), "qgemm");
 }
@@ -294,6 +385,8 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.pair_tok = w.pair_tok;
   p.pair_slot = w.pair_slot;
   p.err = w.err;
+  p.pass_max = L->layout == SB_LAYOUT_TC ? sb::tc_pass_max(L->expert_fmt) : 0;
+  p.pass_off = L->layout == SB_LAYOUT_TC ? w.pass_off : nullptr;
   rc = cuda_check(sb::launch_permute(p, st), "permute");
   if (rc) return rc;
   mark(2);
@@ -315,6 +408,63 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   g.pair_slot = w.pair_slot;
   g.topk_w = w.topk_w;
   g.err = w.err;
+  const int n_units = (int)(max_active + (L->has_shared ? 1 : 0));
+  if (L->layout == SB_LAYOUT_TC) {
+    // tensor-core path: w13 panel, w13 (+ SwiGLU -> h bf16), w2 panel (act_quant of h), w2
+    sb::TcPlan plan;
+    plan.bpanel = w.bpanel;
+    plan.apanel = w.apanel;
+    plan.pass_off = w.pass_off;
+    plan.n_sh_pass = w.n_sh_pass;
+    sb::PanelArgs pa;
+    memset(&pa, 0, sizeof pa);
+    pa.mode = sb::MODE_W13;
+    pa.m = (int)m;
+    pa.topk = L->topk;
+    pa.k = (int)H;
+    pa.act_pow2 = L->act_pow2;
+    pa.has_shared = L->has_shared;
+    pa.n_sh_pass = w.n_sh_pass;
+    pa.nv_routed = L->expert_fmt == SB_FMT_NVFP4;
+    pa.nv_shared = 0;
+    pa.xq = w.xq;
+    pa.xs = w.xs;
+    pa.hbf = w.hbf;
+    pa.counts = w.counts;
+    pa.offsets = w.offsets;
+    pa.active = w.active;
+    pa.n_active = w.n_active;
+    pa.pass_off = w.pass_off;
+    pa.pair_tok = w.pair_tok;
+    pa.bpanel = w.bpanel;
+    pa.apanel = w.apanel;
+    rc = cuda_check(sb::launch_tc_panel(pa, n_units, st), "tc w13 panel");
+    if (rc) return rc;
+    g.mode = sb::MODE_W13;
+    g.n_rows = (int)(2 * I);
+    g.k = (int)H;
+    g.routed = routed_set(L, true);
+    g.shared = shared_set(L, true);
+    g.hbf = w.hbf;
+    g.n_experts = L->n_experts;
+    g.items_per_expert = (int)(I / 64);
+    rc = cuda_check(sb::launch_tc_grouped(g, plan, n_units * g.items_per_expert, st), "tc w13");
+    if (rc) return rc;
+    mark(3);
+    pa.mode = sb::MODE_W2;
+    pa.k = (int)I;
+    rc = cuda_check(sb::launch_tc_panel(pa, n_units, st), "tc w2 panel");
+    if (rc) return rc;
+    g.mode = sb::MODE_W2;
+    g.n_rows = (int)H;
+    g.k = (int)I;
+    g.routed = routed_set(L, false);
+    g.shared = shared_set(L, false);
+    g.o = w.o;
+    g.items_per_expert = (int)(H / 128);
+    rc = cuda_check(sb::launch_tc_grouped(g, plan, n_units * g.items_per_expert, st), "tc w2");
+    if (rc) return rc;
+  } else {
   // w13 (+ SwiGLU, + act_quant of h)
   g.mode = sb::MODE_W13;
   g.n_rows = (int)(2 * I);
@@ -326,8 +476,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   g.hq = w.hq;
   g.hs = w.hs;
   g.items_per_expert = (int)(I / 128);
-  rc = cuda_check(sb::launch_grouped(g, (int)((max_active + (L->has_shared ? 1 : 0)) * g.items_per_expert), 0, st),
-                  "grouped w13");
+  rc = cuda_check(sb::launch_grouped(g, n_units * g.items_per_expert, 0, st), "grouped w13");
   if (rc) return rc;
   mark(3);
   // w2
@@ -340,9 +489,9 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   g.bs = w.hs;
   g.o = w.o;
   g.items_per_expert = (int)((H + 255) / 256);
-  rc = cuda_check(sb::launch_grouped(g, (int)((max_active + (L->has_shared ? 1 : 0)) * g.items_per_expert), 0, st),
-                  "grouped w2");
+  rc = cuda_check(sb::launch_grouped(g, n_units * g.items_per_expert, 0, st), "grouped w2");
   if (rc) return rc;
+  }
   mark(4);
   rc = cuda_check(sb::launch_combine(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
                                      (__nv_bfloat16*)y, st),

@@ -107,6 +107,13 @@ __device__ __forceinline__ uint8_t act_q(float v, float s) {
   return f32_to_e4m3(q);
 }
 
+// act_q with the reciprocal of a power-of-two scale: v * (1/s) is exactly v / s for such s
+__device__ __forceinline__ uint8_t act_q_pow2(float v, float inv_s) {
+  float q = v * inv_s;
+  q = fminf(fmaxf(q, -448.0f), 448.0f);
+  return f32_to_e4m3(q);
+}
+
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
 // ── tensor-core fragments (mma.sync, fp32 accumulate) ───────────────────────────────────────────
@@ -184,6 +191,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// try_wait with a suspend-time hint (ns): the thread sleeps in hardware until the phase completes
+// or the hint expires, instead of spinning on issue slots
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }

@@ -1,6 +1,7 @@
 // Host-side launch interface between the C-ABI layer (sb_abi.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stddef.h>
@@ -34,6 +35,8 @@ struct PermuteArgs {
   int32_t* pair_tok; // [M*K]
   int32_t* pair_slot;// [M*K]
   int32_t* err;      // cleared here, before the grouped kernels run
+  int pass_max;      // tensor-core path: tokens per pass of a routed expert (0: no pass table)
+  int32_t* pass_off; // [E+1] by active slot: first pass of the slot, total passes at [n_active]
 };
 
 // One family of tiled weight matrices (one per expert, or a single matrix).
@@ -72,7 +75,41 @@ struct GroupedArgs {
   __nv_bfloat16* o;    // W2 / DENSE out (bf16), row stride n_rows
   int items_per_expert;
   int* err;            // device flag: set to 1 if a bounded wait gave up (must start at 0)
+  __nv_bfloat16* hbf;  // tensor-core path: h in bf16 (W13 writes it, the W2 panel quantises it)
+  int n_experts;       // tensor-core path: matrices in the routed bank
 };
+
+// Tensor-core path: the activation operand of every pass, prepared before the grouped launch.
+// Pass order: the shared expert's (or the dense matrix's) passes first, then each active expert's
+// in active-slot order. A pass holds up to 16 B rows: 16 tokens, or for NVFP4 weights 8 tokens
+// twice (rows 2t / 2t+1 keep the first / second 16 K of every 32 K, so each output column pair
+// carries the two per-16 partial sums).
+struct TcPlan {
+  const uint8_t* bpanel;    // [pass][stage][16 rows][128 B] e4m3, 128-byte swizzled
+  const float* apanel;      // [pass][stage][16] activation scale of each B row (0 for empty rows)
+  const int32_t* pass_off;  // [E+1] by active slot (routed passes follow the n_sh_pass shared ones)
+  int n_sh_pass;
+};
+
+struct PanelArgs {
+  int mode;                 // MODE_W13 / MODE_DENSE: e4m3 rows; MODE_W2: bf16 rows quantised here
+  int m, topk, k, act_pow2;
+  int has_shared, n_sh_pass;
+  int nv_routed, nv_shared; // 1: NVFP4 weights (8 tokens per pass, split rows)
+  const uint8_t* xq;        // [rows][k] e4m3 (W13: tokens; DENSE: the caller's activations)
+  const float* xs;          // [rows][k/128]
+  const __nv_bfloat16* hbf; // W2: [P + m][k] bf16
+  const int32_t* counts;
+  const int32_t* offsets;
+  const int32_t* active;
+  const int32_t* n_active;
+  const int32_t* pass_off;
+  const int32_t* pair_tok;
+  uint8_t* bpanel;
+  float* apanel;
+};
+
+__host__ __device__ inline int tc_pass_max(int fmt) { return fmt == 1 ? 8 : 16; }
 
 cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int m, int e, int h, cudaStream_t st);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
@@ -86,6 +123,10 @@ cudaError_t launch_tile_weights(int fmt, int kind, const void* src, void* dst, i
 cudaError_t launch_tile_scales(int fmt, int kind, const void* src, void* dst, int64_t n_mat, int64_t n,
                                int64_t k, cudaStream_t st);
 cudaError_t launch_selftest(float* out, cudaStream_t st);
+cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st);
+cudaError_t launch_tc_grouped(const GroupedArgs& a, const TcPlan& plan, int max_items, cudaStream_t st);
+cudaError_t launch_tc_tile(int fmt, int kind, bool scales, const void* src, void* dst, int64_t n_mat, int64_t n,
+                           int64_t k, cudaStream_t st);
 
 int num_sms();
 

@@ -297,49 +297,59 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   const int e = threadIdx.x;
   const int c = e < E ? cnt[e] : 0;
   const int flag = c > 0 ? 1 : 0;
+  const int np = a.pass_max > 0 ? (c + a.pass_max - 1) / a.pass_max : 0;  // passes of expert e
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl = c, fincl = flag;
+  int incl = c, fincl = flag, pincl = np;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int v = __shfl_up_sync(0xffffffffu, incl, o);
     const int fv = __shfl_up_sync(0xffffffffu, fincl, o);
+    const int pv = __shfl_up_sync(0xffffffffu, pincl, o);
     if (lane >= o) {
       incl += v;
       fincl += fv;
+      pincl += pv;
     }
   }
-  __shared__ int warp_ftot[32];
+  __shared__ int warp_ftot[32], warp_ptot[32];
   if (lane == 31) {
     warp_tot[warp] = incl;
     warp_ftot[warp] = fincl;
+    warp_ptot[warp] = pincl;
   }
   __syncthreads();
   if (warp == 0) {
-    int v = warp_tot[lane], fv = warp_ftot[lane];
+    int v = warp_tot[lane], fv = warp_ftot[lane], pv = warp_ptot[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int u = __shfl_up_sync(0xffffffffu, v, o);
       const int fu = __shfl_up_sync(0xffffffffu, fv, o);
+      const int pu = __shfl_up_sync(0xffffffffu, pv, o);
       if (lane >= o) {
         v += u;
         fv += fu;
+        pv += pu;
       }
     }
     warp_tot[lane] = v;
     warp_ftot[lane] = fv;
+    warp_ptot[lane] = pv;
   }
   __syncthreads();
   const int base = warp > 0 ? warp_tot[warp - 1] : 0;
   const int fbase = warp > 0 ? warp_ftot[warp - 1] : 0;
+  const int pbase = warp > 0 ? warp_ptot[warp - 1] : 0;
   if (e < E) {
     const int off = base + incl - c;
     a.offsets[e] = off;
     a.counts[e] = c;
     cursor[e] = off;
     if (flag) a.active[fbase + fincl - 1] = e;
+    if (flag && a.pass_off) a.pass_off[fbase + fincl - 1] = pbase + pincl - np;
     if (e == E - 1) {
       a.offsets[E] = base + incl;
       *a.n_active = fbase + fincl;
+      if (a.pass_off) a.pass_off[fbase + fincl] = pbase + pincl;
     }
   }
   __syncthreads();

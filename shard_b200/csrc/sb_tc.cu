@@ -1,0 +1,766 @@
+// Grouped expert GEMV/GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// One CTA walks ITEMS = (expert or shared expert, 128-row block of a weight matrix) of the
+// device-side permutation (shared expert first); an item runs its expert's token PASSES (up to 16
+// B rows each) over the K stages (128 K per stage). Roles (192 threads):
+//   warp 4     producer: lane 0 keeps ST stages of asynchronous copies in flight. A stage is
+//                - the weight tile, 128 rows x 128 K, by a TMA tensor load that lands it directly
+//                  in the 128B-swizzled K-major operand form tcgen05.mma reads: fp4 weights use the
+//                  16U4_ALIGN16B element type (each 16 packed e2m1 values land in the low 8 bytes
+//                  of a 16-byte slot, the form kind::f8f6f4 reads e2m1 in), FP8 weights are bytes;
+//                - the pass's B tile (16 rows x 128 B e4m3, pre-swizzled by the panel kernel) and
+//                  its 16 row scales, by plain bulk copies;
+//                - the weight scales of the stage (NVFP4 8 B / MXFP4 4 B per row, FP8 two fp32).
+//   warp 5     MMA issuer: allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=16, K=32) and
+//              tcgen05.commit. fp4 weights: one fresh 16-column TMEM slot per 32-K chunk (their
+//              per-16 / per-32 scales are applied at readback); FP8: the stage's 4 chunks
+//              accumulate into one slot (one 128x128 block scale per stage).
+//   warps 0-3  readback: thread r owns weight row r (TMEM lane r); per stage it loads the used
+//              columns with tcgen05.ld, applies the weight scales and the B row scales in fp32 and
+//              accumulates; then the epilogue (W13: SwiGLU pairs rows r / r+64 -> h bf16; W2 /
+//              DENSE: bf16 rows of o).
+// The three roles run decoupled through mbarriers across item and pass boundaries: the producer
+// and the MMA issuer run ahead of the readback by up to ST stages / SA accumulator groups.
+// The tensor core sums exact products (e2m1 x e4m3 and e4m3 x e4m3 are exact in fp32).
+//
+// Every wait is bounded: on timeout the CTA records an error in *err and winds down.
+#include <cudaTypedefs.h>
+
+#include "sb_device.cuh"
+#include "sb_launch.h"
+
+namespace sb {
+namespace tc {
+
+constexpr int NTHREADS = 192;
+constexpr int PRODUCER_WARP = 4;
+constexpr int MMA_WARP = 5;
+constexpr int ST = 5;           // stage ring (A + B + scales)
+constexpr int SA = 4;           // accumulator groups in TMEM
+constexpr int NB = 16;          // MMA N (columns per chunk slot)
+constexpr int GCOLS = 4 * NB;   // TMEM columns of one accumulator group (4 chunk slots)
+constexpr int TMEM_COLS = SA * GCOLS;
+constexpr int A_BYTES = 128 * 128;
+constexpr int B_BYTES = NB * 128;
+constexpr int SCL_BYTES = 1024;
+constexpr uint32_t WAIT_LIMIT = 1u << 16;  // polls; each may sleep up to ~1 us
+
+struct Smem {
+  uint8_t A[ST][A_BYTES];       // 1024-aligned (128B swizzle atoms)
+  uint8_t B[ST][B_BYTES];
+  uint8_t scl[ST][SCL_BYTES];
+  float asc[ST][NB];
+  uint64_t full[ST], sempty[ST], gfull[SA], gempty[SA];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  float xchg[64][17];
+};
+constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
+
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                 // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                 // 128-byte swizzle
+  return d;
+}
+
+// kind::f8f6f4, D fp32, A format afmt (0 e4m3, 5 e2m1), B e4m3, K-major both, M=128, N=NB
+__device__ __forceinline__ uint32_t idesc(uint32_t afmt) {
+  return (1u << 4) | (afmt << 7) | (0u << 10) | ((uint32_t)(NB >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(ad), "l"(bd), "r"(id), "r"(acc));
+}
+
+__device__ __forceinline__ void commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// TMA tensor load of a 2-D box at (c0, c1), completing on an mbarrier (no multicast)
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 16 / 4 consecutive TMEM columns of this warp's 32 lanes; completion is awaited separately
+__device__ __forceinline__ void ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void ld4(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+__device__ __forceinline__ void arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool aborted(Smem& sm) { return *reinterpret_cast<volatile int*>(&sm.abort) != 0; }
+
+__device__ __forceinline__ void set_abort(Smem& sm, int* err, bool flag_err) {
+  if (flag_err) atomicExch(err, 1);
+  *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+}
+
+// bounded wait; on timeout flag the CTA (and the launch) and return false
+__device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t parity) {
+  if (aborted(sm)) return false;
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+    if ((i & 63u) == 63u && aborted(sm)) return false;
+  }
+  set_abort(sm, err, true);
+  return false;
+}
+
+// OR of `pred` over the 128 worker threads, on named barrier 1 (a uniform decision for all of them)
+__device__ __forceinline__ bool workers_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.red.or.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+
+struct Item {
+  int shared, expert, slot, rb, cnt, base;
+};
+
+__device__ __forceinline__ Item item_of(const GroupedArgs& a, int item, int n_sh) {
+  Item it;
+  if (item < n_sh) {
+    it.shared = 1;
+    it.expert = 0;
+    it.slot = 0;
+    it.rb = item;
+    it.cnt = a.m;
+    it.base = 0;
+  } else {
+    const int r = item - n_sh;
+    it.shared = 0;
+    it.slot = r / a.items_per_expert;
+    it.expert = a.active[it.slot];
+    it.rb = r % a.items_per_expert;
+    it.cnt = a.counts[it.expert];
+    it.base = a.offsets[it.expert];
+  }
+  return it;
+}
+
+__host__ __device__ inline int stage_sbytes(int fmt) { return fmt == FMT_NVFP4 ? 1024 : (fmt == FMT_MXFP4 ? 512 : 16); }
+
+// error flag of launches without a workspace
+__device__ int g_tc_dense_err = 0;
+
+struct TcArgs {
+  CUtensorMap map_routed;   // weights of the routed bank (or unused)
+  CUtensorMap map_shared;   // weights of the shared expert / dense matrix
+  GroupedArgs g;
+  TcPlan plan;
+};
+
+template <int FMT_R>
+__global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_constant__ TcArgs ta) {
+  const GroupedArgs& a = ta.g;
+  extern __shared__ uint8_t dyn_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~(uintptr_t)1023);
+  int* err = a.err != nullptr ? a.err : &g_tc_dense_err;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(smem_addr(&sm.full[s]), 1);
+      mbar_init(smem_addr(&sm.sempty[s]), 4);
+    }
+    for (int q = 0; q < SA; ++q) {
+      mbar_init(smem_addr(&sm.gfull[q]), 1);
+      mbar_init(smem_addr(&sm.gempty[q]), 4);
+    }
+    mbar_init(smem_addr(&sm.drain), 1);
+    sm.abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(&sm.tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tbase = sm.tmem_base;
+
+  const int n_sh = a.has_shared ? a.items_per_expert : 0;
+  const int n_items = n_sh + (a.mode == MODE_DENSE ? 0 : (*a.n_active) * a.items_per_expert);
+  const int P = a.m * a.topk;
+  const int K = a.k;
+  const int nst = K / 128;
+  const int nrb = a.n_rows / 128;
+  const bool w13 = a.mode == MODE_W13;
+
+  // per-item constants shared by the roles
+  auto item_fmt = [&](const Item& it) { return it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R; };
+  auto first_pass = [&](const Item& it) { return it.shared ? 0 : ta.plan.n_sh_pass + ta.plan.pass_off[it.slot]; };
+
+  if (warp == PRODUCER_WARP) {
+    if (lane == 0) {
+      prefetch_map(&ta.map_routed);
+      prefetch_map(&ta.map_shared);
+      uint32_t g = 0, issued = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const Item it = item_of(a, item, n_sh);
+        const int fmt = item_fmt(it);
+        const WeightSet& ws = it.shared ? a.shared : a.routed;
+        const CUtensorMap* map = it.shared ? &ta.map_shared : &ta.map_routed;
+        const int pm = tc_pass_max(fmt);
+        const uint32_t abytes = fmt == FMT_FP8 ? 16384u : 8192u;
+        const uint32_t sb = stage_sbytes(fmt);
+        const int row0 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;
+        const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)it.rb * nst * sb;
+        const int pass0 = first_pass(it);
+        for (int pb = 0, pi = 0; pb < it.cnt && ok; pb += pm, ++pi) {
+          if (*reinterpret_cast<volatile int*>(err)) {
+            set_abort(sm, err, false);
+            ok = false;
+            break;
+          }
+          const size_t pst = (size_t)(pass0 + pi) * nst;
+          for (int j = 0; j < nst; ++j, ++g) {
+            const uint32_t s = g % ST;
+            if (!wait(sm, err, smem_addr(&sm.sempty[s]), ((g / ST) & 1u) ^ 1u)) {
+              ok = false;
+              break;
+            }
+            const uint32_t bar = smem_addr(&sm.full[s]);
+            mbar_expect_tx(bar, abytes + B_BYTES + NB * 4 + sb);
+            tma_load_2d(smem_addr(sm.A[s]), map, 0, row0 + j * 128, bar);
+            bulk_g2s(smem_addr(sm.B[s]), ta.plan.bpanel + (pst + j) * B_BYTES, B_BYTES, bar);
+            bulk_g2s(smem_addr(sm.asc[s]), ta.plan.apanel + (pst + j) * NB, NB * 4, bar);
+            bulk_g2s(smem_addr(sm.scl[s]), sbase + (size_t)j * sb, sb, bar);
+            issued = g + 1;
+          }
+        }
+      }
+      // before the CTA's shared memory is released: wait for this CTA's copies still in flight
+      // (only when a wait gave up; otherwise every stage was consumed)
+      for (uint32_t h = issued > (uint32_t)ST ? issued - ST : 0; h < issued; ++h)
+        for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+          if (mbar_try_wait(smem_addr(&sm.full[h % ST]), (h / ST) & 1u)) break;
+    }
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const Item it = item_of(a, item, n_sh);
+        const int fmt = item_fmt(it);
+        const int pm = tc_pass_max(fmt);
+        const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
+        for (int pb = 0; pb < it.cnt && ok; pb += pm) {
+          for (int j = 0; j < nst; ++j, ++g) {
+            const uint32_t s = g % ST, q = g % SA;
+            if (!wait(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u) ||
+                !wait(sm, err, smem_addr(&sm.gempty[q]), ((g / SA) & 1u) ^ 1u)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            const uint32_t abase = smem_addr(sm.A[s]), bbase = smem_addr(sm.B[s]);
+            const uint32_t cols = tbase + q * GCOLS;
+            if (fmt == FMT_FP8) {
+#pragma unroll
+              for (int c = 0; c < 4; ++c) mma(cols, sdesc(abase + c * 32), sdesc(bbase + c * 32), id, c > 0 ? 1u : 0u);
+            } else {
+              // one fresh slot per 32-K chunk: each chunk's partial is scaled on readback
+#pragma unroll
+              for (int c = 0; c < 4; ++c) mma(cols + c * NB, sdesc(abase + c * 32), sdesc(bbase + c * 32), id, 0u);
+            }
+            commit(smem_addr(&sm.gfull[q]));
+          }
+        }
+      }
+      // every MMA issued by this thread has completed once `drain` fires
+      commit(smem_addr(&sm.drain));
+      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
+    }
+  } else {
+    // ── readback + epilogue (warps 0-3) ──
+    const int r = tid;  // weight row of the item = TMEM lane
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const Item it = item_of(a, item, n_sh);
+      const int fmt = item_fmt(it);
+      const WeightSet& ws = it.shared ? a.shared : a.routed;
+      const int pm = tc_pass_max(fmt);
+      const bool nv = fmt == FMT_NVFP4;
+      float ts = 1.f;
+      if (nv && ws.ts != nullptr) {
+        const float* tsp = ws.ts + (it.shared ? 0 : (size_t)it.expert * ws.ts_stride);
+        ts = (w13 && r >= 64) ? tsp[1] : tsp[0];
+      }
+      bool stop = false;
+      for (int pb = 0; pb < it.cnt; pb += pm) {
+        const int pc = min(pm, it.cnt - pb);
+        const int ncol = nv ? 2 * pc : pc;     // used columns of each chunk slot
+        const bool narrow = ncol <= 4;
+        // the pass's tokens: lane t holds token t's output row and routing weight (epilogue)
+        int my_orow = 0;
+        float my_wgt = 1.f;
+        if (lane < pc) {
+          const int i = pb + lane;
+          if (it.shared) {
+            my_orow = a.mode == MODE_DENSE ? i : P + i;
+          } else {
+            const int qp = it.base + i;
+            const int tok = a.pair_tok[qp], slot = a.pair_slot[qp];
+            if (w13) {
+              my_orow = qp;
+              my_wgt = a.topk_w[(size_t)tok * a.topk + slot];
+            } else {
+              my_orow = tok * a.topk + slot;
+            }
+          }
+        }
+        float acc[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+        for (int j = 0; j < nst; ++j, ++g) {
+          const uint32_t s = g % ST, q = g % SA;
+          if (ok) ok = wait(sm, err, smem_addr(&sm.gfull[q]), (g / SA) & 1u);
+          if (!ok) continue;
+          fence_after();
+          const uint32_t taddr = tbase + ((uint32_t)(warp * 32) << 16) + q * GCOLS;
+          float blk[16];
+          if (fmt == FMT_FP8) {
+            uint32_t d[16];
+            if (narrow) {
+              ld4(taddr, d);
+            } else {
+              ld16(taddr, d);
+            }
+            ld_wait();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+            const float* sw = reinterpret_cast<const float*>(sm.scl[s]);
+            const float wsc = w13 ? sw[r >= 64 ? 1 : 0] : sw[0];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) blk[t] = (narrow && t >= 4) ? 0.f : __uint_as_float(d[t]) * wsc;
+          } else {
+            float sc[8];
+            if (nv) {
+              const uint2 sv = *reinterpret_cast<const uint2*>(sm.scl[s] + r * 8);
+              uint32_t h01, h23, h45, h67;
+              e4m3x4_to_f16x2x2(sv.x, h01, h23);
+              e4m3x4_to_f16x2x2(sv.y, h45, h67);
+              const float2 f01 = __half22float2(*reinterpret_cast<__half2*>(&h01));
+              const float2 f23 = __half22float2(*reinterpret_cast<__half2*>(&h23));
+              const float2 f45 = __half22float2(*reinterpret_cast<__half2*>(&h45));
+              const float2 f67 = __half22float2(*reinterpret_cast<__half2*>(&h67));
+              sc[0] = f01.x; sc[1] = f01.y; sc[2] = f23.x; sc[3] = f23.y;
+              sc[4] = f45.x; sc[5] = f45.y; sc[6] = f67.x; sc[7] = f67.y;
+            } else {
+              const uint32_t sv = *reinterpret_cast<const uint32_t*>(sm.scl[s] + r * 4);
+#pragma unroll
+              for (int c = 0; c < 4; ++c) sc[c] = e8m0_to_f32(sv >> (8 * c));
+#pragma unroll
+              for (int c = 4; c < 8; ++c) sc[c] = 0.f;
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t) blk[t] = 0.f;
+            if (narrow) {
+              // columns 0-3 of the 4 chunk slots
+              uint32_t d[16];
+#pragma unroll
+              for (int c = 0; c < 4; ++c) ld4(taddr + c * NB, d + 4 * c);
+              ld_wait();
+              fence_before();
+              __syncwarp();
+              if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+              if (nv) {
+                // column 2t: first 16 K of each chunk (group 2c), column 2t+1: second (group 2c+1)
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                  float v = 0.f;
+#pragma unroll
+                  for (int c = 0; c < 4; ++c) {
+                    v = fmaf(__uint_as_float(d[4 * c + 2 * t]), sc[2 * c], v);
+                    v = fmaf(__uint_as_float(d[4 * c + 2 * t + 1]), sc[2 * c + 1], v);
+                  }
+                  blk[t] = v;
+                }
+              } else {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  float v = 0.f;
+#pragma unroll
+                  for (int c = 0; c < 4; ++c) v = fmaf(__uint_as_float(d[4 * c + t]), sc[c], v);
+                  blk[t] = v;
+                }
+              }
+            } else {
+              // two chunk slots (32 columns) per TMEM load round
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                uint32_t da[16], db[16];
+                ld16(taddr + (2 * half) * NB, da);
+                ld16(taddr + (2 * half + 1) * NB, db);
+                ld_wait();
+                const int c0 = 2 * half, c1 = 2 * half + 1;
+                if (nv) {
+#pragma unroll
+                  for (int t = 0; t < 8; ++t) {
+                    float v = fmaf(__uint_as_float(da[2 * t]), sc[2 * c0], blk[t]);
+                    v = fmaf(__uint_as_float(da[2 * t + 1]), sc[2 * c0 + 1], v);
+                    v = fmaf(__uint_as_float(db[2 * t]), sc[2 * c1], v);
+                    blk[t] = fmaf(__uint_as_float(db[2 * t + 1]), sc[2 * c1 + 1], v);
+                  }
+                } else {
+#pragma unroll
+                  for (int t = 0; t < 16; ++t) {
+                    float v = fmaf(__uint_as_float(da[t]), sc[c0], blk[t]);
+                    blk[t] = fmaf(__uint_as_float(db[t]), sc[c1], v);
+                  }
+                }
+              }
+              fence_before();
+              __syncwarp();
+              if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+            }
+          }
+          // activation scale of each B row (NVFP4: token t's rows 2t / 2t+1 share it)
+#pragma unroll
+          for (int t = 0; t < 16; ++t) acc[t] = fmaf(blk[t], sm.asc[s][nv ? (2 * t) & (NB - 1) : t], acc[t]);
+          __syncwarp();
+          if (lane == 0) arrive(smem_addr(&sm.sempty[s]));
+        }
+        // one decision for all workers: the W13 epilogue below synchronises them
+        if (workers_any(!ok || aborted(sm))) {
+          stop = true;
+          break;
+        }
+        if (w13) {
+          // rows r < 64 are w1 (gate) rows, r >= 64 the matching w3 (up) rows
+          const int I = a.n_rows / 2;
+          if (r >= 64) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) sm.xchg[r - 64][t] = bf16_round(acc[t] * ts);
+          }
+          asm volatile("bar.sync 1, 128;\n" ::: "memory");
+          if (r < 64) {
+            const float lim = a.swiglu_limit;
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              if (t < pc) {
+                const int orow = __shfl_sync(0xffffffffu, my_orow, t);
+                const float wgt = __shfl_sync(0xffffffffu, my_wgt, t);
+                float gv = bf16_round(acc[t] * ts);
+                float uv = sm.xchg[r][t];
+                if (lim > 0.f) {
+                  uv = fminf(fmaxf(uv, -lim), lim);
+                  gv = fminf(gv, lim);
+                }
+                float h = silu(gv) * uv;
+                if (!it.shared) h = wgt * h;
+                a.hbf[(size_t)orow * I + it.rb * 64 + r] = __float2bfloat16_rn(h);
+              }
+            }
+          }
+          asm volatile("bar.sync 1, 128;\n" ::: "memory");   // xchg is rewritten by the next pass
+        } else {
+          const int n0 = it.rb * 128;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            if (t < pc) {
+              const int orow = __shfl_sync(0xffffffffu, my_orow, t);
+              a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(acc[t] * ts);
+            }
+          }
+        }
+      }
+      if (stop) break;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == MMA_WARP)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(TMEM_COLS));
+}
+
+// ── B panels: the activation operand of every pass, one 2 KB swizzled tile per (pass, stage) ──
+// CTA (stage j, slot): slot 0 is the shared expert / dense matrix when present, then active slots.
+// Thread (row = tid / 8, chunk c = tid % 8) writes the 16-byte chunk c of B row `row`.
+// W13 / DENSE: the e4m3 row slice and its scale are copied. W2: the bf16 h row slice is quantised
+// to e4m3 with one scale per 128 K (act_quant, kernel.py:40-125): amax over the 8 threads of the
+// row, scale = amax/448 (or its power-of-two ceiling), q = e4m3(v / scale).
+__global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
+  const int j = blockIdx.x;
+  const int slot = blockIdx.y;
+  const int K = a.k, nst = K / 128, nkb = K / 128;
+  const int P = a.m * a.topk;
+  int shared, cnt, base, pass0, nv;
+  if (slot < a.has_shared) {
+    shared = 1;
+    cnt = a.m;
+    base = 0;
+    pass0 = 0;
+    nv = a.nv_shared;
+  } else {
+    const int s = slot - a.has_shared;
+    if (s >= *a.n_active) return;
+    const int e = a.active[s];
+    shared = 0;
+    cnt = a.counts[e];
+    base = a.offsets[e];
+    pass0 = a.n_sh_pass + a.pass_off[s];
+    nv = a.nv_routed;
+  }
+  const int pm = nv ? 8 : 16;
+  const int row = threadIdx.x >> 3, c = threadIdx.x & 7;
+  const int tslot = nv ? row >> 1 : row;
+  const bool keep = nv ? ((c & 1) == (row & 1)) : true;
+  for (int pb = 0, pi = 0; pb < cnt; pb += pm, ++pi) {
+    const int i = pb + tslot;
+    const bool valid = tslot < pm && i < cnt;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    float sc = 0.f;
+    if (a.mode != MODE_W2) {
+      if (valid) {
+        const int srow = (shared || a.pair_tok == nullptr) ? i : a.pair_tok[base + i];
+        v = *reinterpret_cast<const uint4*>(a.xq + (size_t)srow * K + (size_t)j * 128 + c * 16);
+        sc = a.xs[(size_t)srow * nkb + j];
+      }
+    } else {
+      float f[16];
+      float am = 0.f;
+      if (valid) {
+        const int srow = shared ? P + i : base + i;
+        const uint4* hp = reinterpret_cast<const uint4*>(a.hbf + (size_t)srow * K + (size_t)j * 128 + c * 16);
+        const uint4 h0 = hp[0], h1 = hp[1];
+        const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&h0);
+        const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&h1);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 x0 = __bfloat1622float2(p0[e]), x1 = __bfloat1622float2(p1[e]);
+          f[2 * e] = x0.x;
+          f[2 * e + 1] = x0.y;
+          f[8 + 2 * e] = x1.x;
+          f[8 + 2 * e + 1] = x1.y;
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(f[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) f[e] = 0.f;
+      }
+      // the 8 threads of a row are 8 consecutive lanes
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+      if (valid) {
+        sc = act_scale(am, a.act_pow2 != 0);
+        uint8_t qb[16];
+        if (a.act_pow2) {
+          const float inv = __frcp_rn(sc);   // exact: sc is a power of two
+#pragma unroll
+          for (int e = 0; e < 16; ++e) qb[e] = act_q_pow2(f[e], inv);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) qb[e] = act_q(f[e], sc);
+        }
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = (uint32_t)qb[4 * e] | ((uint32_t)qb[4 * e + 1] << 8) | ((uint32_t)qb[4 * e + 2] << 16) |
+                 ((uint32_t)qb[4 * e + 3] << 24);
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    if (!keep) v = make_uint4(0u, 0u, 0u, 0u);
+    const size_t tile = (size_t)(pass0 + pi) * nst + j;
+    *reinterpret_cast<uint4*>(a.bpanel + tile * B_BYTES + row * 128 + ((c ^ (row & 7)) << 4)) = v;
+    if (c == 0) a.apanel[tile * NB + row] = valid ? sc : 0.f;
+  }
+}
+
+// ── host side ───────────────────────────────────────────────────────────────────────────────────
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Weight tiles of a TC-tiled bank as a 2-D tensor [rows][128 K]: fp4 as 16U4_ALIGN16B (64 B of
+// packed values per row in memory, 128 B per row in shared memory), FP8 as bytes. A box is one
+// stage: 128 rows x 128 K, swizzled 128 B.
+static cudaError_t make_map(CUtensorMap* map, const void* base, int fmt, uint64_t rows) {
+  memset(map, 0, sizeof *map);
+  if (base == nullptr || rows == 0) return cudaSuccess;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (enc == nullptr) return cudaErrorNotSupported;
+  const bool fp8 = fmt == FMT_FP8;
+  const cuuint64_t dims[2] = {128, rows};
+  const cuuint64_t strides[1] = {fp8 ? 128u : 64u};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = enc(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2,
+                         const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int F>
+static cudaError_t launch_tc_one(const TcArgs& a, int grid, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  tc_grouped_kernel<F><<<grid, NTHREADS, SMEM_BYTES, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+
+cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st) {
+  if (max_slots < 1) return cudaSuccess;
+  dim3 grid(a.k / 128, max_slots);
+  tc::panel_kernel<<<grid, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tc_grouped(const GroupedArgs& g, const TcPlan& plan, int max_items, cudaStream_t st) {
+  tc::TcArgs a;
+  a.g = g;
+  a.plan = plan;
+  const uint64_t nst = (uint64_t)g.k / 128, nrb = (uint64_t)g.n_rows / 128;
+  cudaError_t e = tc::make_map(&a.map_routed, g.mode == MODE_DENSE ? nullptr : g.routed.w, g.routed.fmt,
+                               (uint64_t)g.n_experts * nrb * nst * 128);
+  if (e != cudaSuccess) return e;
+  e = tc::make_map(&a.map_shared, g.has_shared ? g.shared.w : nullptr, g.mode == MODE_DENSE ? g.shared.fmt : FMT_FP8,
+                   nrb * nst * 128);
+  if (e != cudaSuccess) return e;
+  int grid = 2 * num_sms();  // 2 CTAs per SM: ~100 KB shared memory and 256 TMEM columns each
+  if (grid > max_items) grid = max_items;
+  if (grid < 1) grid = 1;
+  switch (g.routed.fmt) {
+    case FMT_NVFP4: return tc::launch_tc_one<FMT_NVFP4>(a, grid, st);
+    case FMT_MXFP4: return tc::launch_tc_one<FMT_MXFP4>(a, grid, st);
+    default: return tc::launch_tc_one<FMT_FP8>(a, grid, st);
+  }
+}
+
+// ── TC layout: canonical -> [N/128 row-blocks][K/128 stages][...] ─────────────────────────────────
+// fp4 values   [128 rows][64 B]                  (128 K packed, low nibble first)
+// FP8 values   [128 rows][128 B]
+// NVFP4 scales [128 rows][8 B]                   (the row's 8 group scales of the stage)
+// MXFP4 scales [128 rows][4 B]
+// FP8 scales   [4] fp32: block scale of rows 0-63, of rows 64-127, 2 zero pads (16-byte copies)
+// W13 row-blocks hold 64 w1 rows then the same 64 w3 rows (rb covers intermediate 64*rb..+63).
+__device__ __forceinline__ int64_t tc_row(int kind, int64_t n, int64_t rb, int r) {
+  if (kind == 1) return r < 64 ? 64 * rb + r : n / 2 + 64 * rb + (r - 64);
+  return 128 * rb + r;
+}
+
+__global__ void tc_tile_values_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int fmt, int kind,
+                                      int64_t n_mat, int64_t n, int64_t k) {
+  const int64_t nrb = n / 128, nst = k / 128;
+  const int rowb = fmt == FMT_FP8 ? 128 : 64;   // bytes of a row per stage
+  const int64_t pieces = rowb / 16;             // 16-byte pieces per row per stage
+  const int64_t units = n_mat * nrb * nst * 128 * pieces;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = u % pieces;
+    const int64_t rest = u / pieces;
+    const int r = (int)(rest & 127);
+    const int64_t j = (rest >> 7) % nst;
+    const int64_t rb = ((rest >> 7) / nst) % nrb;
+    const int64_t mat = ((rest >> 7) / nst) / nrb;
+    const int64_t src_row = mat * n + tc_row(kind, n, rb, r);
+    const uint8_t* s = src + src_row * (k * rowb / 128) + j * rowb + c * 16;
+    uint8_t* d = dst + u * 16;
+    *reinterpret_cast<uint4*>(d) = *reinterpret_cast<const uint4*>(s);
+  }
+}
+
+__global__ void tc_tile_scales_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int fmt, int kind,
+                                      int64_t n_mat, int64_t n, int64_t k) {
+  const int64_t nrb = n / 128, nst = k / 128;
+  if (fmt == FMT_FP8) {
+    const float* s = reinterpret_cast<const float*>(src);
+    float* d = reinterpret_cast<float*>(dst);
+    const int64_t nsrb = (n + 127) / 128, nkb = k / 128;
+    const int64_t units = n_mat * nrb * nst;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t j = u % nst, rb = (u / nst) % nrb, mat = (u / nst) / nrb;
+      const float* m = s + mat * nsrb * nkb;
+      d[4 * u] = m[(tc_row(kind, n, rb, 0) / 128) * nkb + j];
+      d[4 * u + 1] = m[(tc_row(kind, n, rb, 64) / 128) * nkb + j];
+      d[4 * u + 2] = 0.f;
+      d[4 * u + 3] = 0.f;
+    }
+  } else {
+    const int per = fmt == FMT_NVFP4 ? 8 : 4;           // scale bytes per row per stage
+    const int64_t rowb = fmt == FMT_NVFP4 ? k / 16 : k / 32;
+    const int64_t units = n_mat * nrb * nst * 128;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+      const int r = (int)(u & 127);
+      const int64_t j = (u >> 7) % nst, rb = ((u >> 7) / nst) % nrb, mat = ((u >> 7) / nst) / nrb;
+      const uint8_t* s = src + (mat * n + tc_row(kind, n, rb, r)) * rowb + j * per;
+      uint8_t* d = dst + u * per;
+      for (int i = 0; i < per; ++i) d[i] = s[i];
+    }
+  }
+}
+
+cudaError_t launch_tc_tile(int fmt, int kind, bool scales, const void* src, void* dst, int64_t n_mat, int64_t n,
+                           int64_t k, cudaStream_t st) {
+  const int64_t units = n_mat * (n / 128) * (k / 128) * 1024;
+  int64_t b = (units + 255) / 256;
+  const int grid = (int)(b < 1 ? 1 : (b > 262144 ? 262144 : b));
+  if (scales)
+    tc_tile_scales_kernel<<<grid, 256, 0, st>>>((const uint8_t*)src, (uint8_t*)dst, fmt, kind, n_mat, n, k);
+  else
+    tc_tile_values_kernel<<<grid, 256, 0, st>>>((const uint8_t*)src, (uint8_t*)dst, fmt, kind, n_mat, n, k);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

@@ -26,17 +26,24 @@ from ._lib import SbMoeLayer, check, lib, ptr, stream_ptr
 
 _SCORE = _lib.SCORE
 
+# The weight layout new layers use: LAYOUT_TC (tcgen05 kernels) or LAYOUT_FRAGMENT (mma.sync kernels).
+DEFAULT_LAYOUT = _lib.LAYOUT_TC
+
 
 def _u8(t):
     return t.contiguous().view(torch.uint8)
 
 
-def tile(fmt: int, kind: int, w: torch.Tensor, s: torch.Tensor, n_mat: int, n: int, k: int):
+def tile(fmt: int, kind: int, w: torch.Tensor, s: torch.Tensor, n_mat: int, n: int, k: int,
+         layout: int = None):
     """Canonical [n_mat, N, K] weights (+ scales) on the device -> tiled (values, scales)."""
     L = lib()
+    layout = DEFAULT_LAYOUT if layout is None else layout
+    if layout == _lib.LAYOUT_TC:
+        kind |= _lib.KIND_TC
     dev = w.device
     wt = torch.empty(n_mat * L.sb_tiled_bytes(fmt, n, k), dtype=torch.uint8, device=dev)
-    st = torch.empty(n_mat * L.sb_tiled_scale_bytes(fmt, n, k), dtype=torch.uint8, device=dev)
+    st = torch.empty(n_mat * L.sb_tiled_scale_bytes(fmt, kind, n, k), dtype=torch.uint8, device=dev)
     sp = stream_ptr()
     check(L.sb_tile_weights(fmt, kind, ptr(_u8(w)), ptr(wt), n_mat, n, k, sp), "sb_tile_weights")
     src_s = s.contiguous().float() if fmt == F.FMT_FP8 else _u8(s)
@@ -57,8 +64,9 @@ class MoELayer:
 
     def __init__(self, *, hidden, inter, n_experts, topk, expert_fmt, gate_w, gate_bias=None, tid2eid=None,
                  score_func="sigmoid", route_scale=1.0, swiglu_limit=0.0, act_pow2=True,
-                 w13, w13_s, w13_ts=None, w2, w2_s, w2_ts=None, shared=None, tiled=False):
+                 w13, w13_s, w13_ts=None, w2, w2_s, w2_ts=None, shared=None, tiled=False, layout=None):
         self.hidden, self.inter, self.n_experts, self.topk = hidden, inter, n_experts, topk
+        self.layout = DEFAULT_LAYOUT if layout is None else layout
         self.expert_fmt = expert_fmt
         self.device = gate_w.device
         self.gate_w = gate_w.contiguous().to(torch.bfloat16)
@@ -68,8 +76,8 @@ class MoELayer:
         if tiled:
             self.w13, self.w13_s, self.w2, self.w2_s = w13, w13_s, w2, w2_s
         else:
-            self.w13, self.w13_s = tile(expert_fmt, _lib.MAT_W13, w13, w13_s, e, 2 * i, h)
-            self.w2, self.w2_s = tile(expert_fmt, _lib.MAT_PLAIN, w2, w2_s, e, h, i)
+            self.w13, self.w13_s = tile(expert_fmt, _lib.MAT_W13, w13, w13_s, e, 2 * i, h, self.layout)
+            self.w2, self.w2_s = tile(expert_fmt, _lib.MAT_PLAIN, w2, w2_s, e, h, i, self.layout)
         self.w13_ts = None if w13_ts is None else w13_ts.contiguous().float()
         self.w2_ts = None if w2_ts is None else w2_ts.contiguous().float()
         self.shared = None
@@ -78,8 +86,8 @@ class MoELayer:
                 self.shared = shared
             else:
                 s13, s13s, s2, s2s = shared
-                a, b = tile(F.FMT_FP8, _lib.MAT_W13, s13, s13s, 1, 2 * i, h)
-                c, d = tile(F.FMT_FP8, _lib.MAT_PLAIN, s2, s2s, 1, h, i)
+                a, b = tile(F.FMT_FP8, _lib.MAT_W13, s13, s13s, 1, 2 * i, h, self.layout)
+                c, d = tile(F.FMT_FP8, _lib.MAT_PLAIN, s2, s2s, 1, h, i, self.layout)
                 self.shared = (a, b, c, d)
         self.desc = SbMoeLayer()
         d = self.desc
@@ -98,6 +106,7 @@ class MoELayer:
         d.w2, d.w2_s, d.w2_ts = ptr(self.w2), ptr(self.w2_s), ptr(self.w2_ts)
         if self.shared is not None:
             d.sh_w13, d.sh_w13_s, d.sh_w2, d.sh_w2_s = (ptr(t) for t in self.shared)
+        d.layout = self.layout
         self._ws = None
         self.score_func, self.route_scale, self.swiglu_limit, self.act_pow2 = score_func, route_scale, swiglu_limit, act_pow2
 

@@ -40,8 +40,8 @@ def act_quant(x: torch.Tensor, block_size: int = 128, scale_fmt=None, scale_dtyp
     return y, s
 
 
-def _tiled(fmt, b, b_s):
-    key = (fmt, b.data_ptr(), b_s.data_ptr(), tuple(b.shape), b._version)
+def _tiled(fmt, b, b_s, layout):
+    key = (fmt, layout, b.data_ptr(), b_s.data_ptr(), tuple(b.shape), b._version)
     t = _TILED.get(key)
     if t is None:
         from .moe import tile
@@ -51,7 +51,7 @@ def _tiled(fmt, b, b_s):
             s = F.e8m0_decode(b_s.view(torch.uint8)) if b_s.dtype == torch.float8_e8m0fnu else b_s.float()
         else:
             s = b_s.view(torch.uint8)
-        t = _TILED[key] = tile(fmt, _lib.MAT_PLAIN, b.view(torch.uint8), s, 1, n, k)
+        t = _TILED[key] = tile(fmt, _lib.MAT_PLAIN, b.view(torch.uint8), s, 1, n, k, layout)
     return t
 
 
@@ -59,20 +59,25 @@ def _act_scales_f32(a_s):
     return F.e8m0_decode(a_s.view(torch.uint8)) if a_s.dtype == torch.float8_e8m0fnu else a_s.float()
 
 
-def quantised_gemm(fmt: int, w, w_s, tensor_scale, a, a_s):
+def quantised_gemm(fmt: int, w, w_s, tensor_scale, a, a_s, layout=None):
     """y bf16 [M, N] = dequant(a, a_s) @ dequant(w, w_s, tensor_scale)^T, canonical weights."""
+    from .moe import DEFAULT_LAYOUT
+    layout = DEFAULT_LAYOUT if layout is None else layout
     assert a.is_contiguous() and w.is_contiguous(), "Input tensors must be contiguous"
     k = a.size(-1)
     m = a.numel() // k
     n = w.size(0)
-    wt, st = _tiled(fmt, w, w_s)
+    wt, st = _tiled(fmt, w, w_s, layout)
     ts = None
     if fmt == F.FMT_NVFP4:
         ts = torch.tensor([float(tensor_scale)], dtype=torch.float32, device=a.device)
     sa = _act_scales_f32(a_s).contiguous()
     y = torch.empty(*a.shape[:-1], n, dtype=torch.bfloat16, device=a.device)
-    check(lib().sb_qgemm(fmt, ptr(wt), ptr(st), ptr(ts), n, k, ptr(a.view(torch.uint8)), ptr(sa), m, ptr(y),
-                         stream_ptr()), "sb_qgemm")
+    L = lib()
+    wsb = L.sb_qgemm_workspace_bytes(fmt, layout, n, k, m)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=a.device) if wsb else None
+    check(L.sb_qgemm(fmt, layout, ptr(wt), ptr(st), ptr(ts), n, k, ptr(a.view(torch.uint8)), ptr(sa), m,
+                     ptr(y), ptr(ws), wsb, stream_ptr()), "sb_qgemm")
     return y
 
 

@@ -196,7 +196,8 @@ def _normal_expert_on_device(cfg, layer, expert, fmt, device):
                          p2, s2, torch.tensor([t2], dtype=torch.float32, device=device))
 
 
-def device_layer(cfg: MoEConfig, layer: int = 0, device="cuda", seeded=None, fill="random", act_pow2=True):
+def device_layer(cfg: MoEConfig, layer: int = 0, device="cuda", seeded=None, fill="random", act_pow2=True,
+                 layout=None):
     """A MoELayer on `device` for config `cfg`.
 
     seeded: expert ids generated from their CPU-seeded draws (the bytes the oracle and the golden
@@ -253,6 +254,6 @@ def device_layer(cfg: MoEConfig, layer: int = 0, device="cuda", seeded=None, fil
                    gate_bias=gb.to(device), score_func=cfg.score_func, route_scale=cfg.route_scale,
                    swiglu_limit=cfg.swiglu_limit, act_pow2=act_pow2, w13=w13, w13_s=w13_s,
                    w13_ts=w13_ts if fmt == F.FMT_NVFP4 else None, w2=w2, w2_s=w2_s,
-                   w2_ts=w2_ts if fmt == F.FMT_NVFP4 else None, shared=shared)
+                   w2_ts=w2_ts if fmt == F.FMT_NVFP4 else None, shared=shared, layout=layout)
     del w13, w13_s, w2, w2_s
     return lay

@@ -58,9 +58,13 @@ def test_act_quant_is_bit_exact(m, k, pow2):
     assert np.array_equal(O.E4M3[q.view(torch.uint8).cpu().numpy()], O.E4M3[qo])
 
 
+LAYOUTS = [1, 0]   # tensor-core (tcgen05) layout, mma.sync fragment layout
+
+
+@pytest.mark.parametrize("layout", LAYOUTS)
 @pytest.mark.parametrize("fmt", [F.FMT_NVFP4, F.FMT_MXFP4, F.FMT_FP8])
 @pytest.mark.parametrize("m,n,k", [(1, 256, 512), (5, 4096, 2048), (37, 512, 4096), (8, 7168, 2048)])
-def test_quantised_gemm_matches_oracle(fmt, m, n, k):
+def test_quantised_gemm_matches_oracle(fmt, m, n, k, layout):
     """The kernel-level seam: fp4_gemm / fp8_gemm (kernel.py:257-273, 518-536)."""
     from shard_b200 import ops
     g = torch.Generator().manual_seed(n + k + fmt)
@@ -78,25 +82,26 @@ def test_quantised_gemm_matches_oracle(fmt, m, n, k):
         ts = 1.0
         wdq = O.dequant_weight(O.FMT_FP8, p.numpy(), s.numpy())
     qx, sx = ops.act_quant(x.cuda(), 128, "ue8m0")
-    y = ops.quantised_gemm(fmt, p.cuda(), s.cuda(), ts, qx, sx)
+    y = ops.quantised_gemm(fmt, p.cuda(), s.cuda(), ts, qx, sx, layout=layout)
     ref = O.qlinear(x.float().numpy(), wdq, True)
     assert O.max_rel_err(_np(y), ref) < TOL
     # and nearly every element is the same bf16 word
     assert (_np(y) != ref).mean() < 0.02
 
 
-def _golden_layer(name):
+def _golden_layer(name, layout=None):
     g = load_golden(name)
     cfg, m, xs, sfmt = case_config(name)
     seeded = None if cfg.n_experts <= 32 else sorted(set(g["indices"].ravel().tolist()))
-    lay = S.device_layer(cfg, 0, "cuda", seeded=seeded, act_pow2=sfmt is not None)
+    lay = S.device_layer(cfg, 0, "cuda", seeded=seeded, act_pow2=sfmt is not None, layout=layout)
     x, ids = case_inputs(cfg, m, xs)
     return g, cfg, lay, x, ids, sfmt
 
 
+@pytest.mark.parametrize("layout", LAYOUTS)
 @pytest.mark.parametrize("name", list(CASES))
-def test_forward_matches_reference_golden(name):
-    g, cfg, lay, x, ids, sfmt = _golden_layer(name)
+def test_forward_matches_reference_golden(name, layout):
+    g, cfg, lay, x, ids, sfmt = _golden_layer(name, layout)
     y, w, idx = lay.forward(x.cuda(), ids.cuda(), routing=True)
     torch.cuda.synchronize()
     assert np.array_equal(idx.cpu().numpy(), g["indices"]), "router top-k indices must be bit-exact"
@@ -115,9 +120,10 @@ def test_forward_matches_oracle(name):
     assert O.max_rel_err(_np(y), yo) < TOL
 
 
+@pytest.mark.parametrize("layout", LAYOUTS)
 @pytest.mark.parametrize("cname,m", [("c1", 1), ("c1", 8), ("c1", 32), ("c1", 64), ("c3", 16), ("c3", 64),
                                      ("c4", 256)])
-def test_full_size_forward(cname, m):
+def test_full_size_forward(cname, m, layout):
     """Full BASELINE shapes. The oracle checks a sample of tokens (its cost grows with the experts
     they route to); the whole batch is checked for row invariance: every token's output equals the
     same token run alone, bit for bit."""
@@ -127,7 +133,7 @@ def test_full_size_forward(cname, m):
     _, idx_o, _ = O.gate(x.float().numpy(), gw.float().numpy(), gb.numpy(), cfg.score_func, cfg.route_scale, cfg.topk)
     sample = sorted(set([0, m // 2, m - 1]))[:3]
     seeded = sorted(set(idx_o[sample].ravel().tolist()))
-    lay = S.device_layer(cfg, 0, "cuda", seeded=seeded)
+    lay = S.device_layer(cfg, 0, "cuda", seeded=seeded, layout=layout)
     y, w, idx = lay.forward(x.cuda(), ids.cuda(), routing=True)
     assert np.array_equal(idx.cpu().numpy(), idx_o), "router top-k indices must be bit-exact"
     sl = SeededLayer(cfg)
