@@ -123,6 +123,21 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
              const void* q, const float* s, int64_t m, void* y, void* workspace, size_t workspace_bytes,
              void* stream);
 
+/* sb_qgemm over the tensor-core layout (SB_LAYOUT_TC weights, n % 128 == 0) for callers that cannot
+ * allocate device memory: it allocates nothing and takes no workspace. No counterpart in the
+ * reference (its fp8_gemm / fp4_gemm allocate through torch).
+ * Its scratch is a file-scope device region of SB_QGEMM_STATIC_SCRATCH_BYTES per device: the
+ * error flag (cleared by every call before its kernels run) and the activation panel of
+ * ceil(m / p) passes x k/128 stages, 2112 bytes each (p = 8 for NVFP4, 16 otherwise). Shapes that
+ * need more return SB_ERR_SHAPE with the byte count (at k = 7168: m <= 272, or m <= 136 for NVFP4).
+ * The first call on a device looks up the region's address (cudaGetSymbolAddress, with that device
+ * current); make that first call before any stream capture. Every call on a device uses the same
+ * region: calls that overlap in time (other streams, other threads) race on it and must be
+ * serialised by the caller. */
+#define SB_QGEMM_STATIC_SCRATCH_BYTES (2u << 20)
+int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
+                    const void* q, const float* s, int64_t m, void* y, void* stream);
+
 /* ── the MoE stage forward (MoE.forward, model.py:634-649; Gate.forward :569-589;
  *    Expert.forward :601-611; grouped decode v4_moe_grouped.py:634-709) ──────────────────────── */
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m);

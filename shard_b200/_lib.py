@@ -53,6 +53,7 @@ SIGNATURES = {
     "sb_act_quant": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _vp]),
     "sb_qgemm_workspace_bytes": (_sz, [_int, _int, _i64, _i64, _i64]),
     "sb_qgemm": (_int, [_int, _int, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _sz, _vp]),
+    "sb_qgemm_static": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "sb_moe_workspace_bytes": (_sz, [ctypes.POINTER(SbMoeLayer), _i64]),
     "sb_moe_forward": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sb_moe_forward_profiled": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp,

@@ -6,6 +6,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 
 #include "../../include/shard_b200.h"
@@ -303,6 +304,109 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
   }
   a.items_per_expert = (int)((n + 255) / 256);
   return cuda_check(sb::launch_grouped(a, a.items_per_expert, 0, (cudaStream_t)stream), "qgemm");
+}
+
+}  // extern "C"
+
+// Scratch of sb_qgemm_static: one file-scope region per device, shared by every call on that device.
+// Bytes [0, 4) are the error flag (must be 0 when the kernels start: each call clears it first);
+// then the activation panel (B tiles, then their row scales), rewritten in full by every call.
+static __device__ __align__(256) uint8_t g_qgemm_static_scratch[SB_QGEMM_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kStaticMaxDevices];
+
+// Device address of this device's static scratch, looked up once per device (with the device
+// current) by the first call on it.
+int static_scratch(void** out) {
+  int dev = 0;
+  int rc = cuda_check(cudaGetDevice(&dev), "qgemm_static: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= kStaticMaxDevices) return fail(SB_ERR_UNSUPPORTED, "qgemm_static: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    rc = cuda_check(cudaGetSymbolAddress(&p, g_qgemm_static_scratch), "qgemm_static: cudaGetSymbolAddress");
+    if (rc) return rc;
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return SB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k, const void* q,
+                    const float* s, int64_t m, void* y, void* stream) {
+  if (!w || !w_s || !q || !s || !y) return fail(SB_ERR_ARG, "qgemm_static: NULL pointer");
+  if (fmt != SB_FMT_NVFP4 && fmt != SB_FMT_MXFP4 && fmt != SB_FMT_FP8)
+    return fail(SB_ERR_FORMAT, "qgemm_static: format %d", fmt);
+  if (fmt == SB_FMT_NVFP4 && !ts) return fail(SB_ERR_ARG, "qgemm_static: NVFP4 needs a tensor scale");
+  if (n < 128 || n % 128 || k < 128 || k % 128 || m < 0 || m > (1 << 24))
+    return fail(SB_ERR_SHAPE, "qgemm_static: need n %% 128 == 0, k %% 128 == 0 (n=%lld k=%lld m=%lld)",
+                (long long)n, (long long)k, (long long)m);
+  if (!aligned16(w) || !aligned16(q)) return fail(SB_ERR_ARG, "qgemm_static: weights and activations must be 16-byte aligned");
+  const size_t need = qgemm_ws(fmt, SB_LAYOUT_TC, k, m, nullptr, nullptr, nullptr, nullptr);
+  if (need > (size_t)SB_QGEMM_STATIC_SCRATCH_BYTES)
+    return fail(SB_ERR_SHAPE,
+                "qgemm_static: m=%lld k=%lld needs %zu bytes of scratch, more than the %zu-byte static region "
+                "(use sb_qgemm with a workspace, or split m)",
+                (long long)m, (long long)k, need, (size_t)SB_QGEMM_STATIC_SCRATCH_BYTES);
+  if (m == 0) return SB_OK;
+  void* base = nullptr;
+  int rc = static_scratch(&base);
+  if (rc) return rc;
+  int* err = nullptr;
+  uint8_t* bpanel = nullptr;
+  float* apanel = nullptr;
+  qgemm_ws(fmt, SB_LAYOUT_TC, k, m, (uint8_t*)base, &err, &bpanel, &apanel);
+  cudaStream_t st = (cudaStream_t)stream;
+  rc = cuda_check(cudaMemsetAsync(err, 0, sizeof(int), st), "qgemm_static");
+  if (rc) return rc;
+  const int pm = sb::tc_pass_max(fmt);
+  sb::PanelArgs pa;
+  memset(&pa, 0, sizeof pa);
+  pa.mode = sb::MODE_DENSE;
+  pa.m = (int)m;
+  pa.topk = 1;
+  pa.k = (int)k;
+  pa.has_shared = 1;
+  pa.n_sh_pass = (int)((m + pm - 1) / pm);
+  pa.nv_shared = fmt == SB_FMT_NVFP4;
+  pa.xq = (const uint8_t*)q;
+  pa.xs = s;
+  pa.bpanel = bpanel;
+  pa.apanel = apanel;
+  rc = cuda_check(sb::launch_tc_panel(pa, 1, st), "qgemm_static panel");
+  if (rc) return rc;
+  sb::TcPlan plan;
+  plan.bpanel = bpanel;
+  plan.apanel = apanel;
+  plan.pass_off = nullptr;
+  plan.n_sh_pass = pa.n_sh_pass;
+  sb::GroupedArgs a;
+  memset(&a, 0, sizeof a);
+  a.mode = sb::MODE_DENSE;
+  a.m = (int)m;
+  a.topk = 1;
+  a.n_rows = (int)n;
+  a.k = (int)k;
+  a.has_shared = 1;
+  a.shared.w = (const uint8_t*)w;
+  a.shared.s = (const uint8_t*)w_s;
+  a.shared.ts = ts;
+  a.shared.ts_stride = 1;
+  a.shared.fmt = fmt;
+  a.routed = a.shared;
+  a.o = (__nv_bfloat16*)y;
+  a.err = err;
+  a.items_per_expert = (int)(n / 128);
+  return cuda_check(sb::launch_tc_grouped(a, plan, a.items_per_expert, st), "qgemm_static");
 }
 
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
