@@ -3,7 +3,7 @@
 // One CTA walks ITEMS = (expert or shared expert, 128-row block of a weight matrix) of the
 // device-side permutation (shared expert first); an item runs its expert's token PASSES (up to 16
 // B rows each) over the K stages (128 K per stage). Roles (192 threads):
-//   warp 4     producer: lane 0 keeps ST stages of asynchronous copies in flight. A stage is
+//   warp 4     producer: lane 0 keeps up to ST stages of asynchronous copies in flight. A stage is
 //                - the weight tile, 128 rows x 128 K, by a TMA tensor load that lands it directly
 //                  in the 128B-swizzled K-major operand form tcgen05.mma reads: fp4 weights use the
 //                  16U4_ALIGN16B element type (each 16 packed e2m1 values land in the low 8 bytes
@@ -19,8 +19,11 @@
 //              columns with tcgen05.ld, applies the weight scales and the B row scales in fp32 and
 //              accumulates; then the epilogue (W13: SwiGLU pairs rows r / r+64 -> h bf16; W2 /
 //              DENSE: bf16 rows of o).
-// The three roles run decoupled through mbarriers across item and pass boundaries: the producer
-// and the MMA issuer run ahead of the readback by up to ST stages / SA accumulator groups.
+// The three roles run decoupled through mbarriers across item and pass boundaries. An operand slot
+// (weight tile + B tile) is released by tcgen05.commit as soon as its MMAs have read it, so the
+// ring holds only copies in flight and tiles waiting for the tensor core; the small per-stage
+// scales live in a deeper side ring released by the readback. The MMA issuer runs ahead of the
+// readback by up to SA accumulator groups.
 // The tensor core sums exact products (e2m1 x e4m3 and e4m3 x e4m3 are exact in fp32).
 //
 // Every wait is bounded: on timeout the CTA records an error in *err and winds down.
@@ -35,10 +38,13 @@ namespace tc {
 constexpr int NTHREADS = 192;
 constexpr int PRODUCER_WARP = 4;
 constexpr int MMA_WARP = 5;
-constexpr int ST = 5;           // stage ring (A + B + scales)
-constexpr int SA = 4;           // accumulator groups in TMEM
+constexpr int ST = 5;           // operand ring (weight tile + B tile), released by the MMA commit
+constexpr int UNIT = 2;         // stages per unit (one accumulator group, side slot and readback)
+constexpr int SA = 2;           // accumulator groups (units) in TMEM
+constexpr int SS = 6;           // side ring (scales of a unit), released by the readback
 constexpr int NB = 16;          // MMA N (columns per chunk slot)
-constexpr int GCOLS = 4 * NB;   // TMEM columns of one accumulator group (4 chunk slots)
+constexpr int SCOLS = 4 * NB;   // TMEM columns of one stage (4 chunk slots)
+constexpr int GCOLS = UNIT * SCOLS;  // TMEM columns of one accumulator group
 constexpr int TMEM_COLS = SA * GCOLS;
 constexpr int A_BYTES = 128 * 128;
 constexpr int B_BYTES = NB * 128;
@@ -48,9 +54,9 @@ constexpr uint32_t WAIT_LIMIT = 1u << 16;  // polls; each may sleep up to ~1 us
 struct Smem {
   uint8_t A[ST][A_BYTES];       // 1024-aligned (128B swizzle atoms)
   uint8_t B[ST][B_BYTES];
-  uint8_t scl[ST][SCL_BYTES];
-  float asc[ST][NB];
-  uint64_t full[ST], sempty[ST], gfull[SA], gempty[SA];
+  uint8_t scl[SS][UNIT * SCL_BYTES];
+  float asc[SS][UNIT * NB];
+  uint64_t full[ST], aempty[ST], sfull[SS], sempty[SS], gfull[SA], gempty[SA];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -128,13 +134,25 @@ __device__ __forceinline__ void set_abort(Smem& sm, int* err, bool flag_err) {
 
 // bounded wait; on timeout flag the CTA (and the launch) and return false
 __device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t parity) {
-  if (aborted(sm)) return false;
   for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
     if ((i & 63u) == 63u && aborted(sm)) return false;
   }
   set_abort(sm, err, true);
   return false;
+}
+
+// bounded wait by a whole warp; true only if every lane saw the phase complete (reconverges the warp)
+__device__ __forceinline__ bool warp_wait(Smem& sm, int* err, uint32_t bar, uint32_t parity) {
+  const bool ok = wait(sm, err, bar, parity);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// one lane of a converged warp (the issuing lane of the producer and MMA warps)
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n selp.u32 %0, 1, 0, e;\n}\n" : "=r"(p));
+  return p != 0;
 }
 
 // OR of `pred` over the 128 worker threads, on named barrier 1 (a uniform decision for all of them)
@@ -196,6 +214,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(smem_addr(&sm.full[s]), 1);
+      mbar_init(smem_addr(&sm.aempty[s]), 1);
+    }
+    for (int s = 0; s < SS; ++s) {
+      mbar_init(smem_addr(&sm.sfull[s]), 1);
       mbar_init(smem_addr(&sm.sempty[s]), 4);
     }
     for (int q = 0; q < SA; ++q) {
@@ -228,93 +250,129 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   auto item_fmt = [&](const Item& it) { return it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R; };
   auto first_pass = [&](const Item& it) { return it.shared ? 0 : ta.plan.n_sh_pass + ta.plan.pass_off[it.slot]; };
 
+  // Stages are grouped in UNITS of up to UNIT consecutive stages of one pass: one side-ring slot
+  // (scales), one accumulator group and one readback per unit. g counts stages, u units.
   if (warp == PRODUCER_WARP) {
-    if (lane == 0) {
+    // the whole warp runs the loop (uniform control flow); one elected lane issues the copies
+    if (elect_one()) {
       prefetch_map(&ta.map_routed);
       prefetch_map(&ta.map_shared);
-      uint32_t g = 0, issued = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const Item it = item_of(a, item, n_sh);
-        const int fmt = item_fmt(it);
-        const WeightSet& ws = it.shared ? a.shared : a.routed;
-        const CUtensorMap* map = it.shared ? &ta.map_shared : &ta.map_routed;
-        const int pm = tc_pass_max(fmt);
-        const uint32_t abytes = fmt == FMT_FP8 ? 16384u : 8192u;
-        const uint32_t sb = stage_sbytes(fmt);
-        const int row0 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;
-        const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)it.rb * nst * sb;
-        const int pass0 = first_pass(it);
-        for (int pb = 0, pi = 0; pb < it.cnt && ok; pb += pm, ++pi) {
-          if (*reinterpret_cast<volatile int*>(err)) {
-            set_abort(sm, err, false);
+    }
+    __syncwarp();
+    uint32_t g = 0, u = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const Item it = item_of(a, item, n_sh);
+      const int fmt = item_fmt(it);
+      const WeightSet& ws = it.shared ? a.shared : a.routed;
+      const CUtensorMap* map = it.shared ? &ta.map_shared : &ta.map_routed;
+      const int pm = tc_pass_max(fmt);
+      const uint32_t abytes = fmt == FMT_FP8 ? 16384u : 8192u;
+      const uint32_t sb = stage_sbytes(fmt);
+      const int row0 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;
+      const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)it.rb * nst * sb;
+      const int pass0 = first_pass(it);
+      for (int pb = 0, pi = 0; pb < it.cnt && ok; pb += pm, ++pi) {
+        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(err) != 0)) {
+          set_abort(sm, err, false);
+          ok = false;
+          break;
+        }
+        const size_t pst = (size_t)(pass0 + pi) * nst;
+        for (int j = 0; j < nst && ok; j += UNIT, ++u) {
+          const int ns = min(UNIT, nst - j);
+          const uint32_t us = u % SS;
+          if (!warp_wait(sm, err, smem_addr(&sm.sempty[us]), ((u / SS) & 1u) ^ 1u)) {
             ok = false;
             break;
           }
-          const size_t pst = (size_t)(pass0 + pi) * nst;
-          for (int j = 0; j < nst; ++j, ++g) {
+          if (elect_one()) {
+            const uint32_t sbar = smem_addr(&sm.sfull[us]);
+            mbar_expect_tx(sbar, ns * (NB * 4 + sb));
+            bulk_g2s(smem_addr(sm.asc[us]), ta.plan.apanel + (pst + j) * NB, ns * NB * 4, sbar);
+            bulk_g2s(smem_addr(sm.scl[us]), sbase + (size_t)j * sb, ns * sb, sbar);
+          }
+          __syncwarp();
+          for (int t = 0; t < ns; ++t, ++g) {
             const uint32_t s = g % ST;
-            if (!wait(sm, err, smem_addr(&sm.sempty[s]), ((g / ST) & 1u) ^ 1u)) {
+            if (!warp_wait(sm, err, smem_addr(&sm.aempty[s]), ((g / ST) & 1u) ^ 1u)) {
               ok = false;
               break;
             }
-            const uint32_t bar = smem_addr(&sm.full[s]);
-            mbar_expect_tx(bar, abytes + B_BYTES + NB * 4 + sb);
-            tma_load_2d(smem_addr(sm.A[s]), map, 0, row0 + j * 128, bar);
-            bulk_g2s(smem_addr(sm.B[s]), ta.plan.bpanel + (pst + j) * B_BYTES, B_BYTES, bar);
-            bulk_g2s(smem_addr(sm.asc[s]), ta.plan.apanel + (pst + j) * NB, NB * 4, bar);
-            bulk_g2s(smem_addr(sm.scl[s]), sbase + (size_t)j * sb, sb, bar);
-            issued = g + 1;
+            if (elect_one()) {
+              const uint32_t bar = smem_addr(&sm.full[s]);
+              mbar_expect_tx(bar, abytes + B_BYTES);
+              tma_load_2d(smem_addr(sm.A[s]), map, 0, row0 + (j + t) * 128, bar);
+              bulk_g2s(smem_addr(sm.B[s]), ta.plan.bpanel + (pst + j + t) * B_BYTES, B_BYTES, bar);
+            }
+            __syncwarp();
           }
         }
       }
-      // before the CTA's shared memory is released: wait for this CTA's copies still in flight
-      // (only when a wait gave up; otherwise every stage was consumed)
-      for (uint32_t h = issued > (uint32_t)ST ? issued - ST : 0; h < issued; ++h)
-        for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-          if (mbar_try_wait(smem_addr(&sm.full[h % ST]), (h / ST) & 1u)) break;
     }
+    // before the CTA's shared memory is released: wait for copies still in flight (only when a
+    // wait gave up; otherwise every stage and unit was consumed)
+    for (uint32_t h = g > (uint32_t)ST ? g - ST : 0; h < g; ++h)
+      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait(smem_addr(&sm.full[h % ST]), (h / ST) & 1u)) break;
+    for (uint32_t h = u > (uint32_t)SS ? u - SS : 0; h < u; ++h)
+      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait(smem_addr(&sm.sfull[h % SS]), (h / SS) & 1u)) break;
   } else if (warp == MMA_WARP) {
-    if (lane == 0) {
-      uint32_t g = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const Item it = item_of(a, item, n_sh);
-        const int fmt = item_fmt(it);
-        const int pm = tc_pass_max(fmt);
-        const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
-        for (int pb = 0; pb < it.cnt && ok; pb += pm) {
-          for (int j = 0; j < nst; ++j, ++g) {
-            const uint32_t s = g % ST, q = g % SA;
-            if (!wait(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u) ||
-                !wait(sm, err, smem_addr(&sm.gempty[q]), ((g / SA) & 1u) ^ 1u)) {
+    // the whole warp runs the loop (uniform control flow); one elected lane issues MMAs and commits
+    uint32_t g = 0, u = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const Item it = item_of(a, item, n_sh);
+      const int fmt = item_fmt(it);
+      const int pm = tc_pass_max(fmt);
+      const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
+      for (int pb = 0; pb < it.cnt && ok; pb += pm) {
+        for (int j = 0; j < nst && ok; j += UNIT, ++u) {
+          const int ns = min(UNIT, nst - j);
+          const uint32_t q = u % SA;
+          if (!warp_wait(sm, err, smem_addr(&sm.gempty[q]), ((u / SA) & 1u) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < ns; ++t, ++g) {
+            const uint32_t s = g % ST;
+            if (!warp_wait(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u)) {
               ok = false;
               break;
             }
             fence_after();
             const uint32_t abase = smem_addr(sm.A[s]), bbase = smem_addr(sm.B[s]);
-            const uint32_t cols = tbase + q * GCOLS;
-            if (fmt == FMT_FP8) {
+            const uint32_t cols = tbase + q * GCOLS + t * SCOLS;
+            if (elect_one()) {
+              if (fmt == FMT_FP8) {
 #pragma unroll
-              for (int c = 0; c < 4; ++c) mma(cols, sdesc(abase + c * 32), sdesc(bbase + c * 32), id, c > 0 ? 1u : 0u);
-            } else {
-              // one fresh slot per 32-K chunk: each chunk's partial is scaled on readback
+                for (int c = 0; c < 4; ++c)
+                  mma(cols, sdesc(abase + c * 32), sdesc(bbase + c * 32), id, c > 0 ? 1u : 0u);
+              } else {
+                // one fresh slot per 32-K chunk: each chunk's partial is scaled on readback
 #pragma unroll
-              for (int c = 0; c < 4; ++c) mma(cols + c * NB, sdesc(abase + c * 32), sdesc(bbase + c * 32), id, 0u);
+                for (int c = 0; c < 4; ++c) mma(cols + c * NB, sdesc(abase + c * 32), sdesc(bbase + c * 32), id, 0u);
+              }
+              commit(smem_addr(&sm.aempty[s]));   // the operand slot is free once these MMAs have read it
             }
-            commit(smem_addr(&sm.gfull[q]));
+            __syncwarp();
           }
+          if (!ok) break;
+          if (elect_one()) commit(smem_addr(&sm.gfull[q]));
+          __syncwarp();
         }
       }
-      // every MMA issued by this thread has completed once `drain` fires
-      commit(smem_addr(&sm.drain));
-      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-        if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
     }
+    // every MMA issued by the elected lane has completed once `drain` fires
+    if (elect_one()) commit(smem_addr(&sm.drain));
+    __syncwarp();
+    for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+      if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
   } else {
     // ── readback + epilogue (warps 0-3) ──
     const int r = tid;  // weight row of the item = TMEM lane
-    uint32_t g = 0;
+    uint32_t u = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const Item it = item_of(a, item, n_sh);
@@ -322,6 +380,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pm = tc_pass_max(fmt);
       const bool nv = fmt == FMT_NVFP4;
+      const uint32_t sb = stage_sbytes(fmt);
       float ts = 1.f;
       if (nv && ws.ts != nullptr) {
         const float* tsp = ws.ts + (it.shared ? 0 : (size_t)it.expert * ws.ts_stride);
@@ -353,32 +412,23 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         float acc[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) acc[t] = 0.f;
-        for (int j = 0; j < nst; ++j, ++g) {
-          const uint32_t s = g % ST, q = g % SA;
-          if (ok) ok = wait(sm, err, smem_addr(&sm.gfull[q]), (g / SA) & 1u);
+        for (int j = 0; j < nst; j += UNIT, ++u) {
+          const int ns = min(UNIT, nst - j);
+          const uint32_t us = u % SS, q = u % SA;
+          // this unit's scales first (they landed long ago), so their loads overlap the MMA wait
+          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u);
           if (!ok) continue;
-          fence_after();
-          const uint32_t taddr = tbase + ((uint32_t)(warp * 32) << 16) + q * GCOLS;
-          float blk[16];
-          if (fmt == FMT_FP8) {
-            uint32_t d[16];
-            if (narrow) {
-              ld4(taddr, d);
-            } else {
-              ld16(taddr, d);
-            }
-            ld_wait();
-            fence_before();
-            __syncwarp();
-            if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
-            const float* sw = reinterpret_cast<const float*>(sm.scl[s]);
-            const float wsc = w13 ? sw[r >= 64 ? 1 : 0] : sw[0];
+          float sc[UNIT][8];
 #pragma unroll
-            for (int t = 0; t < 16; ++t) blk[t] = (narrow && t >= 4) ? 0.f : __uint_as_float(d[t]) * wsc;
-          } else {
-            float sc[8];
-            if (nv) {
-              const uint2 sv = *reinterpret_cast<const uint2*>(sm.scl[s] + r * 8);
+          for (int t = 0; t < UNIT; ++t) {
+            const uint8_t* sp = sm.scl[us] + t * sb;
+            if (fmt == FMT_FP8) {
+              const float* sw = reinterpret_cast<const float*>(sp);
+              sc[t][0] = w13 ? sw[r >= 64 ? 1 : 0] : sw[0];
+#pragma unroll
+              for (int c = 1; c < 8; ++c) sc[t][c] = 0.f;
+            } else if (nv) {
+              const uint2 sv = t < ns ? *reinterpret_cast<const uint2*>(sp + r * 8) : make_uint2(0u, 0u);
               uint32_t h01, h23, h45, h67;
               e4m3x4_to_f16x2x2(sv.x, h01, h23);
               e4m3x4_to_f16x2x2(sv.y, h45, h67);
@@ -386,82 +436,131 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
               const float2 f23 = __half22float2(*reinterpret_cast<__half2*>(&h23));
               const float2 f45 = __half22float2(*reinterpret_cast<__half2*>(&h45));
               const float2 f67 = __half22float2(*reinterpret_cast<__half2*>(&h67));
-              sc[0] = f01.x; sc[1] = f01.y; sc[2] = f23.x; sc[3] = f23.y;
-              sc[4] = f45.x; sc[5] = f45.y; sc[6] = f67.x; sc[7] = f67.y;
+              sc[t][0] = f01.x; sc[t][1] = f01.y; sc[t][2] = f23.x; sc[t][3] = f23.y;
+              sc[t][4] = f45.x; sc[t][5] = f45.y; sc[t][6] = f67.x; sc[t][7] = f67.y;
             } else {
-              const uint32_t sv = *reinterpret_cast<const uint32_t*>(sm.scl[s] + r * 4);
+              const uint32_t sv = t < ns ? *reinterpret_cast<const uint32_t*>(sp + r * 4) : 0u;
 #pragma unroll
-              for (int c = 0; c < 4; ++c) sc[c] = e8m0_to_f32(sv >> (8 * c));
+              for (int c = 0; c < 4; ++c) sc[t][c] = e8m0_to_f32(sv >> (8 * c));
 #pragma unroll
-              for (int c = 4; c < 8; ++c) sc[c] = 0.f;
+              for (int c = 4; c < 8; ++c) sc[t][c] = 0.f;
             }
+          }
+          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.gfull[q]), (u / SA) & 1u);
+          if (!ok) continue;
+          fence_after();
+          const uint32_t taddr = tbase + ((uint32_t)(warp * 32) << 16) + q * GCOLS;
+          // acc[i] += (stage partial of column i) * (its B row's activation scale)
+          auto fold = [&](int t, const float (&blk)[16]) {
+            const float4* ap = reinterpret_cast<const float4*>(sm.asc[us] + t * NB);
+            const float4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
+            const float av[16] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
+                                  a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
+            // NVFP4: token i's rows 2i / 2i+1 share one scale
 #pragma unroll
-            for (int t = 0; t < 16; ++t) blk[t] = 0.f;
-            if (narrow) {
-              // columns 0-3 of the 4 chunk slots
-              uint32_t d[16];
+            for (int i = 0; i < 16; ++i) acc[i] = fmaf(blk[i], av[nv ? (2 * i) & (NB - 1) : i], acc[i]);
+          };
+          if (fmt == FMT_FP8) {
+            // one accumulated 16-column slot per stage
+            uint32_t d[UNIT][16];
 #pragma unroll
-              for (int c = 0; c < 4; ++c) ld4(taddr + c * NB, d + 4 * c);
-              ld_wait();
-              fence_before();
-              __syncwarp();
-              if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+            for (int t = 0; t < UNIT; ++t) {
+              if (t < ns) {
+                if (narrow) ld4(taddr + t * SCOLS, d[t]); else ld16(taddr + t * SCOLS, d[t]);
+              }
+            }
+            ld_wait();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+#pragma unroll
+            for (int t = 0; t < UNIT; ++t) {
+              if (t >= ns) continue;
+              float blk[16];
+#pragma unroll
+              for (int c = 0; c < 16; ++c) blk[c] = (narrow && c >= 4) ? 0.f : __uint_as_float(d[t][c]) * sc[t][0];
+              fold(t, blk);
+            }
+          } else if (narrow) {
+            // columns 0-3 of the 4 chunk slots of each stage
+            uint32_t d[UNIT][16];
+#pragma unroll
+            for (int t = 0; t < UNIT; ++t)
+              if (t < ns)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) ld4(taddr + t * SCOLS + c * NB, &d[t][4 * c]);
+            ld_wait();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+#pragma unroll
+            for (int t = 0; t < UNIT; ++t) {
+              if (t >= ns) continue;
+              float blk[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) blk[i] = 0.f;
               if (nv) {
-                // column 2t: first 16 K of each chunk (group 2c), column 2t+1: second (group 2c+1)
+                // column 2i: first 16 K of each chunk (group 2c), column 2i+1: second (group 2c+1)
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
+                for (int i = 0; i < 2; ++i) {
                   float v = 0.f;
 #pragma unroll
                   for (int c = 0; c < 4; ++c) {
-                    v = fmaf(__uint_as_float(d[4 * c + 2 * t]), sc[2 * c], v);
-                    v = fmaf(__uint_as_float(d[4 * c + 2 * t + 1]), sc[2 * c + 1], v);
+                    v = fmaf(__uint_as_float(d[t][4 * c + 2 * i]), sc[t][2 * c], v);
+                    v = fmaf(__uint_as_float(d[t][4 * c + 2 * i + 1]), sc[t][2 * c + 1], v);
                   }
-                  blk[t] = v;
+                  blk[i] = v;
                 }
               } else {
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
+                for (int i = 0; i < 4; ++i) {
                   float v = 0.f;
 #pragma unroll
-                  for (int c = 0; c < 4; ++c) v = fmaf(__uint_as_float(d[4 * c + t]), sc[c], v);
-                  blk[t] = v;
+                  for (int c = 0; c < 4; ++c) v = fmaf(__uint_as_float(d[t][4 * c + i]), sc[t][c], v);
+                  blk[i] = v;
                 }
               }
-            } else {
-              // two chunk slots (32 columns) per TMEM load round
+              fold(t, blk);
+            }
+          } else {
+            // all 16 columns: two chunk slots (32 columns) per TMEM load round
+#pragma unroll
+            for (int t = 0; t < UNIT; ++t) {
+              if (t >= ns) continue;
+              float blk[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) blk[i] = 0.f;
 #pragma unroll
               for (int half = 0; half < 2; ++half) {
                 uint32_t da[16], db[16];
-                ld16(taddr + (2 * half) * NB, da);
-                ld16(taddr + (2 * half + 1) * NB, db);
+                ld16(taddr + t * SCOLS + (2 * half) * NB, da);
+                ld16(taddr + t * SCOLS + (2 * half + 1) * NB, db);
                 ld_wait();
                 const int c0 = 2 * half, c1 = 2 * half + 1;
                 if (nv) {
 #pragma unroll
-                  for (int t = 0; t < 8; ++t) {
-                    float v = fmaf(__uint_as_float(da[2 * t]), sc[2 * c0], blk[t]);
-                    v = fmaf(__uint_as_float(da[2 * t + 1]), sc[2 * c0 + 1], v);
-                    v = fmaf(__uint_as_float(db[2 * t]), sc[2 * c1], v);
-                    blk[t] = fmaf(__uint_as_float(db[2 * t + 1]), sc[2 * c1 + 1], v);
+                  for (int i = 0; i < 8; ++i) {
+                    float v = fmaf(__uint_as_float(da[2 * i]), sc[t][2 * c0], blk[i]);
+                    v = fmaf(__uint_as_float(da[2 * i + 1]), sc[t][2 * c0 + 1], v);
+                    v = fmaf(__uint_as_float(db[2 * i]), sc[t][2 * c1], v);
+                    blk[i] = fmaf(__uint_as_float(db[2 * i + 1]), sc[t][2 * c1 + 1], v);
                   }
                 } else {
 #pragma unroll
-                  for (int t = 0; t < 16; ++t) {
-                    float v = fmaf(__uint_as_float(da[t]), sc[c0], blk[t]);
-                    blk[t] = fmaf(__uint_as_float(db[t]), sc[c1], v);
+                  for (int i = 0; i < 16; ++i) {
+                    float v = fmaf(__uint_as_float(da[i]), sc[t][c0], blk[i]);
+                    blk[i] = fmaf(__uint_as_float(db[i]), sc[t][c1], v);
                   }
                 }
               }
-              fence_before();
-              __syncwarp();
-              if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+              fold(t, blk);
             }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
           }
-          // activation scale of each B row (NVFP4: token t's rows 2t / 2t+1 share it)
-#pragma unroll
-          for (int t = 0; t < 16; ++t) acc[t] = fmaf(blk[t], sm.asc[s][nv ? (2 * t) & (NB - 1) : t], acc[t]);
           __syncwarp();
-          if (lane == 0) arrive(smem_addr(&sm.sempty[s]));
+          if (lane == 0) arrive(smem_addr(&sm.sempty[us]));
         }
         // one decision for all workers: the W13 epilogue below synchronises them
         if (workers_any(!ok || aborted(sm))) {
