@@ -37,6 +37,7 @@ import torch  # noqa: E402
 
 HEADLINE_M = 16
 LAYERS_PER_GPU = 6
+N_EXPERTS = None       # --experts: fewer routed experts per layer (the small case for ncu captures)
 CHUNKS_PER_STEP = 8
 METRIC = "MoE stage tokens/s (token-layers/s), verify M=16, c1/c2 V4-Flash MoE layer"
 UNIT = "tokens/s"
@@ -123,6 +124,8 @@ class ClockSampler:
 def build_layers(rank, n_layers, device):
     from shard_b200 import synth as S
     cfg = S.CONFIGS["c1"]
+    if N_EXPERTS:
+        cfg = cfg.replace(n_experts=N_EXPERTS)
     layers = []
     for j in range(n_layers):
         layers.append(S.device_layer(cfg, layer=rank * n_layers + j, device=device, seeded=[], fill="normal"))
@@ -378,7 +381,7 @@ def m_sweep(layers, cfg):
 
 
 def main():
-    global LAYERS_PER_GPU
+    global LAYERS_PER_GPU, N_EXPERTS
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -388,6 +391,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS_PER_GPU,
                     help="layers per GPU (a smaller stack is the small case for ncu captures)")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="routed experts per layer (default c1's 256; fewer is the small case for ncu captures)")
     ap.add_argument("--layout", choices=["tc", "fragment"], default=None,
                     help="weight layout / kernel family (default: the library default)")
     args = ap.parse_args()
@@ -397,6 +402,7 @@ def main():
         sbm.DEFAULT_LAYOUT = _lib.LAYOUT_TC if args.layout == "tc" else _lib.LAYOUT_FRAGMENT
     args.warmup = max(args.warmup, 3)
     LAYERS_PER_GPU = args.layers
+    N_EXPERTS = args.experts
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
     local_rank = env_int("LOCAL_RANK", 0)
