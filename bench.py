@@ -40,6 +40,10 @@ LAYERS_PER_GPU = 6
 N_EXPERTS = None       # --experts: fewer routed experts per layer (the small case for ncu captures)
 CHUNKS_PER_STEP = 8
 METRIC = "MoE stage tokens/s (token-layers/s), verify M=16, c1/c2 V4-Flash MoE layer"
+# DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum of one forward's W13 and W2 grouped
+# launches) over that forward's algorithmic bytes, from one capture of the small case
+# (--layers 1 --experts 32) per kernel family; roofline.traffic applies it to the live workload.
+TRAFFIC_RATIO = {"tcgen05": 492.5 / 469.0, "mma.sync": (1.018e9 + 13.4e6 + 0.509e9 + 12.5e6) / 1.44e9}
 UNIT = "tokens/s"
 
 
@@ -63,25 +67,37 @@ def hbm_peak():
 # ── clocks ───────────────────────────────────────────────────────────────────────────────────────
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks and throttle reasons every 50 ms; summary() keeps the samples taken inside
+    the windows marked with region() (the timed regions)."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, path):
         self.path = path
         self.proc = None
+        self.windows = []
 
     def __enter__(self):
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi needs a moment to start sampling: wait for its first line
+        t_end = time.time() + 5.0
+        while time.time() < t_end and self.proc.poll() is None:
+            self.f.flush()
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *a):
         if self.proc is not None:
+            time.sleep(0.12)   # one more sample after the last window
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -89,34 +105,50 @@ class ClockSampler:
                 self.proc.kill()
             self.f.close()
 
+    class _Window:
+        def __init__(self, owner):
+            self.owner = owner
+
+        def __enter__(self):
+            self.t0 = time.time()
+
+        def __exit__(self, *a):
+            self.owner.windows.append((self.t0, time.time()))
+
+    def region(self):
+        return ClockSampler._Window(self)
+
     def summary(self, gpus):
+        import datetime
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         with open(self.path) as f:
             for line in f:
                 p = [x.strip() for x in line.split(",")]
-                if len(p) < 9:
+                if len(p) < 10:
                     continue
                 try:
-                    idx = int(p[0])
+                    ts = datetime.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    idx = int(p[1])
+                    rows.append((ts, idx, float(p[2]), float(p[3]), p[6:10]))
                 except ValueError:
                     continue
-                if idx not in gpus:
-                    continue
-                try:
-                    sm.append(float(p[1]))
-                    smax.append(float(p[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, p[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-        if not sm:
+        rows = [r for r in rows if r[1] in gpus]
+        inside = [r for r in rows if any(t0 <= r[0] <= t1 for t0, t1 in self.windows)]
+        if not inside and rows and self.windows:
+            # windows shorter than the sampling interval: the samples nearest to each window
+            inside = [min(rows, key=lambda r: min(abs(r[0] - t0) + abs(r[0] - t1) for t0, t1 in self.windows))]
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "samples": len(sm),
-                "reasons": sorted(reasons)}
+        reasons = set()
+        for r in inside:
+            for n, v in zip(names, r[4]):
+                if v.lower() in ("active", "1"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(r[2] for r in inside), "sm_max_mhz": max(r[3] for r in inside),
+                "samples": len(inside), "reasons": sorted(reasons)}
 
 
 # ── workload ─────────────────────────────────────────────────────────────────────────────────────
@@ -253,18 +285,20 @@ def run_gpu(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(step_fn, steps, warmup):
+    def timed(step_fn, steps, warmup, clk=None):
+        import contextlib
         for _ in range(warmup):
             step_fn()
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            step_fn()
-        e1.record()
-        torch.cuda.synchronize()
+        with (clk.region() if clk is not None else contextlib.nullcontext()):
+            e0.record()
+            for _ in range(steps):
+                step_fn()
+            e1.record()
+            torch.cuda.synchronize()
         barrier()
         return max_over_ranks(e0.elapsed_time(e1) / 1000.0)
 
@@ -274,8 +308,8 @@ def run_gpu(args, rank, world, local_rank):
 
     clk = ClockSampler(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
                                     f"clocks_bench_r{rank}.csv"))
-    with clk:
-        t = timed(step_dev, args.steps, args.warmup)
+    clk.__enter__()   # sampling spans both timed regions (device-resident and end to end)
+    t = timed(step_dev, args.steps, args.warmup, clk)
     tok_layers = args.steps * C * HEADLINE_M * LAYERS_PER_GPU * world
     value = tok_layers / t
 
@@ -292,7 +326,8 @@ def run_gpu(args, rank, world, local_rank):
                 stage_in[j].copy_(xs_host[j], non_blocking=True)
         pipe.run(C, stage_in, outs_host)
 
-    t_e2e = timed(step_e2e, args.steps, max(args.warmup, 3))
+    t_e2e = timed(step_e2e, args.steps, max(args.warmup, 3), clk)
+    clk.__exit__(None, None, None)
     e2e_value = tok_layers / t_e2e
     bytes_io = C * HEADLINE_M * cfg.hidden * 2
 
@@ -307,9 +342,15 @@ def run_gpu(args, rank, world, local_rank):
         g_time = sum(r[1]["grouped"] for r in rows) / len(rows)
         f_bytes = sum(b[1] for b in nb) / len(nb)
         f_time = sum(r[1]["total"] for r in rows) / len(rows)
-        roof = {"kernel": "grouped_kernel (w13 + w2 launches)", "bound": "hbm",
+        family = "tcgen05" if layers[0].layout == 1 else "mma.sync"
+        kname = ("panel_kernel + tc_grouped_kernel" if family == "tcgen05" else "grouped_kernel") + \
+            " (w13 and w2 launches of one forward)"
+        roof = {"kernel": kname, "bound": "hbm",
                 "achieved": g_bytes / g_time / 1e9, "peak": peak, "unit": "GB/s",
-                "frac": g_bytes / g_time / 1e9 / peak, "traffic": None,
+                "frac": g_bytes / g_time / 1e9 / peak,
+                "traffic": g_bytes * TRAFFIC_RATIO[family],
+                "traffic_basis": "ncu DRAM bytes / algorithmic bytes on the small capture case, times this "
+                                 "workload's algorithmic bytes per forward",
                 "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback",
                 "algorithmic_bytes_per_forward": g_bytes, "grouped_us_per_forward": g_time * 1e6,
                 "forward_us": f_time * 1e6, "forward_frac": f_bytes / f_time / 1e9 / peak,

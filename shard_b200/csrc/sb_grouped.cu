@@ -588,51 +588,67 @@ cudaError_t launch_grouped(const GroupedArgs& a, int max_items, int grid_cap, cu
 // y[t] = bf16( sum over t's slots in ascending expert id of o[t*K + slot] (fp32), + shared o[P + t] )
 // A slot whose expert a later slot of the same token names again is dropped (the reference's
 // `y[idx] +=` with repeated indices keeps only the last write; v4_moe_grouped.py:98-118).
+// Each thread owns 8 columns: it issues the loads of all K slot rows (they do not depend on the
+// routing) together with the token's expert ids, then orders its (id, row) pairs with a bitonic
+// network over KP >= K entries (dropped and padding slots sort last) and sums in that order.
+template <int KP>
 __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16* __restrict__ o,
                                                       const int32_t* __restrict__ topk_idx, int m, int K, int h,
                                                       int has_shared, __nv_bfloat16* __restrict__ y) {
   const int t = blockIdx.x;
-  __shared__ int order[16];
-  __shared__ int n_keep;
-  if (threadIdx.x == 0) {
-    int all[16], ids[16], slots[16], n = 0;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) all[j] = j < K ? topk_idx[(size_t)t * K + j] : -1;
-    for (int j = 0; j < K; ++j) {
-      const int e = all[j];
-      bool later = false;
-#pragma unroll
-      for (int j2 = 0; j2 < 16; ++j2) later |= (j2 > j && j2 < K && all[j2] == e);
-      if (later) continue;
-      int p = n++;
-      while (p > 0 && ids[p - 1] > e) {
-        ids[p] = ids[p - 1];
-        slots[p] = slots[p - 1];
-        --p;
-      }
-      ids[p] = e;
-      slots[p] = j;
-    }
-    for (int j = 0; j < n; ++j) order[j] = slots[j];
-    n_keep = n;
-  }
-  __syncthreads();
   const int P = m * K;
-  const int nk = n_keep;
   const int v = blockIdx.y * blockDim.x + threadIdx.x;  // one 8-element vector per thread
   if (v >= h / 8) return;
-  uint4 r[17];
+  int key[KP];
+  uint4 r[KP];
 #pragma unroll
-  for (int j = 0; j < 16; ++j)
-    if (j < nk) r[j] = *reinterpret_cast<const uint4*>(o + ((size_t)t * K + order[j]) * h + v * 8);
-  if (has_shared) r[16] = *reinterpret_cast<const uint4*>(o + ((size_t)P + t) * h + v * 8);
+  for (int j = 0; j < KP; ++j) {
+    key[j] = j < K ? topk_idx[(size_t)t * K + j] : 0x7fffffff;
+    if (j < K) r[j] = *reinterpret_cast<const uint4*>(o + ((size_t)t * K + j) * h + v * 8);
+    else r[j] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  uint4 rs = make_uint4(0u, 0u, 0u, 0u);
+  if (has_shared) rs = *reinterpret_cast<const uint4*>(o + ((size_t)P + t) * h + v * 8);
+  // drop a slot when a later slot names the same expert
+  int drop[KP];
+#pragma unroll
+  for (int j = 0; j < KP; ++j) {
+    drop[j] = 0;
+#pragma unroll
+    for (int j2 = j + 1; j2 < KP; ++j2) drop[j] |= (j < K && j2 < K && key[j2] == key[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < KP; ++j)
+    if (drop[j]) key[j] = 0x7fffffff;
+  // ascending bitonic sort of (key, row); kept ids are distinct, so the order is total on them
+#pragma unroll
+  for (int k2 = 2; k2 <= KP; k2 <<= 1)
+#pragma unroll
+    for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1)
+#pragma unroll
+      for (int i = 0; i < KP; ++i) {
+        const int l = i ^ j2;
+        if (l > i) {
+          const bool up = (i & k2) == 0;
+          if (up ? key[i] > key[l] : key[i] < key[l]) {
+            const int tk = key[i];
+            key[i] = key[l];
+            key[l] = tk;
+            const uint4 tr = r[i];
+            r[i] = r[l];
+            r[l] = tr;
+          }
+        }
+      }
   float acc[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) acc[q] = 0.f;
 #pragma unroll
-  for (int j = 0; j < 17; ++j) {
-    if ((j < 16 && j < nk) || (j == 16 && has_shared)) {
-      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&r[j]);
+  for (int j = 0; j <= KP; ++j) {
+    const bool use = j < KP ? key[j] != 0x7fffffff : has_shared != 0;
+    if (use) {
+      const uint4 w = j < KP ? r[j] : rs;
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float2 f = __bfloat1622float2(p[q]);
@@ -651,7 +667,10 @@ __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16* __res
 cudaError_t launch_combine(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h, int has_shared,
                            __nv_bfloat16* y, cudaStream_t st) {
   dim3 grid(m, (h / 8 + 127) / 128);
-  combine_kernel<<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
+  if (topk <= 2) combine_kernel<2><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
+  else if (topk <= 4) combine_kernel<4><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
+  else if (topk <= 8) combine_kernel<8><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
+  else combine_kernel<16><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
   return cudaGetLastError();
 }
 

@@ -64,6 +64,7 @@ __global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* _
         xv1[j] = two ? __ldg(xr + 32 + lane) : make_uint4(0u, 0u, 0u, 0u);
       }
     }
+    float p[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float acc = 0.f;
@@ -79,8 +80,37 @@ __global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* _
           acc = fmaf(b.y, wf[8 + 2 * q + 1], acc);
         }
       }
-      acc = warp_sum(acc);
-      if (lane == 0 && j0 + j < nt) out[(size_t)(j0 + j) * e_total] = acc;
+      p[j] = acc;
+    }
+    // reduce-scatter over the xor tree 16, 8, 4, 2, 1 (the pairings of a warp_sum, so every
+    // token's sum is bitwise the one warp_sum gives): after it, lane l holds the sum of token
+    // 4*b4(l) + 2*b3(l) + b2(l), where bk(l) is bit k of l
+    {
+      const int h = (lane >> 4) & 1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float send = h ? p[i] : p[i + 4], keep = h ? p[i + 4] : p[i];
+        p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+    }
+    {
+      const int h = (lane >> 3) & 1;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float send = h ? p[i] : p[i + 2], keep = h ? p[i + 2] : p[i];
+        p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+    }
+    {
+      const int h = (lane >> 2) & 1;
+      const float send = h ? p[0] : p[1], keep = h ? p[1] : p[0];
+      p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    p[0] += __shfl_xor_sync(0xffffffffu, p[0], 2);
+    p[0] += __shfl_xor_sync(0xffffffffu, p[0], 1);
+    {
+      const int j = 4 * ((lane >> 4) & 1) + 2 * ((lane >> 3) & 1) + ((lane >> 2) & 1);
+      if ((lane & 3) == 0 && j0 + j < nt) out[(size_t)(j0 + j) * e_total] = p[0];
     }
   }
 }
@@ -90,23 +120,24 @@ __device__ __forceinline__ bool before(float va, int ea, float vb, int eb) {
   return va > vb || (va == vb && ea < eb);
 }
 
-// One CTA per token: the 4 warps quantise x[t] (act_quant, one 128-block per warp-iteration, loads
-// issued up front), then warp 0 routes. SPL = expert slots per lane (E <= 32 * SPL): every lane
+// One CTA per token: warp 0 routes while warps 1-3 quantise x[t] (act_quant, one 128-block per
+// warp-iteration, loads issued up front). SPL = expert slots per lane (E <= 32 * SPL): every lane
 // sorts its slots once (bitonic network, biased score descending, ties to the lower id), then k
-// rounds of a warp-wide argmax over the lanes' current heads pick the top-k in order.
-__device__ __forceinline__ void quant_row(const RouteArgs& a, int t, int warp, int lane) {
+// rounds of a warp-wide argmax over the lanes' current heads (redux.sync max of the value, then min
+// of the expert id among the lanes holding it) pick the top-k in order.
+__device__ __forceinline__ void quant_row(const RouteArgs& a, int t, int w, int nw, int lane) {
   const __nv_bfloat16* xr = a.x + (size_t)t * a.hidden;
   const int nb = a.hidden / 128;
-  for (int b0 = warp; b0 < nb; b0 += 16) {
+  for (int b0 = w; b0 < nb; b0 += 4 * nw) {
     uint2 raw[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int b = b0 + 4 * u;
+      const int b = b0 + nw * u;
       if (b < nb) raw[u] = *reinterpret_cast<const uint2*>(xr + b * 128 + lane * 4);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int b = b0 + 4 * u;
+      const int b = b0 + nw * u;
       if (b < nb) {
         const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
         const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
@@ -127,25 +158,37 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   if (t >= a.m) return;
-  if (a.xq != nullptr) quant_row(a, t, warp, lane);
-  if (warp != 0) return;
+  if (warp != 0) {
+    if (a.xq != nullptr) quant_row(a, t, warp - 1, 3, lane);
+    return;
+  }
   const int E = a.n_experts;
   const int nsplit = a.hidden / gate_ksplit(a.hidden);
-  // logits: split 0 + split 1 + ... in ascending split order (one memory latency per split)
+  // logits: split 0 + split 1 + ... in ascending split order; the loads of 4 splits are issued
+  // before their adds (one memory latency per 4 splits)
   float sc[SPL];
 #pragma unroll
-  for (int i = 0; i < SPL; ++i) {
-    const int e = lane + 32 * i;
-    sc[i] = e < E ? a.logits[(size_t)t * E + e] : -INFINITY;
-  }
-  for (int ks = 1; ks < nsplit; ++ks) {
-    const float* pk = a.logits + ((size_t)ks * a.m + t) * E;
+  for (int i = 0; i < SPL; ++i) sc[i] = 0.f;
+  for (int ks0 = 0; ks0 < nsplit; ks0 += 4) {
+    float pv[4][SPL];
 #pragma unroll
-    for (int i = 0; i < SPL; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E) sc[i] += pk[e];
+    for (int u = 0; u < 4; ++u) {
+      const float* pk = a.logits + ((size_t)(ks0 + u) * a.m + t) * E;
+#pragma unroll
+      for (int i = 0; i < SPL; ++i) {
+        const int e = lane + 32 * i;
+        pv[u][i] = (ks0 + u < nsplit && e < E) ? pk[e] : 0.f;
+      }
     }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int i = 0; i < SPL; ++i)
+        if (ks0 + u < nsplit) sc[i] = (ks0 + u == 0) ? pv[u][i] : sc[i] + pv[u][i];
   }
+#pragma unroll
+  for (int i = 0; i < SPL; ++i)
+    if (lane + 32 * i >= E) sc[i] = -INFINITY;
   if (a.score_func == SCORE_SOFTMAX) {
     float mx = -INFINITY;
 #pragma unroll
@@ -226,17 +269,11 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       if (j < K) {
-        float v = bv[0];
-        int e = be[0];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-          const int oe = __shfl_xor_sync(0xffffffffu, e, o);
-          if (before(ov, oe, v, e)) {
-            v = ov;
-            e = oe;
-          }
-        }
+        // float -> order-preserving unsigned key; the largest head value, then its lowest id
+        const uint32_t b = __float_as_uint(bv[0] + 0.0f);   // -0 -> +0: equal values tie on the id
+        const uint32_t key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+        int e = (int)__reduce_min_sync(0xffffffffu, key == kmax ? (uint32_t)be[0] : 0x7fffffffu);
         if (e >= E) e = j;  // only reachable with NaN scores; keeps every id in range
         sel[j] = e;
         const float mine = be[0] == e ? uv[0] : 0.f;
@@ -282,16 +319,25 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
 
 // Single CTA. counts -> exclusive offsets -> stable placement (pair p = t*K + j, ascending p
 // within each expert, i.e. ascending token) -> active expert list. Deterministic.
+// pairs whose expert ids are staged in shared memory (with 2 * 1024 ints of counters: < 48 KB)
+constexpr int PERMUTE_SMEM_PAIRS = 8192;
+
 __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   extern __shared__ int smem[];
-  int* cnt = smem;                   // [E]
-  int* cursor = smem + a.n_experts;  // [E]
+  int* cnt = smem;                       // [E]
+  int* cursor = smem + a.n_experts;      // [E]
+  int* tk = smem + 2 * a.n_experts;      // [P] copy of topk_idx when it fits (PERMUTE_SMEM_PAIRS)
   __shared__ int warp_tot[32];
   const int E = a.n_experts, P = a.m * a.topk;
+  const bool staged = P <= PERMUTE_SMEM_PAIRS;
   if (threadIdx.x == 0 && a.err) *a.err = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int p = threadIdx.x; p < P; p += blockDim.x) atomicAdd(&cnt[a.topk_idx[p]], 1);
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int e = a.topk_idx[p];
+    if (staged) tk[p] = e;
+    atomicAdd(&cnt[e], 1);
+  }
   __syncthreads();
   // exclusive scan of cnt over E (E <= 1024 = blockDim), and of the active flags
   const int e = threadIdx.x;
@@ -357,7 +403,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   if (warp == 0) {
     for (int p0 = 0; p0 < P; p0 += 32) {
       const int p = p0 + lane;
-      const int ex = p < P ? a.topk_idx[p] : -1 - lane;
+      const int ex = p < P ? (staged ? tk[p] : a.topk_idx[p]) : -1 - lane;
       const unsigned same = __match_any_sync(0xffffffffu, ex);
       const int rank = __popc(same & ((1u << lane) - 1u));
       const int leader = __ffs(same) - 1;
@@ -393,7 +439,8 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t st) {
-  const size_t smem = (size_t)2 * a.n_experts * sizeof(int);
+  const int P = a.m * a.topk;
+  const size_t smem = (size_t)(2 * a.n_experts + (P <= PERMUTE_SMEM_PAIRS ? P : 0)) * sizeof(int);
   permute_kernel<<<1, 1024, smem, st>>>(a);
   return cudaGetLastError();
 }

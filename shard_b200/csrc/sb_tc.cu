@@ -617,13 +617,16 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
 }
 
 // ── B panels: the activation operand of every pass, one 2 KB swizzled tile per (pass, stage) ──
-// CTA (stage j, slot): slot 0 is the shared expert / dense matrix when present, then active slots.
-// Thread (row = tid / 8, chunk c = tid % 8) writes the 16-byte chunk c of B row `row`.
+// CTA (group of PANEL_STAGES stages, slot): slot 0 is the shared expert / dense matrix when present,
+// then the active slots. Thread (row = tid / 8, chunk c = tid % 8) writes the 16-byte chunk c of B
+// row `row` of every stage of the group, its loads for all the group's stages issued first.
 // W13 / DENSE: the e4m3 row slice and its scale are copied. W2: the bf16 h row slice is quantised
 // to e4m3 with one scale per 128 K (act_quant, kernel.py:40-125): amax over the 8 threads of the
 // row, scale = amax/448 (or its power-of-two ceiling), q = e4m3(v / scale).
+constexpr int PANEL_STAGES = 4;
+
 __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
-  const int j = blockIdx.x;
+  const int j0 = blockIdx.x * PANEL_STAGES;
   const int slot = blockIdx.y;
   const int K = a.k, nst = K / 128, nkb = K / 128;
   const int P = a.m * a.topk;
@@ -651,23 +654,42 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
   for (int pb = 0, pi = 0; pb < cnt; pb += pm, ++pi) {
     const int i = pb + tslot;
     const bool valid = tslot < pm && i < cnt;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    float sc = 0.f;
+    int srow = 0;
+    if (valid) {
+      if (a.mode != MODE_W2) srow = (shared || a.pair_tok == nullptr) ? i : a.pair_tok[base + i];
+      else srow = shared ? P + i : base + i;
+    }
+    uint4 v[PANEL_STAGES];
+    float sc[PANEL_STAGES];
     if (a.mode != MODE_W2) {
-      if (valid) {
-        const int srow = (shared || a.pair_tok == nullptr) ? i : a.pair_tok[base + i];
-        v = *reinterpret_cast<const uint4*>(a.xq + (size_t)srow * K + (size_t)j * 128 + c * 16);
-        sc = a.xs[(size_t)srow * nkb + j];
+#pragma unroll
+      for (int u = 0; u < PANEL_STAGES; ++u) {
+        const int j = j0 + u;
+        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        sc[u] = 0.f;
+        if (valid && j < nst) {
+          v[u] = *reinterpret_cast<const uint4*>(a.xq + (size_t)srow * K + (size_t)j * 128 + c * 16);
+          sc[u] = a.xs[(size_t)srow * nkb + j];
+        }
       }
     } else {
-      float f[16];
-      float am = 0.f;
-      if (valid) {
-        const int srow = shared ? P + i : base + i;
-        const uint4* hp = reinterpret_cast<const uint4*>(a.hbf + (size_t)srow * K + (size_t)j * 128 + c * 16);
-        const uint4 h0 = hp[0], h1 = hp[1];
-        const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&h0);
-        const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&h1);
+      uint4 hv[PANEL_STAGES][2];
+#pragma unroll
+      for (int u = 0; u < PANEL_STAGES; ++u) {
+        const int j = j0 + u;
+        hv[u][0] = hv[u][1] = make_uint4(0u, 0u, 0u, 0u);
+        if (valid && j < nst) {
+          const uint4* hp = reinterpret_cast<const uint4*>(a.hbf + (size_t)srow * K + (size_t)j * 128 + c * 16);
+          hv[u][0] = hp[0];
+          hv[u][1] = hp[1];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PANEL_STAGES; ++u) {
+        float f[16];
+        const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&hv[u][0]);
+        const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&hv[u][1]);
+        float am = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 x0 = __bfloat1622float2(p0[e]), x1 = __bfloat1622float2(p1[e]);
@@ -678,37 +700,42 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
         }
 #pragma unroll
         for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(f[e]));
-      } else {
+        // the 8 threads of a row are 8 consecutive lanes
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        sc[u] = 0.f;
+        if (valid && j0 + u < nst) {
+          const float s_ = act_scale(am, a.act_pow2 != 0);
+          uint8_t qb[16];
+          if (a.act_pow2) {
+            const float inv = __frcp_rn(s_);   // exact: s_ is a power of two
 #pragma unroll
-        for (int e = 0; e < 16; ++e) f[e] = 0.f;
-      }
-      // the 8 threads of a row are 8 consecutive lanes
-      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
-      if (valid) {
-        sc = act_scale(am, a.act_pow2 != 0);
-        uint8_t qb[16];
-        if (a.act_pow2) {
-          const float inv = __frcp_rn(sc);   // exact: sc is a power of two
+            for (int e = 0; e < 16; ++e) qb[e] = act_q_pow2(f[e], inv);
+          } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) qb[e] = act_q_pow2(f[e], inv);
-        } else {
+            for (int e = 0; e < 16; ++e) qb[e] = act_q(f[e], s_);
+          }
+          uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) qb[e] = act_q(f[e], sc);
+          for (int e = 0; e < 4; ++e)
+            w[e] = (uint32_t)qb[4 * e] | ((uint32_t)qb[4 * e + 1] << 8) | ((uint32_t)qb[4 * e + 2] << 16) |
+                   ((uint32_t)qb[4 * e + 3] << 24);
+          v[u] = make_uint4(w[0], w[1], w[2], w[3]);
+          sc[u] = s_;
         }
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          w[e] = (uint32_t)qb[4 * e] | ((uint32_t)qb[4 * e + 1] << 8) | ((uint32_t)qb[4 * e + 2] << 16) |
-                 ((uint32_t)qb[4 * e + 3] << 24);
-        v = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-    if (!keep) v = make_uint4(0u, 0u, 0u, 0u);
-    const size_t tile = (size_t)(pass0 + pi) * nst + j;
-    *reinterpret_cast<uint4*>(a.bpanel + tile * B_BYTES + row * 128 + ((c ^ (row & 7)) << 4)) = v;
-    if (c == 0) a.apanel[tile * NB + row] = valid ? sc : 0.f;
+#pragma unroll
+    for (int u = 0; u < PANEL_STAGES; ++u) {
+      const int j = j0 + u;
+      if (j >= nst) break;
+      const size_t tile = (size_t)(pass0 + pi) * nst + j;
+      *reinterpret_cast<uint4*>(a.bpanel + tile * B_BYTES + row * 128 + ((c ^ (row & 7)) << 4)) =
+          keep ? v[u] : make_uint4(0u, 0u, 0u, 0u);
+      if (c == 0) a.apanel[tile * NB + row] = valid ? sc[u] : 0.f;
+    }
   }
 }
 
@@ -762,7 +789,7 @@ static cudaError_t launch_tc_one(const TcArgs& a, int grid, cudaStream_t st) {
 
 cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st) {
   if (max_slots < 1) return cudaSuccess;
-  dim3 grid(a.k / 128, max_slots);
+  dim3 grid((a.k / 128 + tc::PANEL_STAGES - 1) / tc::PANEL_STAGES, max_slots);
   tc::panel_kernel<<<grid, 128, 0, st>>>(a);
   return cudaGetLastError();
 }
