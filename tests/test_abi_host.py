@@ -1,0 +1,146 @@
+"""The C-ABI library on the host (no GPU work): it loads, exports every entry point the public header
+declares, and validates shapes, pointers and workspaces before any launch, returning the documented
+status codes (include/shard_b200.h). Every call here returns before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from shard_b200 import _lib
+from shard_b200 import formats as F
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "shard_b200.h")
+FAKE = ctypes.c_void_p(1 << 12)   # an aligned address that is never dereferenced by these calls
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(sb_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_loads_with_matching_abi():
+    L = _lib.lib()
+    assert L.sb_abi_version() == _lib.ABI_VERSION
+
+
+def test_every_declared_entry_point_is_exported_and_bound():
+    names = header_functions()
+    assert len(names) >= 15, names
+    L = _lib.lib()
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in the header but not exported"
+        assert n in _lib.SIGNATURES, f"{n} exported but has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_tiled_sizes_match_the_canonical_sizes():
+    L = _lib.lib()
+    n, k = 4096, 2048
+    assert L.sb_tiled_bytes(F.FMT_NVFP4, n, k) == n * k // 2
+    assert L.sb_tiled_bytes(F.FMT_MXFP4, n, k) == n * k // 2
+    assert L.sb_tiled_bytes(F.FMT_FP8, n, k) == n * k
+    assert L.sb_tiled_scale_bytes(F.FMT_NVFP4, 0, n, k) == n * k // 16
+    assert L.sb_tiled_scale_bytes(F.FMT_MXFP4, 0, n, k) == n * k // 32
+    # FP8 block scales: tensor-core layout keeps 16 bytes per 128x128 block (2 scales + 2 pads)
+    assert L.sb_tiled_scale_bytes(F.FMT_FP8, _lib.KIND_TC, n, k) == (n // 128) * (k // 128) * 16
+
+
+def _layer(layout=_lib.LAYOUT_TC, hidden=4096, inter=2048, n_experts=256, topk=8, fmt=F.FMT_NVFP4):
+    d = _lib.SbMoeLayer()
+    d.hidden, d.inter, d.n_experts, d.topk = hidden, inter, n_experts, topk
+    d.expert_fmt, d.has_shared, d.score_func, d.act_pow2 = fmt, 1, 1, 1
+    d.route_scale, d.swiglu_limit = 1.0, 0.0
+    for f in ("gate_w", "w13", "w13_s", "w13_ts", "w2", "w2_s", "w2_ts", "sh_w13", "sh_w13_s", "sh_w2", "sh_w2_s"):
+        setattr(d, f, FAKE.value)
+    d.layout = layout
+    return d
+
+
+def test_workspace_sizes_grow_with_m_and_reject_bad_layers():
+    L = _lib.lib()
+    for layout in (_lib.LAYOUT_FRAGMENT, _lib.LAYOUT_TC):
+        d = _layer(layout)
+        sizes = [L.sb_moe_workspace_bytes(ctypes.byref(d), m) for m in (1, 16, 64, 256)]
+        assert all(s > 0 for s in sizes) and sizes == sorted(sizes)
+    bad = _layer(hidden=100)
+    assert L.sb_moe_workspace_bytes(ctypes.byref(bad), 16) == 0
+    assert L.sb_qgemm_workspace_bytes(F.FMT_FP8, _lib.LAYOUT_FRAGMENT, 4096, 4096, 16) == 0
+    a = L.sb_qgemm_workspace_bytes(F.FMT_NVFP4, _lib.LAYOUT_TC, 4096, 4096, 8)
+    b = L.sb_qgemm_workspace_bytes(F.FMT_NVFP4, _lib.LAYOUT_TC, 4096, 4096, 9)
+    assert 0 < a < b   # 9 tokens need a second NVFP4 pass (8 tokens per pass)
+
+
+def _msg():
+    return _lib.lib().sb_last_error().decode()
+
+
+def test_forward_validates_before_launching():
+    L = _lib.lib()
+    st = None
+    d = _layer(hidden=100)
+    rc = L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, 1 << 30, st)
+    assert rc == -2 and "hidden" in _msg()
+    d = _layer(topk=0)
+    assert L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, 1 << 30, st) == -2
+    d = _layer(fmt=7)
+    assert L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, 1 << 30, st) == -3
+    d = _layer()
+    d.layout = 5
+    assert L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, 1 << 30, st) == -1
+    d = _layer()
+    d.w13 = None
+    assert L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, 1 << 30, st) == -1
+    d = _layer()
+    need = L.sb_moe_workspace_bytes(ctypes.byref(d), 16)
+    rc = L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, need - 1, st)
+    assert rc == -4 and "workspace" in _msg()
+    rc = L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, None, need, st)
+    assert rc == -4
+    # hash routing needs token ids
+    d.tid2eid, d.vocab = FAKE.value, 1000
+    assert L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, need, st) == -1
+    # m == 0 is a no-op
+    d = _layer()
+    assert L.sb_moe_forward(ctypes.byref(d), FAKE, 0, None, FAKE, None, None, None, 0, st) == 0
+    # misaligned activations
+    d = _layer()
+    assert L.sb_moe_forward(ctypes.byref(d), ctypes.c_void_p((1 << 12) + 4), 16, None, FAKE, None, None, FAKE,
+                            need, st) == -1
+
+
+def test_kernel_seam_entry_points_validate():
+    L = _lib.lib()
+    # qgemm: n must be a multiple of 32, the tensor-core layout a multiple of 128 and a workspace
+    assert L.sb_qgemm(F.FMT_FP8, _lib.LAYOUT_FRAGMENT, FAKE, FAKE, None, 100, 512, FAKE, FAKE, 4, FAKE, None, 0,
+                      None) == -2
+    assert L.sb_qgemm(F.FMT_NVFP4, _lib.LAYOUT_FRAGMENT, FAKE, FAKE, None, 256, 512, FAKE, FAKE, 4, FAKE, None, 0,
+                      None) == -1   # NVFP4 without its tensor scale
+    assert L.sb_qgemm(F.FMT_FP8, _lib.LAYOUT_TC, FAKE, FAKE, None, 160, 512, FAKE, FAKE, 4, FAKE, FAKE, 1 << 20,
+                      None) == -2
+    assert L.sb_qgemm(F.FMT_FP8, _lib.LAYOUT_TC, FAKE, FAKE, None, 256, 512, FAKE, FAKE, 4, FAKE, FAKE, 16,
+                      None) == -4
+    assert L.sb_qgemm(9, _lib.LAYOUT_TC, FAKE, FAKE, None, 256, 512, FAKE, FAKE, 4, FAKE, FAKE, 1 << 20, None) == -3
+    # act_quant: k must be a multiple of 128
+    assert L.sb_act_quant(FAKE, 4, 100, 1, FAKE, FAKE, None) == -2
+    assert L.sb_act_quant(FAKE, 0, 128, 1, FAKE, FAKE, None) == 0
+    # tiling: unknown kind, W13 with an odd intermediate size, TC layout with n % 128 != 0
+    assert L.sb_tile_weights(F.FMT_FP8, 2, FAKE, FAKE, 1, 256, 512, None) == -1
+    assert L.sb_tile_weights(F.FMT_FP8, _lib.MAT_W13, FAKE, FAKE, 1, 96, 512, None) == -2
+    assert L.sb_tile_weights(F.FMT_FP8, _lib.MAT_PLAIN | _lib.KIND_TC, FAKE, FAKE, 1, 96, 512, None) == -2
+    assert L.sb_tile_scales(F.FMT_NVFP4, _lib.MAT_PLAIN, None, FAKE, 1, 256, 512, None) == -1
+    assert L.sb_selftest_formats(None, None) == -1
+
+
+@pytest.mark.parametrize("call", ["route", "forward"])
+def test_bad_m_is_rejected(call):
+    L = _lib.lib()
+    d = _layer()
+    f = L.sb_moe_route if call == "route" else None
+    if call == "route":
+        rc = f(ctypes.byref(d), FAKE, -1, None, None, None, FAKE, 1 << 30, None)
+    else:
+        rc = L.sb_moe_forward(ctypes.byref(d), FAKE, -1, None, FAKE, None, None, FAKE, 1 << 30, None)
+    assert rc == -2

@@ -1,0 +1,92 @@
+"""Pipeline stages over torch.distributed on the host: world_size 2 with the gloo backend, each rank
+owning a contiguous layer block (even_tiling, the split of v4_pipe.py:2286-2298) and passing bf16
+activations with send/recv, as the NCCL path does between GPUs. The layers are stand-ins with the
+MoE layer's x -> y contract, so the test checks the host logic: block assignment, chunk streaming
+and ordering, and that the last stage's outputs equal the whole stack applied in order."""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from shard_b200.pipeline import Pipeline, StageStack, even_tiling
+
+HIDDEN, M, N_LAYERS, CHUNKS = 64, 4, 5, 6
+
+
+class Affine:
+    """A stand-in layer: y = bf16(x * a_l + b_l), distinct per layer so the order is observable."""
+
+    def __init__(self, l):
+        self.a, self.b = 1.0 + 0.25 * l, 0.5 * l - 1.0
+
+    def forward(self, x):
+        return (x.float() * self.a + self.b).to(torch.bfloat16)
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(7)
+    return [torch.randn(M, HIDDEN, generator=g).to(torch.bfloat16) for _ in range(CHUNKS)]
+
+
+def _expected():
+    outs = []
+    for x in _inputs():
+        for l in range(N_LAYERS):
+            x = Affine(l).forward(x)
+        outs.append(x)
+    return outs
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        block = even_tiling(N_LAYERS, world)[rank]
+        pipe = Pipeline(StageStack([Affine(l) for l in block]), M, HIDDEN, rank, world, torch.device("cpu"))
+        chunks = _inputs() if rank == 0 else None
+        outs = [torch.empty(M, HIDDEN, dtype=torch.bfloat16) for _ in range(CHUNKS)] if rank == world - 1 else None
+        pipe.run(CHUNKS, chunks, outs)
+        if rank == world - 1:
+            torch.save(outs, out_path)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_even_tiling_front_loads_the_remainder():
+    assert [len(r) for r in even_tiling(48, 8)] == [6] * 8
+    assert [list(r) for r in even_tiling(7, 3)] == [[0, 1, 2], [3, 4], [5, 6]]
+    assert [len(r) for r in even_tiling(61, 8)] == [8, 8, 8, 8, 8, 7, 7, 7]
+    assert sum(len(r) for r in even_tiling(5, 2)) == 5
+
+
+def test_single_stage_runs_locally():
+    pipe = Pipeline(StageStack([Affine(l) for l in range(N_LAYERS)]), M, HIDDEN, 0, 1, torch.device("cpu"))
+    got = pipe.run(CHUNKS, _inputs())
+    for g, e in zip(got, _expected()):
+        assert torch.equal(g, e)
+
+
+@pytest.mark.parametrize("world", [2])
+def test_two_stage_gloo_pipeline_matches_the_whole_stack(world):
+    with tempfile.TemporaryDirectory() as d:
+        out_path = os.path.join(d, "outs.pt")
+        mp.start_processes(_rank_main, args=(world, _free_port(), out_path), nprocs=world, join=True,
+                           start_method="spawn")
+        got = torch.load(out_path)
+    for g, e in zip(got, _expected()):
+        assert torch.equal(g, e)
