@@ -134,6 +134,9 @@ __device__ __forceinline__ void set_abort(Smem& sm, int* err, bool flag_err) {
 
 // bounded wait; on timeout flag the CTA (and the launch) and return false
 __device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t parity) {
+  // poll without a suspend hint first (most waits end within a few hundred cycles), then sleep
+  for (uint32_t i = 0; i < 256; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
   for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
     if ((i & 63u) == 63u && aborted(sm)) return false;
@@ -261,8 +264,16 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     __syncwarp();
     uint32_t g = 0, u = 0;
     bool ok = true;
+    // the next item's descriptor is loaded one item ahead, so its global loads overlap this item
+    Item nxt = blockIdx.x < n_items ? item_of(a, blockIdx.x, n_sh) : Item{};
+    int nxt_pass0 = blockIdx.x < n_items ? first_pass(nxt) : 0;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const Item it = item_of(a, item, n_sh);
+      const Item it = nxt;
+      const int pass0 = nxt_pass0;
+      if (item + (int)gridDim.x < n_items) {
+        nxt = item_of(a, item + gridDim.x, n_sh);
+        nxt_pass0 = first_pass(nxt);
+      }
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const CUtensorMap* map = it.shared ? &ta.map_shared : &ta.map_routed;
@@ -271,7 +282,6 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
       const uint32_t sb = stage_sbytes(fmt);
       const int row0 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;
       const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)it.rb * nst * sb;
-      const int pass0 = first_pass(it);
       for (int pb = 0, pi = 0; pb < it.cnt && ok; pb += pm, ++pi) {
         if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(err) != 0)) {
           set_abort(sm, err, false);
@@ -322,8 +332,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     // the whole warp runs the loop (uniform control flow); one elected lane issues MMAs and commits
     uint32_t g = 0, u = 0;
     bool ok = true;
+    Item nxt = blockIdx.x < n_items ? item_of(a, blockIdx.x, n_sh) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const Item it = item_of(a, item, n_sh);
+      const Item it = nxt;
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, item + gridDim.x, n_sh);
       const int fmt = item_fmt(it);
       const int pm = tc_pass_max(fmt);
       const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
@@ -374,8 +386,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     const int r = tid;  // weight row of the item = TMEM lane
     uint32_t u = 0;
     bool ok = true;
+    Item nxt = blockIdx.x < n_items ? item_of(a, blockIdx.x, n_sh) : Item{};
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-      const Item it = item_of(a, item, n_sh);
+      const Item it = nxt;
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, item + gridDim.x, n_sh);
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pm = tc_pass_max(fmt);
