@@ -215,6 +215,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
   return false;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start
+// while the previous kernel of the stream is still running; pdl_wait() returns once that kernel has
+// completed and its memory is visible, so everything a kernel reads or writes comes after it.
+// pdl_trigger() lets the next kernel of the stream start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }

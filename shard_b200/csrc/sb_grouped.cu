@@ -598,6 +598,8 @@ __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16* __res
   const int t = blockIdx.x;
   const int P = m * K;
   const int v = blockIdx.y * blockDim.x + threadIdx.x;  // one 8-element vector per thread
+  pdl_wait();
+  pdl_trigger();
   if (v >= h / 8) return;
   int key[KP];
   uint4 r[KP];
@@ -667,11 +669,11 @@ __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16* __res
 cudaError_t launch_combine(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h, int has_shared,
                            __nv_bfloat16* y, cudaStream_t st) {
   dim3 grid(m, (h / 8 + 127) / 128);
-  if (topk <= 2) combine_kernel<2><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
-  else if (topk <= 4) combine_kernel<4><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
-  else if (topk <= 8) combine_kernel<8><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
-  else combine_kernel<16><<<grid, 128, 0, st>>>(o, topk_idx, m, topk, h, has_shared, y);
-  return cudaGetLastError();
+  const dim3 block(128);
+  if (topk <= 2) return launch_pdl(combine_kernel<2>, grid, block, 0, st, o, topk_idx, m, topk, h, has_shared, y);
+  if (topk <= 4) return launch_pdl(combine_kernel<4>, grid, block, 0, st, o, topk_idx, m, topk, h, has_shared, y);
+  if (topk <= 8) return launch_pdl(combine_kernel<8>, grid, block, 0, st, o, topk_idx, m, topk, h, has_shared, y);
+  return launch_pdl(combine_kernel<16>, grid, block, 0, st, o, topk_idx, m, topk, h, has_shared, y);
 }
 
 // Standalone act_quant (the kernel seam): one warp per (row, 128-block).

@@ -32,6 +32,8 @@ __global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* _
   const int e = blockIdx.x * 8 + warp;
   const int ks = blockIdx.y;
   const int t0 = blockIdx.z * GATE_TOKENS;
+  pdl_wait();
+  pdl_trigger();
   if (e >= e_total) return;
   const int nt = min(GATE_TOKENS, m - t0);
   const int kspl = gate_ksplit(h);
@@ -157,6 +159,8 @@ template <int SPL>
 __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
   if (t >= a.m) return;
   if (warp != 0) {
     if (a.xq != nullptr) quant_row(a, t, warp - 1, 3, lane);
@@ -330,6 +334,8 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   __shared__ int warp_tot[32];
   const int E = a.n_experts, P = a.m * a.topk;
   const bool staged = P <= PERMUTE_SMEM_PAIRS;
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x == 0 && a.err) *a.err = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
@@ -423,26 +429,25 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
 cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int m, int e, int h,
                                cudaStream_t st) {
   dim3 grid((e + 7) / 8, h / gate_ksplit(h), (m + GATE_TOKENS - 1) / GATE_TOKENS);
-  gate_logits_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w, logits, m, e, h);
-  return cudaGetLastError();
+  return launch_pdl(gate_logits_kernel, grid, dim3(256), 0, st, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w,
+                    logits, m, e, h);
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
   const int spl = (a.n_experts + 31) / 32;
-  if (spl <= 1) route_kernel<1><<<a.m, 128, 0, st>>>(a);
-  else if (spl <= 2) route_kernel<2><<<a.m, 128, 0, st>>>(a);
-  else if (spl <= 4) route_kernel<4><<<a.m, 128, 0, st>>>(a);
-  else if (spl <= 8) route_kernel<8><<<a.m, 128, 0, st>>>(a);
-  else if (spl <= 16) route_kernel<16><<<a.m, 128, 0, st>>>(a);
-  else route_kernel<32><<<a.m, 128, 0, st>>>(a);
-  return cudaGetLastError();
+  const dim3 grid(a.m), block(128);
+  if (spl <= 1) return launch_pdl(route_kernel<1>, grid, block, 0, st, a);
+  if (spl <= 2) return launch_pdl(route_kernel<2>, grid, block, 0, st, a);
+  if (spl <= 4) return launch_pdl(route_kernel<4>, grid, block, 0, st, a);
+  if (spl <= 8) return launch_pdl(route_kernel<8>, grid, block, 0, st, a);
+  if (spl <= 16) return launch_pdl(route_kernel<16>, grid, block, 0, st, a);
+  return launch_pdl(route_kernel<32>, grid, block, 0, st, a);
 }
 
 cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t st) {
   const int P = a.m * a.topk;
   const size_t smem = (size_t)(2 * a.n_experts + (P <= PERMUTE_SMEM_PAIRS ? P : 0)) * sizeof(int);
-  permute_kernel<<<1, 1024, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(permute_kernel, dim3(1), dim3(1024), smem, st, a);
 }
 
 }  // namespace sb

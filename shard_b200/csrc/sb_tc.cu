@@ -240,6 +240,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   __syncthreads();
   fence_after();
   const uint32_t tbase = sm.tmem_base;
+  // everything above touched only this CTA's shared memory and TMEM; the inputs come after
+  pdl_wait();
+  pdl_trigger();
 
   const int n_sh = a.has_shared ? a.items_per_expert : 0;
   const int n_items = n_sh + (a.mode == MODE_DENSE ? 0 : (*a.n_active) * a.items_per_expert);
@@ -644,6 +647,8 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
   const int slot = blockIdx.y;
   const int K = a.k, nst = K / 128, nkb = K / 128;
   const int P = a.m * a.topk;
+  pdl_wait();
+  pdl_trigger();
   int shared, cnt, base, pass0, nv;
   if (slot < a.has_shared) {
     shared = 1;
@@ -795,8 +800,7 @@ static cudaError_t launch_tc_one(const TcArgs& a, int grid, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  tc_grouped_kernel<F><<<grid, NTHREADS, SMEM_BYTES, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(tc_grouped_kernel<F>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
 }
 
 }  // namespace tc
@@ -804,8 +808,7 @@ static cudaError_t launch_tc_one(const TcArgs& a, int grid, cudaStream_t st) {
 cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st) {
   if (max_slots < 1) return cudaSuccess;
   dim3 grid((a.k / 128 + tc::PANEL_STAGES - 1) / tc::PANEL_STAGES, max_slots);
-  tc::panel_kernel<<<grid, 128, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(tc::panel_kernel, grid, dim3(128), 0, st, a);
 }
 
 cudaError_t launch_tc_grouped(const GroupedArgs& g, const TcPlan& plan, int max_items, cudaStream_t st) {
