@@ -16,6 +16,9 @@ bf16 activations between stages and 8 chunks streamed per step. Per-GPU work is 
             and scales + the shared expert) / time, against MEASURED_PEAKS.json's HBM copy figure.
   cpu_baseline = the CPU oracle (numpy restatement of the reference MoE.forward) on a sample of the
             same workload on the host cores.
+  sweep   = (N=1) c1 at M = 1, 8, 32, 64 over the same 6 layers; one c3 layer (FP8 experts, Zipf
+            selection) at M = 1, 16, 64 and one c4 layer (Kimi-K3-scale NVFP4, the prefill regime)
+            at M = 256, 1024, each forward starting from a flushed L2.
 
 --impl reference times that CPU path alone (rank 0), as the reference arm.
 """
@@ -358,6 +361,9 @@ def run_gpu(args, rank, world, local_rank):
                              for k in ("route", "permute", "w13", "w2", "combine")}}
         if world == 1 and not args.no_sweep:
             sweep = m_sweep(layers, cfg)
+            if not N_EXPERTS:
+                sweep.update(cfg_sweep("c3", (1, 16, 64)))
+                sweep.update(cfg_sweep("c4", (256, 1024)))
     clocks = clk.summary(set(range(world)) if world > 1 else {local_rank}) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -418,6 +424,49 @@ def m_sweep(layers, cfg):
         f = sum(b[1] for b in nb) / len(nb) / t_fwd / 1e9
         out[f"c1_m{m}"] = {"tokens_per_s": m / t_fwd, "forward_us": t_fwd * 1e6, "grouped_gbs": g,
                            "grouped_frac": g / peak, "forward_gbs": f, "forward_frac": f / peak}
+    return out
+
+
+def cfg_sweep(name, ms, reps=4):
+    """One layer of config `name` (c3: FP8 experts, Zipf selection, no shared expert; c4: Kimi-K3-scale
+    NVFP4 prefill) at each M: every timed forward gets fresh tokens and starts with L2 flushed
+    (a 256 MB write outside the timed region), since a single layer's active experts can be close to
+    the 126 MB L2 at small M."""
+    from shard_b200 import synth as S
+    peak, _ = hbm_peak()
+    cfg = S.CONFIGS[name]
+    lay = S.device_layer(cfg, layer=0, device=torch.device("cuda", torch.cuda.current_device()), seeded=[],
+                         fill="normal")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=lay.device)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in evs:   # recorded once through torch, so torch accepts the C ABI's later records
+        e.record()
+    out = {}
+    for m in ms:
+        lay.reserve(m)
+        xs = [S.make_inputs(cfg, m, step=900 + r)[0].to(lay.device) for r in range(reps + 1)]
+        lay.forward(xs[-1])
+        t_fwd, rows = 0.0, []
+        for r in range(reps):
+            flush.fill_(r & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            lay.forward(xs[r])
+            e1.record()
+            torch.cuda.synchronize()
+            t_fwd += e0.elapsed_time(e1) / 1000.0 / reps
+            flush.fill_((r + 7) & 0xFF)
+            y, idx, t = lay.forward_profiled(xs[r], evs)
+            torch.cuda.synchronize()
+            rows.append((idx.cpu().numpy(), t))
+        nb = algorithmic_bytes(cfg, [r_[0] for r_ in rows], m)
+        g = sum(b[0] for b in nb) / sum(r_[1]["grouped"] for r_ in rows) / 1e9
+        f = sum(b[1] for b in nb) / len(nb) / t_fwd / 1e9
+        out[f"{name}_m{m}"] = {"tokens_per_s": m / t_fwd, "forward_us": t_fwd * 1e6, "grouped_gbs": g,
+                               "grouped_frac": g / peak, "forward_gbs": f, "forward_frac": f / peak,
+                               "l2": "flushed before each forward"}
+    del lay, flush
+    torch.cuda.empty_cache()
     return out
 
 

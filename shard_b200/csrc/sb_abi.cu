@@ -54,6 +54,8 @@ struct Workspace {
   __nv_bfloat16* o;
   __nv_bfloat16* hbf;  // tensor-core layout: h in bf16 (quantised per 128 K into the w2 panel)
   int32_t* pass_off;   // tensor-core layout: first pass of each active slot
+  int32_t* pass_slot;  //                     slot and first token of every routed pass
+  int32_t* pass_pb;
   uint8_t* bpanel;     // tensor-core layout: B tiles of every (pass, stage)
   float* apanel;       //                     and their row scales
   int n_sh_pass;
@@ -63,12 +65,14 @@ struct Workspace {
 // Tensor-core layout: passes of the shared expert (FP8, 16 tokens each).
 int64_t shared_passes(const sb_moe_layer* L, int64_t m) { return L->has_shared ? (m + 15) / 16 : 0; }
 
-// Upper bound of the passes of one grouped launch: sum over experts of ceil(count / pass_max)
-// <= P / pass_max + (active experts).
-int64_t max_passes(const sb_moe_layer* L, int64_t m) {
+// Upper bound of the routed passes of one grouped launch: sum over experts of
+// ceil(count / pass_max) <= P / pass_max + (active experts).
+int64_t max_routed_passes(const sb_moe_layer* L, int64_t m) {
   const int64_t P = m * L->topk, E = L->n_experts;
-  return shared_passes(L, m) + P / sb::tc_pass_max(L->expert_fmt) + (P < E ? P : E);
+  return P / sb::tc_pass_max(L->expert_fmt) + (P < E ? P : E);
 }
+
+int64_t max_passes(const sb_moe_layer* L, int64_t m) { return shared_passes(L, m) + max_routed_passes(L, m); }
 
 Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   Workspace w;
@@ -99,6 +103,8 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   w.o = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * H);
   w.hbf = (__nv_bfloat16*)take(tc ? sizeof(__nv_bfloat16) * R * I : 0);
   w.pass_off = (int32_t*)take(tc ? sizeof(int32_t) * (E + 1) : 0);
+  w.pass_slot = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
+  w.pass_pb = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
   const int64_t panel_tiles = tc ? max_passes(L, m) * ((H > I ? H : I) / 128) : 0;
   w.bpanel = take((size_t)panel_tiles * 2048);
   w.apanel = (float*)take((size_t)panel_tiles * 16 * sizeof(float));
@@ -295,12 +301,14 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
     plan.bpanel = bpanel;
     plan.apanel = apanel;
     plan.pass_off = nullptr;
+    plan.pass_slot = nullptr;
+    plan.pass_pb = nullptr;
     plan.n_sh_pass = pa.n_sh_pass;
     a.shared.s_stride = 0;
     a.routed = a.shared;
     a.err = err;
     a.items_per_expert = (int)(n / 128);
-    return cuda_check(sb::launch_tc_grouped(a, plan, a.items_per_expert, st), "qgemm");
+    return cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert, st), "qgemm");
   }
   a.items_per_expert = (int)((n + 255) / 256);
   return cuda_check(sb::launch_grouped(a, a.items_per_expert, 0, (cudaStream_t)stream), "qgemm");
@@ -388,6 +396,8 @@ int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, in
   plan.bpanel = bpanel;
   plan.apanel = apanel;
   plan.pass_off = nullptr;
+  plan.pass_slot = nullptr;
+  plan.pass_pb = nullptr;
   plan.n_sh_pass = pa.n_sh_pass;
   sb::GroupedArgs a;
   memset(&a, 0, sizeof a);
@@ -406,7 +416,7 @@ int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, in
   a.o = (__nv_bfloat16*)y;
   a.err = err;
   a.items_per_expert = (int)(n / 128);
-  return cuda_check(sb::launch_tc_grouped(a, plan, a.items_per_expert, st), "qgemm_static");
+  return cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert, st), "qgemm_static");
 }
 
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
@@ -491,6 +501,8 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.err = w.err;
   p.pass_max = L->layout == SB_LAYOUT_TC ? sb::tc_pass_max(L->expert_fmt) : 0;
   p.pass_off = L->layout == SB_LAYOUT_TC ? w.pass_off : nullptr;
+  p.pass_slot = w.pass_slot;
+  p.pass_pb = w.pass_pb;
   rc = cuda_check(sb::launch_permute(p, st), "permute");
   if (rc) return rc;
   mark(2);
@@ -519,6 +531,8 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     plan.bpanel = w.bpanel;
     plan.apanel = w.apanel;
     plan.pass_off = w.pass_off;
+    plan.pass_slot = w.pass_slot;
+    plan.pass_pb = w.pass_pb;
     plan.n_sh_pass = w.n_sh_pass;
     sb::PanelArgs pa;
     memset(&pa, 0, sizeof pa);
@@ -552,7 +566,8 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     g.hbf = w.hbf;
     g.n_experts = L->n_experts;
     g.items_per_expert = (int)(I / 64);
-    rc = cuda_check(sb::launch_tc_grouped(g, plan, n_units * g.items_per_expert, st), "tc w13");
+    const int64_t n_pass_max = max_passes(L, m);
+    rc = cuda_check(sb::launch_tc_grouped(g, plan, (int)(n_pass_max * g.items_per_expert), st), "tc w13");
     if (rc) return rc;
     mark(3);
     pa.mode = sb::MODE_W2;
@@ -566,7 +581,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     g.shared = shared_set(L, false);
     g.o = w.o;
     g.items_per_expert = (int)(H / 128);
-    rc = cuda_check(sb::launch_tc_grouped(g, plan, n_units * g.items_per_expert, st), "tc w2");
+    rc = cuda_check(sb::launch_tc_grouped(g, plan, (int)(n_pass_max * g.items_per_expert), st), "tc w2");
     if (rc) return rc;
   } else {
   // w13 (+ SwiGLU, + act_quant of h)

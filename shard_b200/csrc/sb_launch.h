@@ -37,6 +37,8 @@ struct PermuteArgs {
   int32_t* err;      // cleared here, before the grouped kernels run
   int pass_max;      // tensor-core path: tokens per pass of a routed expert (0: no pass table)
   int32_t* pass_off; // [E+1] by active slot: first pass of the slot, total passes at [n_active]
+  int32_t* pass_slot;// [routed passes] active slot of each pass
+  int32_t* pass_pb;  // [routed passes] first token (within its expert) of each pass
 };
 
 // One family of tiled weight matrices (one per expert, or a single matrix).
@@ -73,7 +75,7 @@ struct GroupedArgs {
   uint8_t* hq;         // W13 out: e4m3 h rows (stride I)
   float* hs;           // W13 out: h scales (stride I/128)
   __nv_bfloat16* o;    // W2 / DENSE out (bf16), row stride n_rows
-  int items_per_expert;
+  int items_per_expert;  // row blocks per weight matrix (items per pass, tensor-core path)
   int* err;            // device flag: set to 1 if a bounded wait gave up (must start at 0)
   __nv_bfloat16* hbf;  // tensor-core path: h in bf16 (W13 writes it, the W2 panel quantises it)
   int n_experts;       // tensor-core path: matrices in the routed bank
@@ -88,6 +90,8 @@ struct TcPlan {
   const uint8_t* bpanel;    // [pass][stage][16 rows][128 B] e4m3, 128-byte swizzled
   const float* apanel;      // [pass][stage][16] activation scale of each B row (0 for empty rows)
   const int32_t* pass_off;  // [E+1] by active slot (routed passes follow the n_sh_pass shared ones)
+  const int32_t* pass_slot; // [routed passes] active slot of each routed pass
+  const int32_t* pass_pb;   // [routed passes] first token of each routed pass within its expert
   int n_sh_pass;
 };
 

@@ -397,7 +397,14 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
     a.counts[e] = c;
     cursor[e] = off;
     if (flag) a.active[fbase + fincl - 1] = e;
-    if (flag && a.pass_off) a.pass_off[fbase + fincl - 1] = pbase + pincl - np;
+    if (flag && a.pass_off) {
+      const int slot = fbase + fincl - 1, p0 = pbase + pincl - np;
+      a.pass_off[slot] = p0;
+      for (int i = 0; i < np; ++i) {   // the pass table: every routed pass's slot and first token
+        a.pass_slot[p0 + i] = slot;
+        a.pass_pb[p0 + i] = i * a.pass_max;
+      }
+    }
     if (e == E - 1) {
       a.offsets[E] = base + incl;
       *a.n_active = fbase + fincl;

@@ -169,25 +169,32 @@ __device__ __forceinline__ bool workers_any(bool pred) {
   return r != 0;
 }
 
+// An ITEM is one pass (up to 16 B rows of one expert's tokens) over one 128-row block of a weight
+// matrix. Items are numbered pass-major: item = pass * nrb + rb, passes being the shared expert's
+// (or the dense matrix's) first, then each active expert's in slot order, so a hot expert's passes
+// run on different CTAs at about the same time and share its weight tiles through L2.
 struct Item {
-  int shared, expert, slot, rb, cnt, base;
+  int shared, expert, rb, cnt, base, pb, pass;
 };
 
-__device__ __forceinline__ Item item_of(const GroupedArgs& a, int item, int n_sh) {
+template <int FMT_R>
+__device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan, int item, int nrb) {
   Item it;
-  if (item < n_sh) {
+  const int p = item / nrb;
+  it.rb = item - p * nrb;
+  it.pass = p;
+  if (p < plan.n_sh_pass) {
     it.shared = 1;
     it.expert = 0;
-    it.slot = 0;
-    it.rb = item;
     it.cnt = a.m;
     it.base = 0;
+    it.pb = p * tc_pass_max(a.mode == MODE_DENSE ? FMT_R : FMT_FP8);
   } else {
-    const int r = item - n_sh;
+    const int q = p - plan.n_sh_pass;
+    const int slot = plan.pass_slot[q];
     it.shared = 0;
-    it.slot = r / a.items_per_expert;
-    it.expert = a.active[it.slot];
-    it.rb = r % a.items_per_expert;
+    it.pb = plan.pass_pb[q];
+    it.expert = a.active[slot];
     it.cnt = a.counts[it.expert];
     it.base = a.offsets[it.expert];
   }
@@ -244,17 +251,17 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   pdl_wait();
   pdl_trigger();
 
-  const int n_sh = a.has_shared ? a.items_per_expert : 0;
-  const int n_items = n_sh + (a.mode == MODE_DENSE ? 0 : (*a.n_active) * a.items_per_expert);
   const int P = a.m * a.topk;
   const int K = a.k;
   const int nst = K / 128;
   const int nrb = a.n_rows / 128;
+  const int n_pass = (a.has_shared ? ta.plan.n_sh_pass : 0) +
+                     (a.mode == MODE_DENSE ? 0 : ta.plan.pass_off[*a.n_active]);
+  const int n_items = n_pass * nrb;
   const bool w13 = a.mode == MODE_W13;
 
   // per-item constants shared by the roles
   auto item_fmt = [&](const Item& it) { return it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R; };
-  auto first_pass = [&](const Item& it) { return it.shared ? 0 : ta.plan.n_sh_pass + ta.plan.pass_off[it.slot]; };
 
   // Stages are grouped in UNITS of up to UNIT consecutive stages of one pass: one side-ring slot
   // (scales), one accumulator group and one readback per unit. g counts stages, u units.
@@ -268,30 +275,24 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     uint32_t g = 0, u = 0;
     bool ok = true;
     // the next item's descriptor is loaded one item ahead, so its global loads overlap this item
-    Item nxt = blockIdx.x < n_items ? item_of(a, blockIdx.x, n_sh) : Item{};
-    int nxt_pass0 = blockIdx.x < n_items ? first_pass(nxt) : 0;
+    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item it = nxt;
-      const int pass0 = nxt_pass0;
-      if (item + (int)gridDim.x < n_items) {
-        nxt = item_of(a, item + gridDim.x, n_sh);
-        nxt_pass0 = first_pass(nxt);
-      }
+      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb);
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const CUtensorMap* map = it.shared ? &ta.map_shared : &ta.map_routed;
-      const int pm = tc_pass_max(fmt);
       const uint32_t abytes = fmt == FMT_FP8 ? 16384u : 8192u;
       const uint32_t sb = stage_sbytes(fmt);
       const int row0 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;
       const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)it.rb * nst * sb;
-      for (int pb = 0, pi = 0; pb < it.cnt && ok; pb += pm, ++pi) {
+      {
         if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(err) != 0)) {
           set_abort(sm, err, false);
           ok = false;
           break;
         }
-        const size_t pst = (size_t)(pass0 + pi) * nst;
+        const size_t pst = (size_t)it.pass * nst;
         for (int j = 0; j < nst && ok; j += UNIT, ++u) {
           const int ns = min(UNIT, nst - j);
           const uint32_t us = u % SS;
@@ -335,14 +336,13 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     // the whole warp runs the loop (uniform control flow); one elected lane issues MMAs and commits
     uint32_t g = 0, u = 0;
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of(a, blockIdx.x, n_sh) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of(a, item + gridDim.x, n_sh);
+      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb);
       const int fmt = item_fmt(it);
-      const int pm = tc_pass_max(fmt);
       const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
-      for (int pb = 0; pb < it.cnt && ok; pb += pm) {
+      {
         for (int j = 0; j < nst && ok; j += UNIT, ++u) {
           const int ns = min(UNIT, nst - j);
           const uint32_t q = u % SA;
@@ -389,10 +389,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     const int r = tid;  // weight row of the item = TMEM lane
     uint32_t u = 0;
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of(a, blockIdx.x, n_sh) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of(a, item + gridDim.x, n_sh);
+      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb);
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pm = tc_pass_max(fmt);
@@ -404,7 +404,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         ts = (w13 && r >= 64) ? tsp[1] : tsp[0];
       }
       bool stop = false;
-      for (int pb = 0; pb < it.cnt; pb += pm) {
+      {
+        const int pb = it.pb;
         const int pc = min(pm, it.cnt - pb);
         const int ncol = nv ? 2 * pc : pc;     // used columns of each chunk slot
         const bool narrow = ncol <= 4;
@@ -580,45 +581,44 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
           if (lane == 0) arrive(smem_addr(&sm.sempty[us]));
         }
         // one decision for all workers: the W13 epilogue below synchronises them
-        if (workers_any(!ok || aborted(sm))) {
-          stop = true;
-          break;
-        }
-        if (w13) {
-          // rows r < 64 are w1 (gate) rows, r >= 64 the matching w3 (up) rows
-          const int I = a.n_rows / 2;
-          if (r >= 64) {
+        if (workers_any(!ok || aborted(sm))) stop = true;
+        if (!stop) {
+          if (w13) {
+            // rows r < 64 are w1 (gate) rows, r >= 64 the matching w3 (up) rows
+            const int I = a.n_rows / 2;
+            if (r >= 64) {
 #pragma unroll
-            for (int t = 0; t < 16; ++t) sm.xchg[r - 64][t] = bf16_round(acc[t] * ts);
-          }
-          asm volatile("bar.sync 1, 128;\n" ::: "memory");
-          if (r < 64) {
-            const float lim = a.swiglu_limit;
+              for (int t = 0; t < 16; ++t) sm.xchg[r - 64][t] = bf16_round(acc[t] * ts);
+            }
+            asm volatile("bar.sync 1, 128;\n" ::: "memory");
+            if (r < 64) {
+              const float lim = a.swiglu_limit;
+#pragma unroll
+              for (int t = 0; t < 16; ++t) {
+                if (t < pc) {
+                  const int orow = __shfl_sync(0xffffffffu, my_orow, t);
+                  const float wgt = __shfl_sync(0xffffffffu, my_wgt, t);
+                  float gv = bf16_round(acc[t] * ts);
+                  float uv = sm.xchg[r][t];
+                  if (lim > 0.f) {
+                    uv = fminf(fmaxf(uv, -lim), lim);
+                    gv = fminf(gv, lim);
+                  }
+                  float h = silu(gv) * uv;
+                  if (!it.shared) h = wgt * h;
+                  a.hbf[(size_t)orow * I + it.rb * 64 + r] = __float2bfloat16_rn(h);
+                }
+              }
+            }
+            asm volatile("bar.sync 1, 128;\n" ::: "memory");   // xchg is rewritten by the next pass
+          } else {
+            const int n0 = it.rb * 128;
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
               if (t < pc) {
                 const int orow = __shfl_sync(0xffffffffu, my_orow, t);
-                const float wgt = __shfl_sync(0xffffffffu, my_wgt, t);
-                float gv = bf16_round(acc[t] * ts);
-                float uv = sm.xchg[r][t];
-                if (lim > 0.f) {
-                  uv = fminf(fmaxf(uv, -lim), lim);
-                  gv = fminf(gv, lim);
-                }
-                float h = silu(gv) * uv;
-                if (!it.shared) h = wgt * h;
-                a.hbf[(size_t)orow * I + it.rb * 64 + r] = __float2bfloat16_rn(h);
+                a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(acc[t] * ts);
               }
-            }
-          }
-          asm volatile("bar.sync 1, 128;\n" ::: "memory");   // xchg is rewritten by the next pass
-        } else {
-          const int n0 = it.rb * 128;
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            if (t < pc) {
-              const int orow = __shfl_sync(0xffffffffu, my_orow, t);
-              a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(acc[t] * ts);
             }
           }
         }
