@@ -269,7 +269,7 @@ def run_gpu(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     cfg, layers = build_layers(rank, LAYERS_PER_GPU, device)
-    pipe = Pipeline(StageStack(layers), HEADLINE_M, cfg.hidden, rank, world, device)
+    pipe = Pipeline(StageStack(layers), HEADLINE_M, cfg.hidden, rank, world, device, wire=args.wire)
     C = CHUNKS_PER_STEP
     xs_dev = chunk_inputs(cfg, C, device) if rank == 0 else None
     outs_dev = [torch.empty(HEADLINE_M, cfg.hidden, dtype=torch.bfloat16, device=device) for _ in range(C)] \
@@ -381,7 +381,7 @@ def run_gpu(args, rank, world, local_rank):
                            "routed_fmt": "nvfp4", "shared_fmt": "fp8-128x128",
                            "kernels": "tcgen05" if layers[0].layout == 1 else "mma.sync",
                            "l2": "no flush: each step streams >1 GB of distinct expert weights per layer (L2 126 MB)",
-                           "parallelism": f"pp{world}"},
+                           "parallelism": f"pp{world}", "wire": args.wire},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": bytes_io,
                         "d2h_bytes_per_step": bytes_io},
                 "gpu_launches": args.steps * C * LAYERS_PER_GPU * 6 * world,
@@ -483,6 +483,8 @@ def main():
                     help="layers per GPU (a smaller stack is the small case for ncu captures)")
     ap.add_argument("--experts", type=int, default=None,
                     help="routed experts per layer (default c1's 256; fewer is the small case for ncu captures)")
+    ap.add_argument("--wire", choices=["bf16", "fp8"], default="bf16",
+                    help="stage-boundary activation wire at N > 1 (fp8: the reference's e4m3 + per-row scale)")
     ap.add_argument("--layout", choices=["tc", "fragment"], default=None,
                     help="weight layout / kernel family (default: the library default)")
     args = ap.parse_args()

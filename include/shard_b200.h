@@ -155,6 +155,20 @@ int sb_moe_forward_profiled(const sb_moe_layer* layer, const void* x, int64_t m,
                             void* y, float* out_weights, int64_t* out_indices, void* workspace,
                             size_t workspace_bytes, void* stream, void* const* events);
 
+/* sb_moe_forward whose last step also emits the stage-boundary FP8 wire form of y (the combine with
+ * the pack fused in; the pack is sb_wire_pack's): q e4m3 [M, H], scale bf16 [M]. y may be NULL when
+ * only the wire form is needed. hidden <= 8192. */
+int sb_moe_forward_wire(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
+                        void* q, void* scale, float* out_weights, int64_t* out_indices, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* ── the stage-boundary FP8 wire (engines/deepseek_v4/v4_pipe.py:335-384, _pack_t / _unpack_t) ─── */
+/* pack: x bf16 [rows, dim] -> q e4m3 [rows, dim], scale bf16 [rows]; one scale per row:
+ * bf16(clamp(amax / 448, 1e-8, bf16 max)), q = e4m3(clamp(x / scale, +-448)). dim % 8 == 0. */
+int sb_wire_pack(const void* x, int64_t rows, int64_t dim, void* q, void* scale, void* stream);
+/* unpack: y bf16 [rows, dim] = bf16(e4m3(q) * scale). */
+int sb_wire_unpack(const void* q, const void* scale, int64_t rows, int64_t dim, void* y, void* stream);
+
 /* Routing alone (Gate.forward, model.py:569-589): weights fp32 [M, k], indices int64 [M, k]. */
 int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,
                  float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes,

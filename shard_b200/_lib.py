@@ -59,6 +59,10 @@ SIGNATURES = {
     "sb_moe_forward_profiled": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp,
                                         ctypes.POINTER(_vp)]),
     "sb_moe_route": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "sb_moe_forward_wire": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                                   _vp]),
+    "sb_wire_pack": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "sb_wire_unpack": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "sb_selftest_formats": (_int, [_vp, _vp]),
 }
 

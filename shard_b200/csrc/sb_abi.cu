@@ -466,7 +466,7 @@ int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int6
 
 static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
                         float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes,
-                        void* stream, void* const* events) {
+                        void* stream, void* const* events, void* wire_q = nullptr, void* wire_s = nullptr) {
   cudaStream_t st = (cudaStream_t)stream;
   auto mark = [&](int i) {
     if (events && events[i]) cudaEventRecord((cudaEvent_t)events[i], st);
@@ -474,8 +474,10 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   int rc = check_layer(layer);
   if (rc) return rc;
   const sb_moe_layer* L = layer;
-  if (!x || !y) return fail(SB_ERR_ARG, "x or y is NULL");
-  if (!aligned16(x) || !aligned16(y)) return fail(SB_ERR_ARG, "x and y must be 16-byte aligned");
+  if (!x || (!y && !wire_q)) return fail(SB_ERR_ARG, "x or y is NULL");
+  if (!aligned16(x) || !aligned16(y) || !aligned16(wire_q)) return fail(SB_ERR_ARG, "x, y and q must be 16-byte aligned");
+  if (wire_q && (!wire_s || layer->hidden > 8192))
+    return fail(SB_ERR_SHAPE, "wire output needs a scale buffer and hidden <= 8192 (hidden=%d)", layer->hidden);
   if (m < 0 || m > (1 << 20)) return fail(SB_ERR_SHAPE, "m=%lld outside 0..2^20", (long long)m);
   if (m == 0) return SB_OK;
   if (L->tid2eid && !input_ids) return fail(SB_ERR_ARG, "hash routing needs input_ids");
@@ -612,9 +614,14 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   if (rc) return rc;
   }
   mark(4);
-  rc = cuda_check(sb::launch_combine(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
-                                     (__nv_bfloat16*)y, st),
-                  "combine");
+  if (wire_q)
+    rc = cuda_check(sb::launch_combine_pack(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
+                                            (__nv_bfloat16*)y, (uint8_t*)wire_q, (__nv_bfloat16*)wire_s, st),
+                    "combine+pack");
+  else
+    rc = cuda_check(sb::launch_combine(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
+                                       (__nv_bfloat16*)y, st),
+                    "combine");
   if (rc) return rc;
   mark(5);
   return SB_OK;
@@ -631,6 +638,34 @@ int sb_moe_forward_profiled(const sb_moe_layer* layer, const void* x, int64_t m,
                             void* stream, void* const* events) {
   return forward_impl(layer, x, m, input_ids, y, out_weights, out_indices, workspace, workspace_bytes, stream,
                       events);
+}
+
+int sb_moe_forward_wire(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
+                        void* q, void* scale, float* out_weights, int64_t* out_indices, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!q) return fail(SB_ERR_ARG, "q is NULL");
+  return forward_impl(layer, x, m, input_ids, y, out_weights, out_indices, workspace, workspace_bytes, stream, nullptr,
+                      q, scale);
+}
+
+int sb_wire_pack(const void* x, int64_t rows, int64_t dim, void* q, void* scale, void* stream) {
+  if (!x || !q || !scale) return fail(SB_ERR_ARG, "wire_pack: NULL pointer");
+  if (rows < 0 || rows > (1 << 30) || dim <= 0 || dim % 8)
+    return fail(SB_ERR_SHAPE, "wire_pack: need rows >= 0 and dim a positive multiple of 8 (rows=%lld dim=%lld)",
+                (long long)rows, (long long)dim);
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(SB_ERR_ARG, "wire_pack: x 16-byte, q 8-byte aligned");
+  if (rows == 0) return SB_OK;
+  return cuda_check(sb::launch_wire_pack(x, rows, dim, (uint8_t*)q, scale, (cudaStream_t)stream), "wire_pack");
+}
+
+int sb_wire_unpack(const void* q, const void* scale, int64_t rows, int64_t dim, void* y, void* stream) {
+  if (!q || !scale || !y) return fail(SB_ERR_ARG, "wire_unpack: NULL pointer");
+  if (rows < 0 || rows > (1 << 30) || dim <= 0 || dim % 8)
+    return fail(SB_ERR_SHAPE, "wire_unpack: need rows >= 0 and dim a positive multiple of 8 (rows=%lld dim=%lld)",
+                (long long)rows, (long long)dim);
+  if (!aligned16(y) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(SB_ERR_ARG, "wire_unpack: y 16-byte, q 8-byte aligned");
+  if (rows == 0) return SB_OK;
+  return cuda_check(sb::launch_wire_unpack((const uint8_t*)q, scale, rows, dim, y, (cudaStream_t)stream), "wire_unpack");
 }
 
 int sb_selftest_formats(float* out, void* stream) {

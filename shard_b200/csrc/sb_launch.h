@@ -129,6 +129,10 @@ cudaError_t launch_tile_scales(int fmt, int kind, const void* src, void* dst, in
 cudaError_t launch_selftest(float* out, cudaStream_t st);
 cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st);
 cudaError_t launch_tc_grouped(const GroupedArgs& a, const TcPlan& plan, int max_items, cudaStream_t st);
+cudaError_t launch_wire_pack(const void* x, int64_t rows, int64_t dim, uint8_t* q, void* s, cudaStream_t st);
+cudaError_t launch_wire_unpack(const uint8_t* q, const void* s, int64_t rows, int64_t dim, void* y, cudaStream_t st);
+cudaError_t launch_combine_pack(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h,
+                                int has_shared, __nv_bfloat16* y, uint8_t* q, __nv_bfloat16* s, cudaStream_t st);
 cudaError_t launch_tc_tile(int fmt, int kind, bool scales, const void* src, void* dst, int64_t n_mat, int64_t n,
                            int64_t k, cudaStream_t st);
 

@@ -161,6 +161,24 @@ class MoELayer:
 
     __call__ = forward
 
+    def forward_wire(self, x: torch.Tensor, input_ids: Optional[torch.Tensor] = None, y: Optional[torch.Tensor] = None,
+                     stream=None):
+        """forward() that emits the stage-boundary FP8 wire form of its output (the combine with the
+        pack fused in): returns (q e4m3 [M, H], scale bf16 [M]); y, when given, also receives the
+        bf16 output. The same bytes as shard_b200.wire.pack(forward(x))."""
+        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] == self.hidden
+        x = x.contiguous()
+        m = x.shape[0]
+        q = torch.empty(m, self.hidden, dtype=torch.float8_e4m3fn, device=x.device)
+        s = torch.empty(m, dtype=torch.bfloat16, device=x.device)
+        ws = self.reserve(m)
+        ids = None
+        if self.tid2eid is not None:
+            ids = input_ids.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
+        check(lib().sb_moe_forward_wire(ctypes.byref(self.desc), ptr(x), m, ptr(ids), ptr(y), ptr(q), ptr(s), None,
+                                        None, ptr(ws), ws.numel(), stream_ptr(stream)), "sb_moe_forward_wire")
+        return q, s
+
     def forward_profiled(self, x: torch.Tensor, events, input_ids: Optional[torch.Tensor] = None):
         """forward() with CUDA events between its launches (six torch.cuda.Event(enable_timing=True),
         each already recorded once so it exists). Synchronises; returns (y, top-k indices,

@@ -7,6 +7,10 @@ Here each stage is one rank of a torch.distributed NCCL group, and the hop is an
 the bf16 activation [M, H] device to device over NVLink. Several verify chunks stream through the
 stages back to back, so stage r works on chunk j while stage r+1 works on chunk j-1; each hop is
 enqueued without a host sync (the host runs ahead and the streams order the work).
+
+With wire="fp8" a hop carries the reference's FP8 activation wire instead (v4_pipe.py:320-384:
+e4m3 + one bf16 scale per row, half the bytes): the stage's last MoE layer emits it from its combine
+kernel (MoELayer.forward_wire) and the next stage unpacks it before its first layer.
 """
 from __future__ import annotations
 
@@ -42,18 +46,40 @@ class StageStack:
 
     __call__ = forward
 
+    def forward_wire(self, x: torch.Tensor, pack):
+        """The stack's output in the FP8 wire form: the last layer emits it directly when it can,
+        otherwise `pack` is applied to the output."""
+        for layer in self.layers[:-1]:
+            x = layer.forward(x)
+        last = self.layers[-1] if self.layers else None
+        if last is not None and hasattr(last, "forward_wire"):
+            return last.forward_wire(x)
+        return pack(last.forward(x) if last is not None else x)
+
 
 class Pipeline:
     """One rank's view of the pipeline: receive a chunk from the previous stage (or take it from the
     caller on stage 0), run the stage's layers, send it on (or hand it back on the last stage)."""
 
     def __init__(self, stack: StageStack, m: int, hidden: int, rank: int = 0, world: int = 1,
-                 device: Optional[torch.device] = None, depth: int = 4):
+                 device: Optional[torch.device] = None, depth: int = 4, wire: str = "bf16", codec=None):
+        """wire: "bf16" or "fp8". codec: (pack, unpack) for the fp8 wire; shard_b200.wire's CUDA
+        codec by default."""
+        assert wire in ("bf16", "fp8")
         self.stack, self.m, self.hidden = stack, m, hidden
         self.rank, self.world = rank, world
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.depth = depth
+        self.wire = wire
+        if wire == "fp8" and codec is None:
+            from . import wire as _wire
+            codec = (_wire.pack, _wire.unpack)
+        self.codec = codec
         self.recv_bufs = [torch.empty(m, hidden, dtype=torch.bfloat16, device=self.device) for _ in range(depth)]
+        if wire == "fp8":
+            # the wire travels as raw bytes: e4m3 codes and bf16 scale bits
+            self.recv_q = [torch.empty(m, hidden, dtype=torch.uint8, device=self.device) for _ in range(depth)]
+            self.recv_s = [torch.empty(2 * m, dtype=torch.uint8, device=self.device) for _ in range(depth)]
         self._slot = 0
 
     @property
@@ -69,10 +95,21 @@ class Pipeline:
         if self.first:
             assert x is not None
             h = x
+        elif self.wire == "fp8":
+            q, s = self.recv_q[self._slot], self.recv_s[self._slot]
+            self._slot = (self._slot + 1) % self.depth
+            dist.recv(q, src=self.rank - 1)
+            dist.recv(s, src=self.rank - 1)
+            h = self.codec[1](q.view(torch.float8_e4m3fn), s.view(torch.bfloat16))
         else:
             h = self.recv_bufs[self._slot]
             self._slot = (self._slot + 1) % self.depth
             dist.recv(h, src=self.rank - 1)
+        if not self.last and self.wire == "fp8":
+            q, s = self.stack.forward_wire(h, self.codec[0])
+            dist.send(q.view(torch.uint8), dst=self.rank + 1)
+            dist.send(s.contiguous().view(torch.uint8), dst=self.rank + 1)
+            return None
         y = self.stack(h)
         if not self.last:
             dist.send(y, dst=self.rank + 1)

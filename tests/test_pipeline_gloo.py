@@ -49,14 +49,45 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, out_path):
+def _oracle_codec():
+    """The FP8 wire on the host for these CPU stages: the oracle's restatement of the reference
+    codec (the product codec is CUDA-only)."""
+    from oracle import wire_oracle as W
+
+    def pack(t):
+        q, s = W.pack(t.float().numpy())
+        return torch.from_numpy(q).view(torch.float8_e4m3fn), torch.from_numpy(s).to(torch.bfloat16)
+
+    def unpack(q, s):
+        return torch.from_numpy(W.unpack(q.view(torch.uint8).numpy(), s.float().numpy())).to(torch.bfloat16)
+
+    return pack, unpack
+
+
+def _expected_fp8(world):
+    """The whole stack with every stage boundary passing through the wire codec."""
+    pack, unpack = _oracle_codec()
+    blocks = even_tiling(N_LAYERS, world)
+    outs = []
+    for x in _inputs():
+        for b, block in enumerate(blocks):
+            for l in block:
+                x = Affine(l).forward(x)
+            if b < len(blocks) - 1:
+                x = unpack(*pack(x))
+        outs.append(x)
+    return outs
+
+
+def _rank_main(rank, world, port, out_path, wire="bf16"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         block = even_tiling(N_LAYERS, world)[rank]
-        pipe = Pipeline(StageStack([Affine(l) for l in block]), M, HIDDEN, rank, world, torch.device("cpu"))
+        pipe = Pipeline(StageStack([Affine(l) for l in block]), M, HIDDEN, rank, world, torch.device("cpu"),
+                        wire=wire, codec=_oracle_codec() if wire == "fp8" else None)
         chunks = _inputs() if rank == 0 else None
         outs = [torch.empty(M, HIDDEN, dtype=torch.bfloat16) for _ in range(CHUNKS)] if rank == world - 1 else None
         pipe.run(CHUNKS, chunks, outs)
@@ -90,3 +121,17 @@ def test_two_stage_gloo_pipeline_matches_the_whole_stack(world):
         got = torch.load(out_path)
     for g, e in zip(got, _expected()):
         assert torch.equal(g, e)
+
+
+def test_two_stage_gloo_pipeline_with_the_fp8_wire():
+    """The hop carries e4m3 codes + bf16 scale bits; the result equals the stack with the codec
+    applied at the stage boundary, and differs from the bf16 wire (the codec is lossy)."""
+    with tempfile.TemporaryDirectory() as d:
+        out_path = os.path.join(d, "outs.pt")
+        mp.start_processes(_rank_main, args=(2, _free_port(), out_path, "fp8"), nprocs=2, join=True,
+                           start_method="spawn")
+        got = torch.load(out_path)
+    exp = _expected_fp8(2)
+    for g, e in zip(got, exp):
+        assert torch.equal(g, e)
+    assert any(not torch.equal(g, e) for g, e in zip(got, _expected()))
