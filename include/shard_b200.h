@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define SB_ABI_VERSION 3
+#define SB_ABI_VERSION 4
 
 enum sb_status {
   SB_OK = 0,
@@ -93,6 +93,13 @@ typedef struct sb_moe_layer {
   const void* sh_w2;
   const void* sh_w2_s;
   int32_t layout;        /* sb_layout of every weight above */
+  /* Router variants of other engines' MoE call sites (0 = the V4 Gate.forward):
+   * logits_bf16  round the fp32 router logits to bf16 before scoring (a bf16 F.linear router,
+   *              engines/minimax_m25/m25_stage.py:412-416)
+   * no_renorm    keep the selected sigmoid/sqrtsoftplus weights un-normalised (FusedMoE
+   *              renormalize=False, m25_stage.py:301) */
+  int32_t logits_bf16;
+  int32_t no_renorm;
 } sb_moe_layer;
 
 /* ── introspection ───────────────────────────────────────────────────────────────────────────── */

@@ -148,11 +148,17 @@ def _sigmoid(x):
     return (np.float32(1.0) / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
 
 
-def gate(x: np.ndarray, w: np.ndarray, bias, score_func: str, route_scale: float, topk: int):
+def gate(x: np.ndarray, w: np.ndarray, bias, score_func: str, route_scale: float, topk: int,
+         logits_bf16: bool = False, renormalize: bool = True):
     """Gate.forward (model.py:569-589): fp32 logits, score, bias for selection only, sorted top-k,
     weights gathered from the unbiased scores, renormalised unless softmax, times route_scale.
-    Ties in the biased score go to the lower expert id."""
+    Ties in the biased score go to the lower expert id.
+
+    logits_bf16 / renormalize=False restate the MiniMax-M2.5 router (engines/minimax_m25/
+    m25_stage.py:412-416: a bf16 F.linear; :299-303: FusedMoE renormalize=norm_topk_prob)."""
     logits = (x.astype(np.float32) @ w.astype(np.float32).T).astype(np.float32)
+    if logits_bf16:
+        logits = bf16_round(logits)
     if score_func == "softmax":
         z = logits - logits.max(-1, keepdims=True)
         ez = np.exp(z).astype(np.float32)
@@ -167,7 +173,7 @@ def gate(x: np.ndarray, w: np.ndarray, bias, score_func: str, route_scale: float
     order = np.lexsort((np.broadcast_to(np.arange(e), sel.shape), -sel), axis=-1)
     idx = order[:, :topk].astype(np.int64)
     wts = np.take_along_axis(scores, idx, axis=-1).astype(np.float32)
-    if score_func != "softmax":
+    if score_func != "softmax" and renormalize:
         wts = (wts / wts.sum(-1, keepdims=True)).astype(np.float32)
     wts = (wts * np.float32(route_scale)).astype(np.float32)
     return wts, idx, logits
@@ -210,13 +216,15 @@ class OracleLayer:
     can materialise only the experts a batch routes to."""
 
     def __init__(self, *, hidden, inter, topk, score_func, route_scale, swiglu_limit, expert_fmt,
-                 gate_w, gate_b, expert, shared=None, shared_fmt=FMT_FP8, pow2=True):
+                 gate_w, gate_b, expert, shared=None, shared_fmt=FMT_FP8, pow2=True, logits_bf16=False,
+                 renormalize=True):
         self.hidden, self.inter, self.topk = hidden, inter, topk
         self.score_func, self.route_scale, self.swiglu_limit = score_func, route_scale, swiglu_limit
         self.expert_fmt, self.shared_fmt = expert_fmt, shared_fmt
         self.gate_w, self.gate_b = gate_w, gate_b
         self.expert, self.shared = expert, shared
         self.pow2 = pow2
+        self.logits_bf16, self.renormalize = logits_bf16, renormalize
 
 
 def moe_forward(layer: OracleLayer, x: np.ndarray, workers: int = 1):
@@ -225,7 +233,8 @@ def moe_forward(layer: OracleLayer, x: np.ndarray, workers: int = 1):
     Returns (y [M, H] fp32 on the bf16 grid, routing weights [M, k], indices [M, k]).
     Duplicate ids in one row (hash layers) follow the reference's `y[idx] +=` semantics: the last
     slot naming an expert wins, the earlier ones are dropped."""
-    wts, idx, _ = gate(x, layer.gate_w, layer.gate_b, layer.score_func, layer.route_scale, layer.topk)
+    wts, idx, _ = gate(x, layer.gate_w, layer.gate_b, layer.score_func, layer.route_scale, layer.topk,
+                       getattr(layer, "logits_bf16", False), getattr(layer, "renormalize", True))
     y = np.zeros_like(x, dtype=np.float32)
     experts = sorted(set(idx.ravel().tolist()))
 

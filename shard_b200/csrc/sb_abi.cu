@@ -440,6 +440,8 @@ static int route_impl(const sb_moe_layer* L, const void* x, int64_t m, const int
   r.act_pow2 = L->act_pow2;
   r.hidden = L->hidden;
   r.route_scale = L->route_scale;
+  r.logits_bf16 = L->logits_bf16;
+  r.no_renorm = L->no_renorm;
   r.topk_idx = w.topk_idx;
   r.topk_w = w.topk_w;
   r.out_idx = out_idx;

@@ -15,6 +15,7 @@ struct RouteArgs {
   const int32_t* tid2eid;    // [vocab, K] or null
   const int64_t* input_ids;  // [M] (hash routing)
   int m, n_experts, topk, score_func, act_pow2, hidden;
+  int logits_bf16, no_renorm;  // router variants: bf16-rounded logits, no renormalisation
   float route_scale;
   int32_t* topk_idx;         // [M, K]
   float* topk_w;             // [M, K]

@@ -191,8 +191,10 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
         if (ks0 + u < nsplit) sc[i] = (ks0 + u == 0) ? pv[u][i] : sc[i] + pv[u][i];
   }
 #pragma unroll
-  for (int i = 0; i < SPL; ++i)
+  for (int i = 0; i < SPL; ++i) {
+    if (a.logits_bf16) sc[i] = bf16_round(sc[i]);   // a bf16 router GEMM's output
     if (lane + 32 * i >= E) sc[i] = -INFINITY;
+  }
   if (a.score_func == SCORE_SOFTMAX) {
     float mx = -INFINITY;
 #pragma unroll
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
       }
     }
   }
-  if (a.score_func != SCORE_SOFTMAX) {
+  if (a.score_func != SCORE_SOFTMAX && !a.no_renorm) {
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 16; ++j)

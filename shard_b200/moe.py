@@ -64,7 +64,8 @@ class MoELayer:
 
     def __init__(self, *, hidden, inter, n_experts, topk, expert_fmt, gate_w, gate_bias=None, tid2eid=None,
                  score_func="sigmoid", route_scale=1.0, swiglu_limit=0.0, act_pow2=True,
-                 w13, w13_s, w13_ts=None, w2, w2_s, w2_ts=None, shared=None, tiled=False, layout=None):
+                 w13, w13_s, w13_ts=None, w2, w2_s, w2_ts=None, shared=None, tiled=False, layout=None,
+                 logits_bf16=False, renormalize=True):
         self.hidden, self.inter, self.n_experts, self.topk = hidden, inter, n_experts, topk
         self.layout = DEFAULT_LAYOUT if layout is None else layout
         self.expert_fmt = expert_fmt
@@ -107,6 +108,8 @@ class MoELayer:
         if self.shared is not None:
             d.sh_w13, d.sh_w13_s, d.sh_w2, d.sh_w2_s = (ptr(t) for t in self.shared)
         d.layout = self.layout
+        d.logits_bf16 = 1 if logits_bf16 else 0
+        d.no_renorm = 0 if renormalize else 1
         self._ws = None
         self.score_func, self.route_scale, self.swiglu_limit, self.act_pow2 = score_func, route_scale, swiglu_limit, act_pow2
 
