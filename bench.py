@@ -363,7 +363,7 @@ def run_gpu(args, rank, world, local_rank):
             sweep = m_sweep(layers, cfg)
             if not N_EXPERTS:
                 sweep.update(cfg_sweep("c3", (1, 16, 64)))
-                sweep.update(cfg_sweep("c4", (256, 1024)))
+                sweep.update(cfg_sweep("c4", (256, 1024), modes=(0, 1)))
     clocks = clk.summary(set(range(world)) if world > 1 else {local_rank}) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -427,11 +427,12 @@ def m_sweep(layers, cfg):
     return out
 
 
-def cfg_sweep(name, ms, reps=4):
+def cfg_sweep(name, ms, reps=4, modes=(0,)):
     """One layer of config `name` (c3: FP8 experts, Zipf selection, no shared expert; c4: Kimi-K3-scale
     NVFP4 prefill) at each M: every timed forward gets fresh tokens and starts with L2 flushed
     (a 256 MB write outside the timed region), since a single layer's active experts can be close to
-    the 126 MB L2 at small M."""
+    the 126 MB L2 at small M. modes: expert-kernel choices timed (0 the default choice, keyed
+    `<name>_m<M>`; 1 the verify kernel and 2 the prefill kernel, keyed with a suffix)."""
     from shard_b200 import synth as S
     peak, _ = hbm_peak()
     cfg = S.CONFIGS[name]
@@ -442,7 +443,8 @@ def cfg_sweep(name, ms, reps=4):
     for e in evs:   # recorded once through torch, so torch accepts the C ABI's later records
         e.record()
     out = {}
-    for m in ms:
+    for m, mode in [(m, mode) for m in ms for mode in modes]:
+        lay.prefill = mode
         lay.reserve(m)
         xs = [S.make_inputs(cfg, m, step=900 + r)[0].to(lay.device) for r in range(reps + 1)]
         lay.forward(xs[-1])
@@ -462,9 +464,10 @@ def cfg_sweep(name, ms, reps=4):
         nb = algorithmic_bytes(cfg, [r_[0] for r_ in rows], m)
         g = sum(b[0] for b in nb) / sum(r_[1]["grouped"] for r_ in rows) / 1e9
         f = sum(b[1] for b in nb) / len(nb) / t_fwd / 1e9
-        out[f"{name}_m{m}"] = {"tokens_per_s": m / t_fwd, "forward_us": t_fwd * 1e6, "grouped_gbs": g,
-                               "grouped_frac": g / peak, "forward_gbs": f, "forward_frac": f / peak,
-                               "l2": "flushed before each forward"}
+        key = f"{name}_m{m}" + {0: "", 1: "_verify", 2: "_prefill"}[mode]
+        out[key] = {"tokens_per_s": m / t_fwd, "forward_us": t_fwd * 1e6, "grouped_gbs": g,
+                    "grouped_frac": g / peak, "forward_gbs": f, "forward_frac": f / peak,
+                    "l2": "flushed before each forward"}
     del lay, flush
     torch.cuda.empty_cache()
     return out

@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define SB_ABI_VERSION 4
+#define SB_ABI_VERSION 5
 
 enum sb_status {
   SB_OK = 0,
@@ -100,7 +100,14 @@ typedef struct sb_moe_layer {
    *              renormalize=False, m25_stage.py:301) */
   int32_t logits_bf16;
   int32_t no_renorm;
+  /* Which tensor-core grouped kernel runs the experts (SB_LAYOUT_TC only). SB_PREFILL_AUTO picks the
+   * prefill kernel (bf16 operands, the whole K in TMEM, passes of 128 tokens) when the batch routes
+   * at least 4 tokens per expert on average, else the verify kernel (per-stage readback, passes of
+   * 8-16 tokens). Each kernel is row-invariant on its own; the two differ in summation order. */
+  int32_t prefill;
 } sb_moe_layer;
+
+enum sb_prefill { SB_PREFILL_AUTO = 0, SB_PREFILL_VERIFY = 1, SB_PREFILL_WIDE = 2 };
 
 /* ── introspection ───────────────────────────────────────────────────────────────────────────── */
 int sb_abi_version(void);
@@ -147,6 +154,7 @@ int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, in
 
 /* ── the MoE stage forward (MoE.forward, model.py:634-649; Gate.forward :569-589;
  *    Expert.forward :601-611; grouped decode v4_moe_grouped.py:634-709) ──────────────────────── */
+/* Bytes of workspace for a forward of up to m tokens (the size serves every m' <= m). */
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m);
 /* x bf16 [M, H] -> y bf16 [M, H]. input_ids int64 [M] (read only for hash routing; may be NULL
  * otherwise). Optional outputs (NULL to skip): routing weights fp32 [M, k] and top-k indices

@@ -58,18 +58,36 @@ struct Workspace {
   int32_t* pass_pb;
   uint8_t* bpanel;     // tensor-core layout: B tiles of every (pass, stage)
   float* apanel;       //                     and their row scales
+  __nv_bfloat16* xw;   // prefill kernel: act-quantised x as bf16, routed pairs in expert order + shared rows
+  __nv_bfloat16* hw;   //                 act-quantised h as bf16, rows of h
+  bool wide;           // the forward runs the prefill kernel
   int n_sh_pass;
   size_t bytes;
 };
 
-// Tensor-core layout: passes of the shared expert (FP8, 16 tokens each).
-int64_t shared_passes(const sb_moe_layer* L, int64_t m) { return L->has_shared ? (m + 15) / 16 : 0; }
+// The prefill kernel runs when asked, or by default when the batch routes >= 4 tokens per expert.
+bool use_wide(const sb_moe_layer* L, int64_t m) {
+  if (L->layout != SB_LAYOUT_TC || L->prefill == SB_PREFILL_VERIFY) return false;
+  if (L->prefill == SB_PREFILL_WIDE) return true;
+  return m * L->topk >= 4 * (int64_t)L->n_experts;
+}
+
+// tokens per pass of a routed expert and of the shared expert
+int64_t routed_pass_max(const sb_moe_layer* L, int64_t m) {
+  return use_wide(L, m) ? sb::TC_WIDE_PASS : sb::tc_pass_max(L->expert_fmt);
+}
+
+// Tensor-core layout: passes of the shared expert (FP8: 16 tokens each, 128 in the prefill kernel).
+int64_t shared_passes(const sb_moe_layer* L, int64_t m) {
+  const int64_t pm = use_wide(L, m) ? sb::TC_WIDE_PASS : 16;
+  return L->has_shared ? (m + pm - 1) / pm : 0;
+}
 
 // Upper bound of the routed passes of one grouped launch: sum over experts of
 // ceil(count / pass_max) <= P / pass_max + (active experts).
 int64_t max_routed_passes(const sb_moe_layer* L, int64_t m) {
   const int64_t P = m * L->topk, E = L->n_experts;
-  return P / sb::tc_pass_max(L->expert_fmt) + (P < E ? P : E);
+  return P / routed_pass_max(L, m) + (P < E ? P : E);
 }
 
 int64_t max_passes(const sb_moe_layer* L, int64_t m) { return shared_passes(L, m) + max_routed_passes(L, m); }
@@ -105,9 +123,14 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   w.pass_off = (int32_t*)take(tc ? sizeof(int32_t) * (E + 1) : 0);
   w.pass_slot = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
   w.pass_pb = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
-  const int64_t panel_tiles = tc ? max_passes(L, m) * ((H > I ? H : I) / 128) : 0;
+  w.wide = use_wide(L, m);
+  const int64_t panel_tiles = tc && !w.wide ? max_passes(L, m) * ((H > I ? H : I) / 128) : 0;
   w.bpanel = take((size_t)panel_tiles * 2048);
   w.apanel = (float*)take((size_t)panel_tiles * 16 * sizeof(float));
+  // fp32 activation scales: a residual plane below each matrix (hi + lo)
+  const int64_t planes = L->act_pow2 ? 1 : 2;
+  w.xw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * R * H : 0);
+  w.hw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * R * I : 0);
   w.n_sh_pass = (int)shared_passes(L, m);
   w.bytes = off;
   return w;
@@ -134,6 +157,7 @@ int check_layer(const sb_moe_layer* L) {
     return fail(SB_ERR_ARG, "weight pointers must be 16-byte aligned");
   if (L->tid2eid && L->vocab <= 0) return fail(SB_ERR_ARG, "tid2eid given with vocab=%lld", (long long)L->vocab);
   if (L->layout != SB_LAYOUT_FRAGMENT && L->layout != SB_LAYOUT_TC) return fail(SB_ERR_ARG, "layout=%d unknown", L->layout);
+  if (L->prefill < SB_PREFILL_AUTO || L->prefill > SB_PREFILL_WIDE) return fail(SB_ERR_ARG, "prefill=%d unknown", L->prefill);
   return SB_OK;
 }
 
@@ -421,7 +445,18 @@ int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, in
 
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
   if (check_layer(layer) != SB_OK || m < 0) return 0;
-  return carve(layer, m < 1 ? 1 : m, nullptr).bytes;
+  if (m < 1) m = 1;
+  size_t need = carve(layer, m, nullptr).bytes;
+  // A workspace sized for m serves every m' <= m: past the verify/prefill switch the largest
+  // verify-kernel batch can need more than the prefill kernel at m.
+  if (layer->layout == SB_LAYOUT_TC && layer->prefill == SB_PREFILL_AUTO && use_wide(layer, m)) {
+    const int64_t m_verify = (4 * (int64_t)layer->n_experts + layer->topk - 1) / layer->topk - 1;
+    if (m_verify >= 1) {
+      const size_t v = carve(layer, m_verify < m ? m_verify : m, nullptr).bytes;
+      if (v > need) need = v;
+    }
+  }
+  return need;
 }
 
 static int route_impl(const sb_moe_layer* L, const void* x, int64_t m, const int64_t* ids, float* out_w,
@@ -503,7 +538,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.pair_tok = w.pair_tok;
   p.pair_slot = w.pair_slot;
   p.err = w.err;
-  p.pass_max = L->layout == SB_LAYOUT_TC ? sb::tc_pass_max(L->expert_fmt) : 0;
+  p.pass_max = L->layout == SB_LAYOUT_TC ? (int)routed_pass_max(L, m) : 0;
   p.pass_off = L->layout == SB_LAYOUT_TC ? w.pass_off : nullptr;
   p.pass_slot = w.pass_slot;
   p.pass_pb = w.pass_pb;
@@ -529,7 +564,45 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   g.topk_w = w.topk_w;
   g.err = w.err;
   const int n_units = (int)(max_active + (L->has_shared ? 1 : 0));
-  if (L->layout == SB_LAYOUT_TC) {
+  if (L->layout == SB_LAYOUT_TC && w.wide) {
+    // prefill kernel: x (act-quantised, bf16) in expert order, w13 (+ SwiGLU -> h), h act-quantised
+    // as bf16, w2
+    sb::TcPlan plan;
+    memset(&plan, 0, sizeof plan);
+    plan.pass_off = w.pass_off;
+    plan.pass_slot = w.pass_slot;
+    plan.pass_pb = w.pass_pb;
+    plan.n_sh_pass = w.n_sh_pass;
+    const int64_t R = P + m;
+    const int split = L->act_pow2 ? 0 : 1;
+    rc = cuda_check(sb::launch_wide_x(w.xq, w.xs, w.pair_tok, (int)m, (int)P, (int)H, split, w.xw, st), "wide x");
+    if (rc) return rc;
+    g.mode = sb::MODE_W13;
+    g.n_rows = (int)(2 * I);
+    g.k = (int)H;
+    g.routed = routed_set(L, true);
+    g.shared = shared_set(L, true);
+    g.hbf = w.hbf;
+    g.n_experts = L->n_experts;
+    g.items_per_expert = (int)(I / 64);
+    const int64_t n_pass_max = max_passes(L, m);
+    rc = cuda_check(sb::launch_tc_wide(g, plan, w.xw, R, split, (int)(n_pass_max * g.items_per_expert), st),
+                    "wide w13");
+    if (rc) return rc;
+    mark(3);
+    rc = cuda_check(sb::launch_wide_h(w.hbf, R, (int)I, L->act_pow2, w.hw, st), "wide h");
+    if (rc) return rc;
+    g.mode = sb::MODE_W2;
+    g.n_rows = (int)H;
+    g.k = (int)I;
+    g.routed = routed_set(L, false);
+    g.shared = shared_set(L, false);
+    g.o = w.o;
+    g.items_per_expert = (int)(H / 128);
+    rc = cuda_check(sb::launch_tc_wide(g, plan, w.hw, R, split, (int)(n_pass_max * g.items_per_expert), st),
+                    "wide w2");
+    if (rc) return rc;
+  } else if (L->layout == SB_LAYOUT_TC) {
     // tensor-core path: w13 panel, w13 (+ SwiGLU -> h bf16), w2 panel (act_quant of h), w2
     sb::TcPlan plan;
     plan.bpanel = w.bpanel;

@@ -51,6 +51,17 @@ def tile(fmt: int, kind: int, w: torch.Tensor, s: torch.Tensor, n_mat: int, n: i
     return wt, st
 
 
+def _pow2_scales(*scales) -> bool:
+    """True when every nonzero fp32 scale is a power of two. Tiled scales are fp32 words held as
+    bytes, with zero pads."""
+    for t in scales:
+        f = t.contiguous().view(torch.float32) if t.dtype == torch.uint8 else t.float()
+        m, _ = torch.frexp(f[f != 0])
+        if not bool((m.abs() == 0.5).all()):
+            return False
+    return True
+
+
 class MoELayer:
     """One MoE layer resident on a B200, in the layout the forward streams.
 
@@ -65,7 +76,7 @@ class MoELayer:
     def __init__(self, *, hidden, inter, n_experts, topk, expert_fmt, gate_w, gate_bias=None, tid2eid=None,
                  score_func="sigmoid", route_scale=1.0, swiglu_limit=0.0, act_pow2=True,
                  w13, w13_s, w13_ts=None, w2, w2_s, w2_ts=None, shared=None, tiled=False, layout=None,
-                 logits_bf16=False, renormalize=True):
+                 logits_bf16=False, renormalize=True, prefill=0):
         self.hidden, self.inter, self.n_experts, self.topk = hidden, inter, n_experts, topk
         self.layout = DEFAULT_LAYOUT if layout is None else layout
         self.expert_fmt = expert_fmt
@@ -90,6 +101,13 @@ class MoELayer:
                 a, b = tile(F.FMT_FP8, _lib.MAT_W13, s13, s13s, 1, 2 * i, h, self.layout)
                 c, d = tile(F.FMT_FP8, _lib.MAT_PLAIN, s2, s2s, 1, h, i, self.layout)
                 self.shared = (a, b, c, d)
+        # The prefill kernel dequantises weights to bf16 operands: exact for NVFP4 / MXFP4 and for FP8
+        # with power-of-two block scales (ue8m0). Layers with other FP8 scales stay on the verify kernel
+        # unless the prefill kernel is asked for explicitly.
+        fp8_scales = [self.shared[1], self.shared[3]] if self.shared is not None else []
+        if expert_fmt == F.FMT_FP8:
+            fp8_scales += [self.w13_s, self.w2_s]
+        self.prefill_exact = _pow2_scales(*fp8_scales)
         self.desc = SbMoeLayer()
         d = self.desc
         d.hidden, d.inter, d.n_experts, d.topk = h, i, e, topk
@@ -110,8 +128,24 @@ class MoELayer:
         d.layout = self.layout
         d.logits_bf16 = 1 if logits_bf16 else 0
         d.no_renorm = 0 if renormalize else 1
+        self.prefill = prefill     # 0 auto, 1 verify kernel, 2 prefill kernel
         self._ws = None
         self.score_func, self.route_scale, self.swiglu_limit, self.act_pow2 = score_func, route_scale, swiglu_limit, act_pow2
+
+    @property
+    def prefill(self) -> int:
+        """Expert-kernel choice on the tensor-core layout: 0 by batch size (the prefill kernel once
+        the batch routes >= 4 tokens per expert), 1 always the verify kernel, 2 always the prefill
+        kernel."""
+        return int(self.desc.prefill)
+
+    @prefill.setter
+    def prefill(self, mode: int):
+        """0 resolves to 1 on layers whose FP8 block scales are not all powers of two."""
+        mode = int(mode)
+        if mode not in (0, 1, 2):
+            raise ValueError(f"prefill mode {mode} is not 0, 1 or 2")
+        self.desc.prefill = 1 if mode == 0 and not self.prefill_exact else mode
 
     # ── scratch ───────────────────────────────────────────────────────────────────────────────
     def workspace_bytes(self, m: int) -> int:

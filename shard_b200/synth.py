@@ -197,13 +197,14 @@ def _normal_expert_on_device(cfg, layer, expert, fmt, device):
 
 
 def device_layer(cfg: MoEConfig, layer: int = 0, device="cuda", seeded=None, fill="random", act_pow2=True,
-                 layout=None):
+                 layout=None, prefill=0):
     """A MoELayer on `device` for config `cfg`.
 
     seeded: expert ids generated from their CPU-seeded draws (the bytes the oracle and the golden
             vectors use); None means all of them.
     fill:   how the other experts are made: "random" (valid random bytes, for experts no check
             reads) or "normal" (N(0, 0.02) drawn and quantised on the device, for benchmarks).
+    prefill: expert-kernel choice on the tensor-core layout (0 by batch size, 1 verify, 2 prefill).
     The shared expert and the gate are always the seeded ones."""
     from .moe import MoELayer
     e, h, i, fmt = cfg.n_experts, cfg.hidden, cfg.inter, cfg.expert_fmt
@@ -254,6 +255,7 @@ def device_layer(cfg: MoEConfig, layer: int = 0, device="cuda", seeded=None, fil
                    gate_bias=gb.to(device), score_func=cfg.score_func, route_scale=cfg.route_scale,
                    swiglu_limit=cfg.swiglu_limit, act_pow2=act_pow2, w13=w13, w13_s=w13_s,
                    w13_ts=w13_ts if fmt == F.FMT_NVFP4 else None, w2=w2, w2_s=w2_s,
-                   w2_ts=w2_ts if fmt == F.FMT_NVFP4 else None, shared=shared, layout=layout)
+                   w2_ts=w2_ts if fmt == F.FMT_NVFP4 else None, shared=shared, layout=layout,
+                   prefill=prefill)
     del w13, w13_s, w2, w2_s
     return lay

@@ -73,6 +73,29 @@ def test_workspace_sizes_grow_with_m_and_reject_bad_layers():
     assert 0 < a < b   # 9 tokens need a second NVFP4 pass (8 tokens per pass)
 
 
+def test_workspace_serves_every_smaller_batch_across_the_prefill_switch():
+    """A workspace sized for m serves every m' <= m: under the default kernel choice the size at m
+    covers both the verify kernel's largest batch below the switch and the prefill kernel at m."""
+    L = _lib.lib()
+    for e, k in ((16, 4), (256, 8), (384, 8)):
+        d = _layer(n_experts=e, topk=k)
+        sizes = {}
+        for mode in (0, 1, 2):
+            d.prefill = mode
+            sizes[mode] = [L.sb_moe_workspace_bytes(ctypes.byref(d), m) for m in range(1, 4 * e // k + 40)]
+            assert all(s > 0 for s in sizes[mode])
+            assert sizes[mode] == sorted(sizes[mode]), (e, k, mode)
+        switch = 4 * e // k                              # first m the default sends to the prefill kernel
+        for m in range(1, len(sizes[0]) + 1):
+            below = max(sizes[1][:min(m, switch - 1)])
+            assert sizes[0][m - 1] >= below
+            assert sizes[0][m - 1] >= (sizes[2][m - 1] if m >= switch else sizes[1][m - 1])
+    d = _layer()
+    d.prefill = 3
+    assert L.sb_moe_workspace_bytes(ctypes.byref(d), 16) == 0
+    assert L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, 1 << 30, None) == -1
+
+
 def _msg():
     return _lib.lib().sb_last_error().decode()
 
@@ -144,3 +167,31 @@ def test_bad_m_is_rejected(call):
     else:
         rc = L.sb_moe_forward(ctypes.byref(d), FAKE, -1, None, FAKE, None, None, FAKE, 1 << 30, None)
     assert rc == -2
+
+
+def _host_layer(shared_scale, fp8_experts=False, prefill=0):
+    """A MoELayer over host tensors in the tiled form (its constructor makes no library call then)."""
+    import torch
+    from shard_b200.moe import MoELayer
+    e, h, i = 4, 256, 128
+    u8 = lambda n: torch.zeros(n, dtype=torch.uint8)
+    sc = torch.full((16,), shared_scale, dtype=torch.float32).view(torch.uint8)
+    fmt = F.FMT_FP8 if fp8_experts else F.FMT_NVFP4
+    ex_s = sc.repeat(e) if fp8_experts else u8(64)
+    return MoELayer(hidden=h, inter=i, n_experts=e, topk=2, expert_fmt=fmt, gate_w=torch.zeros(e, h),
+                    w13=u8(64), w13_s=ex_s, w2=u8(64), w2_s=ex_s, w13_ts=torch.ones(e, 2), w2_ts=torch.ones(e),
+                    shared=(u8(64), sc, u8(64), sc), tiled=True, prefill=prefill)
+
+
+def test_non_power_of_two_fp8_scales_keep_the_verify_kernel():
+    """The prefill kernel's bf16 weight operand is exact only for power-of-two FP8 block scales: the
+    default choice resolves to the verify kernel otherwise; an explicit choice stands."""
+    assert _host_layer(2.0 ** -7).prefill == 0
+    lay = _host_layer(0.3)
+    assert not lay.prefill_exact and lay.prefill == 1
+    assert _host_layer(0.3, prefill=2).prefill == 2
+    assert _host_layer(0.3, fp8_experts=True).prefill == 1
+    lay = _host_layer(0.25, fp8_experts=True)
+    assert lay.prefill_exact and lay.prefill == 0
+    with pytest.raises(ValueError):
+        lay.prefill = 4

@@ -89,19 +89,23 @@ def test_quantised_gemm_matches_oracle(fmt, m, n, k, layout):
     assert (_np(y) != ref).mean() < 0.02
 
 
-def _golden_layer(name, layout=None):
+# (layout, prefill): the tensor-core layout's verify kernel and prefill kernel, the fragment layout
+KERNELS = {"tc_verify": (1, 1), "tc_prefill": (1, 2), "fragment": (0, 0)}
+
+
+def _golden_layer(name, layout=None, prefill=0):
     g = load_golden(name)
     cfg, m, xs, sfmt = case_config(name)
     seeded = None if cfg.n_experts <= 32 else sorted(set(g["indices"].ravel().tolist()))
-    lay = S.device_layer(cfg, 0, "cuda", seeded=seeded, act_pow2=sfmt is not None, layout=layout)
+    lay = S.device_layer(cfg, 0, "cuda", seeded=seeded, act_pow2=sfmt is not None, layout=layout, prefill=prefill)
     x, ids = case_inputs(cfg, m, xs)
     return g, cfg, lay, x, ids, sfmt
 
 
-@pytest.mark.parametrize("layout", LAYOUTS)
+@pytest.mark.parametrize("kernel", list(KERNELS))
 @pytest.mark.parametrize("name", list(CASES))
-def test_forward_matches_reference_golden(name, layout):
-    g, cfg, lay, x, ids, sfmt = _golden_layer(name, layout)
+def test_forward_matches_reference_golden(name, kernel):
+    g, cfg, lay, x, ids, sfmt = _golden_layer(name, *KERNELS[kernel])
     y, w, idx = lay.forward(x.cuda(), ids.cuda(), routing=True)
     torch.cuda.synchronize()
     assert np.array_equal(idx.cpu().numpy(), g["indices"]), "router top-k indices must be bit-exact"
@@ -122,11 +126,12 @@ def test_forward_matches_oracle(name):
 
 @pytest.mark.parametrize("layout", LAYOUTS)
 @pytest.mark.parametrize("cname,m", [("c1", 1), ("c1", 8), ("c1", 32), ("c1", 64), ("c3", 16), ("c3", 64),
-                                     ("c4", 256)])
+                                     ("c4", 256), ("c4", 1024)])
 def test_full_size_forward(cname, m, layout):
     """Full BASELINE shapes. The oracle checks a sample of tokens (its cost grows with the experts
     they route to); the whole batch is checked for row invariance: every token's output equals the
-    same token run alone, bit for bit."""
+    same token run alone through the same kernel, bit for bit. The tensor-core layout runs both of
+    its expert kernels (verify and prefill), and the default choice must equal the one it picks."""
     cfg = S.CONFIGS[cname]
     x, ids = S.make_inputs(cfg, m)
     gw, gb = S.make_gate(cfg)
@@ -134,23 +139,36 @@ def test_full_size_forward(cname, m, layout):
     sample = sorted(set([0, m // 2, m - 1]))[:3]
     seeded = sorted(set(idx_o[sample].ravel().tolist()))
     lay = S.device_layer(cfg, 0, "cuda", seeded=seeded, layout=layout)
-    y, w, idx = lay.forward(x.cuda(), ids.cuda(), routing=True)
-    assert np.array_equal(idx.cpu().numpy(), idx_o), "router top-k indices must be bit-exact"
     sl = SeededLayer(cfg)
     yo, _, _ = O.moe_forward(sl.oracle(), x[sample].float().numpy(), workers=8)
-    err = O.max_rel_err(_np(y[sample]), yo)
-    assert err < TOL, f"{cname} M={m}: max rel err {err:.3e}"
-    for t in sample:
-        alone = lay.forward(x[t:t + 1].cuda(), ids[t:t + 1].cuda())
-        assert torch.equal(alone, y[t:t + 1]), "a token's output must not depend on its batch"
-    assert torch.isfinite(y.float()).all()
-    assert lay.device_error() == 0
+    modes = [1, 2] if layout == 1 else [0]
+    ys = {}
+    for mode in modes:
+        lay.prefill = mode
+        y, w, idx = lay.forward(x.cuda(), ids.cuda(), routing=True)
+        assert np.array_equal(idx.cpu().numpy(), idx_o), "router top-k indices must be bit-exact"
+        err = O.max_rel_err(_np(y[sample]), yo)
+        assert err < TOL, f"{cname} M={m} prefill={mode}: max rel err {err:.3e}"
+        for t in sample:
+            alone = lay.forward(x[t:t + 1].cuda(), ids[t:t + 1].cuda())
+            assert torch.equal(alone, y[t:t + 1]), "a token's output must not depend on its batch"
+        assert torch.isfinite(y.float()).all()
+        assert lay.device_error() == 0
+        ys[mode] = y
+    if layout == 1:
+        lay.prefill = 0
+        auto = lay.forward(x.cuda(), ids.cuda())
+        wide = m * cfg.topk >= 4 * cfg.n_experts
+        assert torch.equal(auto, ys[2 if wide else 1])
+        # the two kernels sum in different orders; they agree to well within the parity bar
+        assert O.max_rel_err(_np(ys[1]), _np(ys[2])) < TOL
 
 
-def test_merged_chunks_equal_unmerged():
-    """Row invariance across batch composition: two verify chunks run together equal each run alone."""
+@pytest.mark.parametrize("prefill", [1, 2])
+def test_merged_chunks_equal_unmerged(prefill):
+    """Row invariance across batch composition: two chunks run together equal each run alone."""
     cfg = S.CONFIGS["c0"]
-    lay = S.device_layer(cfg, 0, "cuda")
+    lay = S.device_layer(cfg, 0, "cuda", prefill=prefill)
     a, _ = S.make_inputs(cfg, 16, step=1)
     b, _ = S.make_inputs(cfg, 16, step=2)
     ya, yb = lay.forward(a.cuda()), lay.forward(b.cuda())
