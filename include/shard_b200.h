@@ -101,9 +101,11 @@ typedef struct sb_moe_layer {
   int32_t logits_bf16;
   int32_t no_renorm;
   /* Which tensor-core grouped kernel runs the experts (SB_LAYOUT_TC only). SB_PREFILL_AUTO picks the
-   * prefill kernel (bf16 operands, the whole K in TMEM, passes of 128 tokens) when the batch routes
-   * at least 4 tokens per expert on average, else the verify kernel (per-stage readback, passes of
-   * 8-16 tokens). Each kernel is row-invariant on its own; the two differ in summation order. */
+   * prefill kernel (16-bit operands, the whole K in TMEM, passes of 128 tokens) when the batch routes
+   * at least 16 tokens per expert on average, else the verify kernel (per-stage readback, passes of
+   * 8-16 tokens). Each kernel is row-invariant on its own; the two differ in summation order. The
+   * prefill kernel's dequantised weights are exact for NVFP4, MXFP4 and for FP8 whose 128x128
+   * block scales are powers of two; pick SB_PREFILL_VERIFY for FP8 banks with other scales. */
   int32_t prefill;
 } sb_moe_layer;
 

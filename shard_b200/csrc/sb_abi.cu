@@ -60,26 +60,35 @@ struct Workspace {
   float* apanel;       //                     and their row scales
   __nv_bfloat16* xw;   // prefill kernel: act-quantised x as bf16, routed pairs in expert order + shared rows
   __nv_bfloat16* hw;   //                 act-quantised h as bf16, rows of h
+  float* cx;           //                 the power of two each row of xw / hw was divided by
+  float* ch;
   bool wide;           // the forward runs the prefill kernel
+  int64_t sb_row;      //   its padded row space: the shared expert's first row, and all rows
+  int64_t wide_rows;
   int n_sh_pass;
   size_t bytes;
 };
 
-// The prefill kernel runs when asked, or by default when the batch routes >= 4 tokens per expert.
+// The prefill kernel runs when asked, or by default when the batch routes >= 16 tokens per expert on
+// average: below that the verify kernel's narrow passes cost less (measured on B200 at c1 / c4 shapes).
+constexpr int64_t WIDE_TOKENS_PER_EXPERT = 16;
 bool use_wide(const sb_moe_layer* L, int64_t m) {
   if (L->layout != SB_LAYOUT_TC || L->prefill == SB_PREFILL_VERIFY) return false;
   if (L->prefill == SB_PREFILL_WIDE) return true;
-  return m * L->topk >= 4 * (int64_t)L->n_experts;
+  return m * L->topk >= WIDE_TOKENS_PER_EXPERT * (int64_t)L->n_experts;
 }
 
-// tokens per pass of a routed expert and of the shared expert
+// Tokens per pass of a routed expert and of the shared expert. The prefill kernel takes passes of
+// 128 tokens, or 64 when fp32 activation scales double its B operand (hi and lo planes).
+int64_t wide_pass(const sb_moe_layer* L) { return L->act_pow2 ? sb::TC_WIDE_PASS : sb::TC_WIDE_PASS / 2; }
+
 int64_t routed_pass_max(const sb_moe_layer* L, int64_t m) {
-  return use_wide(L, m) ? sb::TC_WIDE_PASS : sb::tc_pass_max(L->expert_fmt);
+  return use_wide(L, m) ? wide_pass(L) : sb::tc_pass_max(L->expert_fmt);
 }
 
-// Tensor-core layout: passes of the shared expert (FP8: 16 tokens each, 128 in the prefill kernel).
+// Tensor-core layout: passes of the shared expert (FP8: 16 tokens each, more in the prefill kernel).
 int64_t shared_passes(const sb_moe_layer* L, int64_t m) {
-  const int64_t pm = use_wide(L, m) ? sb::TC_WIDE_PASS : 16;
+  const int64_t pm = use_wide(L, m) ? wide_pass(L) : 16;
   return L->has_shared ? (m + pm - 1) / pm : 0;
 }
 
@@ -119,18 +128,23 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   w.hq = take(tc ? 0 : (size_t)R * I);
   w.hs = (float*)take(tc ? 0 : sizeof(float) * R * (I / 128));
   w.o = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * H);
-  w.hbf = (__nv_bfloat16*)take(tc ? sizeof(__nv_bfloat16) * R * I : 0);
+  // the prefill kernel keeps h in the padded row space of its B operands (wide_rows >= R)
+  w.wide = use_wide(L, m);
+  w.sb_row = sb::wide_sb_row(P, E);
+  w.wide_rows = w.sb_row + ((m + 7) & ~(int64_t)7);
+  w.hbf = (__nv_bfloat16*)take(tc ? sizeof(__nv_bfloat16) * (w.wide ? w.wide_rows : R) * I : 0);
   w.pass_off = (int32_t*)take(tc ? sizeof(int32_t) * (E + 1) : 0);
   w.pass_slot = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
   w.pass_pb = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
-  w.wide = use_wide(L, m);
   const int64_t panel_tiles = tc && !w.wide ? max_passes(L, m) * ((H > I ? H : I) / 128) : 0;
   w.bpanel = take((size_t)panel_tiles * 2048);
   w.apanel = (float*)take((size_t)panel_tiles * 16 * sizeof(float));
   // fp32 activation scales: a residual plane below each matrix (hi + lo)
   const int64_t planes = L->act_pow2 ? 1 : 2;
-  w.xw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * R * H : 0);
-  w.hw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * R * I : 0);
+  w.xw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * w.wide_rows * H : 0);
+  w.hw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * w.wide_rows * I : 0);
+  w.cx = (float*)take(w.wide ? sizeof(float) * w.wide_rows : 0);
+  w.ch = (float*)take(w.wide ? sizeof(float) * w.wide_rows : 0);
   w.n_sh_pass = (int)shared_passes(L, m);
   w.bytes = off;
   return w;
@@ -450,7 +464,7 @@ size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
   // A workspace sized for m serves every m' <= m: past the verify/prefill switch the largest
   // verify-kernel batch can need more than the prefill kernel at m.
   if (layer->layout == SB_LAYOUT_TC && layer->prefill == SB_PREFILL_AUTO && use_wide(layer, m)) {
-    const int64_t m_verify = (4 * (int64_t)layer->n_experts + layer->topk - 1) / layer->topk - 1;
+    const int64_t m_verify = (WIDE_TOKENS_PER_EXPERT * layer->n_experts + layer->topk - 1) / layer->topk - 1;
     if (m_verify >= 1) {
       const size_t v = carve(layer, m_verify < m ? m_verify : m, nullptr).bytes;
       if (v > need) need = v;
@@ -575,7 +589,10 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     plan.n_sh_pass = w.n_sh_pass;
     const int64_t R = P + m;
     const int split = L->act_pow2 ? 0 : 1;
-    rc = cuda_check(sb::launch_wide_x(w.xq, w.xs, w.pair_tok, (int)m, (int)P, (int)H, split, w.xw, st), "wide x");
+    const int rbf = L->expert_fmt == SB_FMT_MXFP4 ? 1 : 0;   // MXFP4 experts take bf16 operands
+    rc = cuda_check(sb::launch_wide_x(w.xq, w.xs, w.pair_tok, w.offsets, L->n_experts, (int)m, (int)P, (int)H,
+                                      w.wide_rows, (int)w.sb_row, split, rbf, w.xw, w.cx, st),
+                    "wide x");
     if (rc) return rc;
     g.mode = sb::MODE_W13;
     g.n_rows = (int)(2 * I);
@@ -586,11 +603,14 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     g.n_experts = L->n_experts;
     g.items_per_expert = (int)(I / 64);
     const int64_t n_pass_max = max_passes(L, m);
-    rc = cuda_check(sb::launch_tc_wide(g, plan, w.xw, R, split, (int)(n_pass_max * g.items_per_expert), st),
+    rc = cuda_check(sb::launch_tc_wide(g, plan, w.xw, w.cx, w.wide_rows, (int)w.sb_row, split,
+                                       (int)(n_pass_max * g.items_per_expert), st),
                     "wide w13");
     if (rc) return rc;
     mark(3);
-    rc = cuda_check(sb::launch_wide_h(w.hbf, R, (int)I, L->act_pow2, w.hw, st), "wide h");
+    rc = cuda_check(sb::launch_wide_h(w.hbf, w.wide_rows, w.wide_rows, (int)w.sb_row, (int)I, L->act_pow2, rbf, w.hw,
+                                      w.ch, st),
+                    "wide h");
     if (rc) return rc;
     g.mode = sb::MODE_W2;
     g.n_rows = (int)H;
@@ -599,7 +619,8 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     g.shared = shared_set(L, false);
     g.o = w.o;
     g.items_per_expert = (int)(H / 128);
-    rc = cuda_check(sb::launch_tc_wide(g, plan, w.hw, R, split, (int)(n_pass_max * g.items_per_expert), st),
+    rc = cuda_check(sb::launch_tc_wide(g, plan, w.hw, w.ch, w.wide_rows, (int)w.sb_row, split,
+                                       (int)(n_pass_max * g.items_per_expert), st),
                     "wide w2");
     if (rc) return rc;
   } else if (L->layout == SB_LAYOUT_TC) {

@@ -135,13 +135,19 @@ cudaError_t launch_wire_unpack(const uint8_t* q, const void* s, int64_t rows, in
 cudaError_t launch_combine_pack(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h,
                                 int has_shared, __nv_bfloat16* y, uint8_t* q, __nv_bfloat16* s, cudaStream_t st);
 constexpr int TC_WIDE_PASS = 128;   // tokens per pass of the prefill kernel (sb_tcw.cu)
-// B operand matrices of the prefill kernel: b_rows bf16 rows, followed (split) by b_rows rows of the
-// residuals, so that hi + lo carries a non-power-of-two activation scale's product to ~16 bits.
-cudaError_t launch_tc_wide(const GroupedArgs& g, const TcPlan& plan, const void* bmat, int64_t b_rows, int split,
-                           int max_items, cudaStream_t st);
-cudaError_t launch_wide_x(const uint8_t* xq, const float* xs, const int32_t* pair_tok, int m, int P, int h, int split,
-                          __nv_bfloat16* xw, cudaStream_t st);
-cudaError_t launch_wide_h(const __nv_bfloat16* hbf, int64_t rows, int k, int pow2, __nv_bfloat16* hw, cudaStream_t st);
+// Prefill kernel (sb_tcw.cu). B operand matrices live in a padded row space of r_pad rows (expert e's
+// rows from a multiple of 8, the shared expert's tokens from sb_row), chunk-major and 128B-swizzled;
+// 16-bit rows (f16, or bf16 for the routed rows of MXFP4 layers), each divided by the power of two
+// cvec[row]; with `split` a second plane of residuals follows, so that hi + lo carries a
+// non-power-of-two activation scale's product.
+constexpr int wide_sb_row(int64_t P, int64_t n_experts) { return (int)((P + 8 * n_experts + 7) & ~(int64_t)7); }
+cudaError_t launch_tc_wide(const GroupedArgs& g, const TcPlan& plan, const void* bmat, const float* cvec,
+                           int64_t r_pad, int sb_row, int split, int max_items, cudaStream_t st);
+cudaError_t launch_wide_x(const uint8_t* xq, const float* xs, const int32_t* pair_tok, const int32_t* offsets,
+                          int n_experts, int m, int P, int h, int64_t r_pad, int sb_row, int split, int routed_bf16,
+                          void* xw, float* cvec, cudaStream_t st);
+cudaError_t launch_wide_h(const __nv_bfloat16* hbf, int64_t rows, int64_t r_pad, int sb_row, int k, int pow2,
+                          int routed_bf16, void* hw, float* cvec, cudaStream_t st);
 cudaError_t launch_tc_tile(int fmt, int kind, bool scales, const void* src, void* dst, int64_t n_mat, int64_t n,
                            int64_t k, cudaStream_t st);
 

@@ -1,24 +1,37 @@
-// Grouped expert GEMM at prefill widths on the tensor cores: bf16 operands and the whole K reduced
+// Grouped expert GEMM at prefill widths on the tensor cores: 16-bit operands and the whole K reduced
 // in TMEM, so each pass is read back once (the verify-width kernel, sb_tc.cu, reads back per stage).
 //
 // Items are (pass, 128-row block) as in sb_tc.cu, with passes of up to WN = 128 tokens. Operands per
 // 64-K sub-stage:
-//   A  the weight tile dequantised to bf16 by the worker warps from a compact staging copy:
-//      NVFP4 e2m1 x e4m3 (scale per 16) and MXFP4 e2m1 x e8m0 (per 32) are exact in bf16 (at most
-//      6 significant bits); FP8 e4m3 x its 128x128 block scale (a power of two here). The NVFP4
-//      tensor scale is applied in the epilogue.
-//   B  the pass's activation rows, bf16 values of the act-quantised activations, from an
-//      expert-ordered activation matrix by 2-D TMA boxes of 32 rows, 128-byte swizzled. With
-//      power-of-two activation scales (ue8m0) e4m3 x scale is exact in bf16; with fp32 scales the
-//      product is carried as two bf16 planes, hi = bf16(v) and lo = bf16(v - hi) (~16 significant
-//      bits), and each sub-stage multiplies A by both into the same accumulator.
+//   A  the weight tile, dequantised by the worker warps from a compact staging copy (TMA, 64-byte
+//      swizzled, so that thread r reading row r is free of bank conflicts) into tensor memory
+//      (tcgen05.st; the MMA reads A from TMEM, so the 16-bit tile never passes through shared
+//      memory):
+//        NVFP4  e2m1 x its e4m3 scale (per 16) in f16: exact (<= 6 significant bits, 2^-10..2688);
+//               the fp32 tensor scale is applied in the epilogue;
+//        FP8    e4m3 x its 128x128 block scale / c_A in f16, c_A = 16 x the item's first block
+//               scale (a power of two for ue8m0 scales): exact while the row block's scales stay
+//               within 2^+-11 of it; c_A is applied in the epilogue;
+//        MXFP4  e2m1 x its e8m0 scale (per 32) in bf16: exact (e8m0 exceeds the f16 range).
+//   B  the pass's activation rows from an expert-ordered activation matrix, copied by a loader warp
+//      with cp.async (the LSU path: the TMA engine carries only the weight stream) into the
+//      128-byte-swizzled K-major layout: dequant(act_quant(v)) = e4m3 x scale, divided by a power of two
+//      c_B per row (f16 rows: c_B = 2^ceil(log2(max scale)) / 128, so |values| <= 448 * 128) or
+//      as is (bf16 rows, MXFP4 experts). With power-of-two activation scales (ue8m0) the values
+//      are exact; with fp32 scales they are carried as two planes, hi = round(v) and
+//      lo = round(v - hi), and each sub-stage multiplies A by both into the same accumulator.
 // tcgen05.mma kind::f16 (M=128, N = tokens rounded up to 16, K=16) accumulates the whole K into one
 // of two TMEM accumulators (double-buffered across passes); the products are exact and the sum is
-// fp32, the reference's dequant-then-fp32-matmul up to summation order.
+// fp32, the reference's dequant-then-fp32-matmul up to summation order. The epilogue scales the
+// accumulator by the powers of two c_A c_B (exact) and the NVFP4 tensor scale.
 //
-// Roles (192 threads): warps 0-3 convert (thread r = weight row r) and, after a pass's last
-// sub-stage, run its epilogue (TMEM lanes = rows); warp 4 producer (TMA / bulk copies); warp 5 MMA
-// issuer (allocates TMEM). Every wait is bounded; on timeout the CTA records an error and winds down.
+// One CTA per SM (its shared memory holds deep rings), persistent over the items. Roles (352
+// threads): warps 0-7 convert, two threads per weight row r (each one 64-K half of a 128-K stage),
+// and after a pass's last stage run its epilogue (TMEM lanes = rows, the two halves taking
+// alternate 32-column chunks); warp 8 weight producer (TMA / bulk copies); warp 9 MMA issuer
+// (allocates TMEM); warp 10 B loader. The B ring's 16 KB slots hold the B tiles of 4, 2 or 1 sub-stages (passes of <= 32, <= 64,
+// <= 128 tokens), so narrow passes keep many sub-stages of activations in flight. Every wait is
+// bounded; on timeout the CTA records an error and winds down.
 #include <cudaTypedefs.h>
 
 #include "sb_launch.h"
@@ -29,50 +42,62 @@ namespace tcw {
 
 using namespace tc5;
 
-constexpr int NTHREADS = 192;
-constexpr int PRODUCER_WARP = 4;
-constexpr int MMA_WARP = 5;
+constexpr int NWORK = 8;                // converter / epilogue warps: 2 threads per weight row
+constexpr int NTHREADS = 32 * (NWORK + 3);
+constexpr int PRODUCER_WARP = NWORK;
+constexpr int MMA_WARP = NWORK + 1;
+constexpr int BLOAD_WARP = NWORK + 2;
+constexpr int BLAG = 3;                 // B slots the loader keeps in flight before releasing one
 constexpr int WN = TC_WIDE_PASS;        // tokens (B rows) per pass
-constexpr int SC = 4;                   // staging ring (compact weight stage + scales)
-constexpr int SAR = 2;                  // bf16 A tiles (64 K)
-constexpr int SBR = 2;                  // bf16 B tiles (64 K)
+constexpr int SC = 12;                  // staging ring (compact weight stage + scales)
+constexpr int SAR = 4;                  // A slots in TMEM: one staging stage each (64 columns)
+constexpr int SBR = 6;                  // B slots of 16 KB: the B tiles of 1, 2 or 4 sub-stages
 constexpr int STG_W = 8192;             // fp4: 128 rows x 64 B (128 K); FP8: 128 rows x 64 B (64 K)
 constexpr int STG_S = 1024;             // NVFP4 [128][8 B], MXFP4 [128][4 B], FP8 16 B
-constexpr int A_BYTES = 128 * 128;      // 128 rows x 64 bf16
-constexpr int B_BYTES = WN * 128;       // WN rows x 64 bf16
+constexpr int B_BYTES = WN * 128;       // WN rows x 64 16-bit values
 constexpr int BOX_ROWS = 32;
-constexpr int TMEM_COLS = 2 * WN;
+constexpr int BOX_BYTES = BOX_ROWS * 128;
+constexpr int A_COL0 = 2 * WN;          // TMEM: accumulators in columns 0 .. 2 WN, then the A slots
+constexpr int A_COLS = 64;              // 128 K of 16-bit values, two per column
+constexpr int TMEM_COLS = A_COL0 + SAR * A_COLS;
+static_assert(TMEM_COLS == 512, "TMEM columns of one CTA per SM");
 constexpr uint32_t WAIT_LIMIT = 1u << 16;
 
 struct Smem {
-  uint8_t A[SAR][A_BYTES];              // 1024-aligned (128B swizzle atoms)
-  uint8_t B[SBR][B_BYTES];
-  uint8_t stg[SC][STG_W + STG_S];
+  uint8_t B[SBR][B_BYTES];              // 1024-aligned (128B swizzle atoms)
+  uint8_t stg[SC][STG_W + STG_S];       // each 1024-aligned (64B swizzle atoms)
+  __nv_bfloat16 xchg[2][64][34];        // W13 epilogue: the up rows of each column half
   uint64_t sfull[SC], sempty[SC], afull[SAR], aempty[SAR], bfull[SBR], bempty[SBR], accfull[2], accempty[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float xchg[64][33];
 };
 constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory of one CTA per SM");
 
 struct WideArgs {
-  CUtensorMap map_b;        // activations, bf16 [rows][k]: box 64 x 32, 128-byte swizzle
-  CUtensorMap map_w8;       // FP8 routed bank as bytes [rows][128]: box 64 x 128 (unused for fp4)
-  CUtensorMap map_w8_sh;    // the FP8 shared expert / dense matrix, same form
+  CUtensorMap map_w4;       // fp4 routed bank as bytes [rows/2][128]: box 128 x 64, 128-byte swizzle
+  CUtensorMap map_w8;       // FP8 routed bank as bytes [rows][128]: box 64 x 128, 64-byte swizzle
+  CUtensorMap map_w8_sh;    // the FP8 shared expert, same form
   GroupedArgs g;
   TcPlan plan;
-  int use_w8, use_w8_sh;    // which FP8 maps were encoded (the others stay zeroed and untouched)
-  int b_split;              // B carries a residual plane (rows b_lo_row.. of map_b)
-  int b_lo_row;
+  const uint8_t* bmat;      // activations, chunk-major: [plane][k/64][r_pad][128 B], 128B-swizzled rows
+  const float* cvec;        // [r_pad] the power of two c_B each B row was divided by
+  int64_t r_pad;            // rows of the padded row space
+  int sb_row;               // first row of the shared expert's tokens
+  int use_w4, use_w8, use_w8_sh;   // which weight maps were encoded (the others stay zeroed)
+  int b_split;              // B carries a residual plane (the second plane of bmat); passes <= 64
 };
+
+// Padded row space of the B matrices: expert e's rows start at pbase(offsets[e], e), a multiple of 8
+// (its passes then start at multiples of 8 too); the shared expert's tokens follow at sb_row.
+__host__ __device__ __forceinline__ int pbase(int off, int e) { return (off + 8 * e + 7) & ~7; }
 
 struct Item {
   int shared, expert, rb, cnt, base, pb, pass;
 };
 
-template <int FMT_R>
-__device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan, int item, int nrb) {
+__device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan, int item, int nrb, int wn) {
   Item it;
   const int p = item / nrb;
   it.rb = item - p * nrb;
@@ -82,7 +107,7 @@ __device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan
     it.expert = 0;
     it.cnt = a.m;
     it.base = 0;
-    it.pb = p * WN;
+    it.pb = p * wn;
   } else {
     const int q = p - plan.n_sh_pass;
     const int slot = plan.pass_slot[q];
@@ -110,64 +135,97 @@ __device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t s2) {
   return *reinterpret_cast<const uint32_t*>(&r);
 }
 
-__device__ __forceinline__ uint32_t bf16_splat(float v) {
-  const __nv_bfloat162 b = __floats2bfloat162_rn(v, v);
-  return *reinterpret_cast<const uint32_t*>(&b);
+__device__ __forceinline__ uint32_t f16_splat(float v) {
+  const __half2 h = __float2half2_rn(v);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Row r's 64 values of one sub-stage -> 8 swizzled 16-byte chunks of the bf16 A tile.
-//   fp4: src = the row's 32 packed bytes (4 groups of 16 values); scl = the row's scale bytes of
-//        the sub-stage (NVFP4: 4 e4m3, MXFP4: 2 e8m0)
-//   FP8: src = the row's 64 e4m3 bytes; wsc = its block scale
-template <int FMT>
-__device__ __forceinline__ void convert_row(const uint8_t* src, uint32_t scl, float wsc, uint8_t* dst, int r) {
-  if (FMT == FMT_FP8) {
-    const uint32_t s2 = bf16_splat(wsc);
+// 16-byte chunk c (0-3) of staging row r. fp4 stages arrive as 64 rows of 128 B (weight rows 2q and
+// 2q+1) with TMA's 128-byte swizzle (chunk index XOR q & 7); FP8 stages as 128 rows of 64 B with the
+// 64-byte swizzle (chunk index XOR (r >> 1) & 3). Either way thread r reading row r is free of bank
+// conflicts.
+__device__ __forceinline__ uint4 stg_chunk(const uint8_t* stg, int r, int c) {
+  return *reinterpret_cast<const uint4*>(stg + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ uint4 stg_chunk4(const uint8_t* stg, int r, int c) {
+  const int q = r >> 1, cc = ((r & 1) << 2) | c;
+  return *reinterpret_cast<const uint4*>(stg + q * 128 + ((cc ^ (q & 7)) << 4));
+}
+
+// Thread (row r, half hh) converts its row's values of one staging stage into TMEM columns (two
+// 16-bit values each, K ascending). fp4 stages hold 128 K: the thread takes sub-stage hh
+// (K 64hh .. 64hh+63, staging chunks 2hh, 2hh+1) -> 32 columns.
+//   NVFP4: e2m1 x e4m3 group scale (scale bytes 4hh .. 4hh+3 of the row) in f16
+__device__ __forceinline__ void convert_nvfp4(const uint8_t* stg, int r, int hh, uint32_t (&o)[32]) {
+  const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(stg + STG_W + r * 8 + hh * 4);
+  uint32_t sh0, sh1;
+  e4m3x4_to_f16x2x2(sc4, sh0, sh1);
+  const uint32_t sq[4] = {splat_lo(sh0), splat_hi(sh0), splat_lo(sh1), splat_hi(sh1)};
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint2 v = *reinterpret_cast<const uint2*>(src + c * 8);
-      uint32_t h0, h1, h2, h3;
-      e4m3x4_to_f16x2x2(v.x, h0, h1);
-      e4m3x4_to_f16x2x2(v.y, h2, h3);
-      uint4 o;
-      o.x = bmul2(f16x2_to_bf16x2(h0), s2);
-      o.y = bmul2(f16x2_to_bf16x2(h1), s2);
-      o.z = bmul2(f16x2_to_bf16x2(h2), s2);
-      o.w = bmul2(f16x2_to_bf16x2(h3), s2);
-      *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = o;
-    }
-  } else {
+  for (int cc = 0; cc < 2; ++cc) {
+    const uint4 v = stg_chunk4(stg, r, 2 * hh + cc);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint2 v = *reinterpret_cast<const uint2*>(src + q * 8);   // 16 values
-      uint32_t h[8];
-      e2m1x8_to_f16x2x4(v.x, h[0], h[1], h[2], h[3]);
-      e2m1x8_to_f16x2x4(v.y, h[4], h[5], h[6], h[7]);
-      uint32_t b[8];
-      if (FMT == FMT_NVFP4) {
-        // e2m1 x e4m3 in f16 is exact (<= 6 significant bits, |v| <= 2688, >= 2^-10)
-        uint32_t sh0, sh1;
-        e4m3x4_to_f16x2x2(scl, sh0, sh1);
-        const uint32_t sq = (q & 1) ? splat_hi(q < 2 ? sh0 : sh1) : splat_lo(q < 2 ? sh0 : sh1);
+    for (int j = 0; j < 4; ++j) {
+      uint32_t* q = o + 16 * cc + 4 * j;
+      e2m1x8_to_f16x2x4(w[j], q[0], q[1], q[2], q[3]);
+      const uint32_t s = sq[2 * cc + (j >> 1)];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) b[e] = f16x2_to_bf16x2(hmul2_u32(h[e], sq));
-      } else {
-        // MXFP4: the power-of-two e8m0 scale of the 32 values (groups q/2), applied in bf16
-        const uint32_t eb = (scl >> (8 * (q >> 1))) & 0xFFu;
-        const uint32_t sbits = eb ? (eb << 7) : 0x0040u;          // 2^(eb-127) as bf16
-        const uint32_t s2 = sbits | (sbits << 16);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) b[e] = bmul2(f16x2_to_bf16x2(h[e]), s2);
-      }
-      const int c0 = 2 * q, c1 = 2 * q + 1;
-      *reinterpret_cast<uint4*>(dst + ((c0 ^ (r & 7)) << 4)) = make_uint4(b[0], b[1], b[2], b[3]);
-      *reinterpret_cast<uint4*>(dst + ((c1 ^ (r & 7)) << 4)) = make_uint4(b[4], b[5], b[6], b[7]);
+      for (int e = 0; e < 4; ++e) q[e] = hmul2_u32(q[e], s);
     }
   }
 }
 
+//   MXFP4: e2m1 x e8m0 group scale (scale bytes 2hh, 2hh+1) in bf16
+__device__ __forceinline__ void convert_mxfp4(const uint8_t* stg, int r, int hh, uint32_t (&o)[32]) {
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    const uint32_t eb = stg[STG_W + r * 4 + hh * 2 + cc];
+    const uint32_t sbits = eb ? (eb << 7) : 0x0040u;          // 2^(eb-127) as bf16
+    const uint32_t s2 = sbits | (sbits << 16);
+    const uint4 v = stg_chunk4(stg, r, 2 * hh + cc);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t* q = o + 16 * cc + 4 * j;
+      e2m1x8_to_f16x2x4(w[j], q[0], q[1], q[2], q[3]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) q[e] = bmul2(f16x2_to_bf16x2(q[e]), s2);
+    }
+  }
+}
+
+//   FP8 stages hold 64 K (one sub-stage): the thread takes K 32hh .. 32hh+31 (chunks 2hh, 2hh+1)
+//   -> 16 columns, e4m3 x (block scale / c_A) in f16 (s2)
+__device__ __forceinline__ void convert_fp8(const uint8_t* stg, int r, int hh, uint32_t s2, uint32_t (&o)[16]) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const uint4 v = stg_chunk(stg, r, 2 * hh + c);
+    uint32_t* q = o + 8 * c;
+    e4m3x4_to_f16x2x2(v.x, q[0], q[1]);
+    e4m3x4_to_f16x2x2(v.y, q[2], q[3]);
+    e4m3x4_to_f16x2x2(v.z, q[4], q[5]);
+    e4m3x4_to_f16x2x2(v.w, q[6], q[7]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = hmul2_u32(q[e], s2);
+  }
+}
+
+// B slot geometry of a pass of pc tokens: boxes of 32 rows per sub-stage tile (rounded up to a power
+// of two, so that tiles tile a 16 KB slot), and the sub-stages one slot holds
+struct BGeom {
+  int nbox, nboxp, spb;
+};
+__device__ __forceinline__ BGeom bgeom(int pc, int nb) {
+  BGeom b;
+  b.nbox = (pc + BOX_ROWS - 1) / BOX_ROWS;
+  b.nboxp = b.nbox <= 1 ? 1 : (b.nbox <= 2 ? 2 : 4);
+  b.spb = (B_BYTES / BOX_BYTES) / (b.nboxp * nb);
+  return b;
+}
+
 template <int FMT_R>
-__global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant__ WideArgs wa) {
+__global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant__ WideArgs wa) {
   const GroupedArgs& a = wa.g;
   extern __shared__ uint8_t dyn_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~(uintptr_t)1023);
@@ -178,10 +236,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
   if (tid == 0) {
     for (int s = 0; s < SC; ++s) {
       mbar_init(smem_addr(&sm.sfull[s]), 1);
-      mbar_init(smem_addr(&sm.sempty[s]), 4);
+      mbar_init(smem_addr(&sm.sempty[s]), NWORK);
     }
     for (int s = 0; s < SAR; ++s) {
-      mbar_init(smem_addr(&sm.afull[s]), 4);
+      mbar_init(smem_addr(&sm.afull[s]), NWORK);
       mbar_init(smem_addr(&sm.aempty[s]), 1);
     }
     for (int s = 0; s < SBR; ++s) {
@@ -190,7 +248,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_addr(&sm.accfull[s]), 1);
-      mbar_init(smem_addr(&sm.accempty[s]), 4);
+      mbar_init(smem_addr(&sm.accempty[s]), NWORK);
     }
     mbar_init(smem_addr(&sm.drain), 1);
     sm.abort = 0;
@@ -212,30 +270,33 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
   const int P = a.m * a.topk;
   const int K = a.k;
   const int nsub = K / 64;
+  const int nst = K / 128;
   const int nrb = a.n_rows / 128;
-  const int n_pass = (a.has_shared ? wa.plan.n_sh_pass : 0) +
-                     (a.mode == MODE_DENSE ? 0 : wa.plan.pass_off[*a.n_active]);
+  const int nb = wa.b_split ? 2 : 1;              // B tiles per sub-stage (hi, lo)
+  const int wn = wa.b_split ? WN / 2 : WN;        // tokens per pass
+  const int n_pass = (a.has_shared ? wa.plan.n_sh_pass : 0) + wa.plan.pass_off[*a.n_active];
   const int n_items = n_pass * nrb;
   const bool w13 = a.mode == MODE_W13;
-  const int nb = wa.b_split ? 2 : 1;   // B tiles per sub-stage
-  auto item_fmt = [&](const Item& it) { return it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R; };
-  auto pass_tokens = [&](const Item& it) { return min(WN, it.cnt - it.pb); };
+  // shared expert items are FP8; f16 operands for every format but MXFP4
+  auto item_fmt = [&](const Item& it) { return it.shared ? FMT_FP8 : FMT_R; };
+  auto pass_tokens = [&](const Item& it) { return min(wn, it.cnt - it.pb); };
   auto wait = [&](uint32_t bar, uint32_t parity) { return wait_bounded(abort_flag, err, bar, parity, WAIT_LIMIT); };
   auto warp_wait = [&](uint32_t bar, uint32_t parity) { return __all_sync(0xffffffffu, wait(bar, parity)); };
 
   if (warp == PRODUCER_WARP) {
+    // weight stages (TMA) and their scales (bulk copies)
     if (elect_one()) {
-      prefetch_map(&wa.map_b);
+      if (wa.use_w4) prefetch_map(&wa.map_w4);
       if (wa.use_w8) prefetch_map(&wa.map_w8);
       if (wa.use_w8_sh) prefetch_map(&wa.map_w8_sh);
     }
     __syncwarp();
-    uint32_t c = 0, gb = 0;   // compact stages (staging ring), B tiles (B ring)
+    uint32_t c = 0;   // compact stages (staging ring)
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, wa.plan, blockIdx.x, nrb) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, wa.plan, item + gridDim.x, nrb);
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
       if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(err) != 0)) {
         *abort_flag = 1;
         break;
@@ -243,99 +304,122 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
       const int fmt = item_fmt(it);
       const bool fp4 = fmt != FMT_FP8;
       const WeightSet& ws = it.shared ? a.shared : a.routed;
-      const int nst = K / 128;
       const uint32_t sb = fmt == FMT_NVFP4 ? 1024u : (fmt == FMT_MXFP4 ? 512u : 16u);
-      const uint8_t* wbase = ws.w + (it.shared ? 0 : (size_t)it.expert * ws.w_stride) + (size_t)it.rb * nst * 8192;
       const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)it.rb * nst * sb;
-      const int row8 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;   // FP8 bank row of stage 0
-      const CUtensorMap* map8 = it.shared ? &wa.map_w8_sh : &wa.map_w8;
-      const int pc = pass_tokens(it);
-      const int nbox = (pc + BOX_ROWS - 1) / BOX_ROWS;
-      const int brow0 = it.shared ? P + it.pb : it.base + it.pb;
-      for (int i = 0; i < nsub && ok; ++i) {
-        if (!fp4 || (i & 1) == 0) {
-          const uint32_t s = c % SC;
-          if (!warp_wait(smem_addr(&sm.sempty[s]), ((c / SC) & 1u) ^ 1u)) {
-            ok = false;
-            break;
-          }
-          if (elect_one()) {
-            const uint32_t bar = smem_addr(&sm.sfull[s]);
-            mbar_expect_tx(bar, 8192u + sb);
-            if (fp4) {
-              bulk_g2s(smem_addr(sm.stg[s]), wbase + (size_t)(i >> 1) * 8192, 8192, bar);
-              bulk_g2s(smem_addr(sm.stg[s] + STG_W), sbase + (size_t)(i >> 1) * sb, sb, bar);
-            } else {
-              tma_load_2d(smem_addr(sm.stg[s]), map8, (i & 1) * 64, row8 + (i >> 1) * 128, bar);
-              bulk_g2s(smem_addr(sm.stg[s] + STG_W), sbase + (size_t)(i >> 1) * 16, 16, bar);
-            }
-          }
-          __syncwarp();
-          ++c;
+      const int row0 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;   // bank row of stage 0
+      const CUtensorMap* mapw = fp4 ? &wa.map_w4 : (it.shared ? &wa.map_w8_sh : &wa.map_w8);
+      const int nstg = fp4 ? nst : nsub;
+      for (int st = 0; st < nstg; ++st, ++c) {
+        const uint32_t s = c % SC;
+        if (!warp_wait(smem_addr(&sm.sempty[s]), ((c / SC) & 1u) ^ 1u)) {
+          ok = false;
+          break;
         }
-        for (int h = 0; h < nb; ++h, ++gb) {
-          const uint32_t sbf = gb % SBR;
-          if (!warp_wait(smem_addr(&sm.bempty[sbf]), ((gb / SBR) & 1u) ^ 1u)) {
-            ok = false;
-            break;
-          }
-          if (elect_one()) {
-            const uint32_t bar = smem_addr(&sm.bfull[sbf]);
-            const int row = brow0 + h * wa.b_lo_row;
-            mbar_expect_tx(bar, (uint32_t)nbox * BOX_ROWS * 128u);
-            for (int b = 0; b < nbox; ++b)
-              tma_load_2d(smem_addr(sm.B[sbf] + b * BOX_ROWS * 128), &wa.map_b, i * 64, row + b * BOX_ROWS, bar);
-          }
-          __syncwarp();
+        if (elect_one()) {
+          const uint32_t bar = smem_addr(&sm.sfull[s]);
+          mbar_expect_tx(bar, 8192u + sb);
+          if (fp4)
+            tma_load_2d(smem_addr(sm.stg[s]), mapw, 0, (row0 >> 1) + st * 64, bar);
+          else
+            tma_load_2d(smem_addr(sm.stg[s]), mapw, (st & 1) * 64, row0 + (st >> 1) * 128, bar);
+          bulk_g2s(smem_addr(sm.stg[s] + STG_W), sbase + (size_t)(fp4 ? st : st >> 1) * sb, sb, bar);
         }
+        __syncwarp();
       }
     }
     // copies still in flight (only when a wait gave up) land before the CTA exits
     for (uint32_t h = c > (uint32_t)SC ? c - SC : 0; h < c; ++h)
       for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
         if (mbar_try_wait(smem_addr(&sm.sfull[h % SC]), (h / SC) & 1u)) break;
+  } else if (warp == BLOAD_WARP) {
+    // B slots: one bulk copy per sub-stage and plane. In the chunk-major padded matrix a pass's rows
+    // of one 64-K chunk are one contiguous run of 128-byte rows, already 128B-swizzled by row index;
+    // the pass starts at a multiple of 8 rows, so the copy lands in exactly the layout the MMA's
+    // descriptor reads (row t at 128 t, 16-byte chunk k at (k ^ (t & 7)) * 16). Only the pass's
+    // rows (rounded up to 8) are copied: the MMA's rows beyond them feed output columns the
+    // epilogue never reads.
+    uint32_t gb = 0;
+    bool ok = true;
+    const size_t plane = (size_t)(K / 64) * (size_t)wa.r_pad * 128;
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const Item it = nxt;
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
+      const int pc = pass_tokens(it);
+      const BGeom bg = bgeom(pc, nb);
+      const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
+      const uint32_t bytes = (uint32_t)((pc + 7) & ~7) * 128u;
+      for (int i = 0; i < nsub; i += bg.spb, ++gb) {
+        const uint32_t sbf = gb % SBR;
+        if (!warp_wait(smem_addr(&sm.bempty[sbf]), ((gb / SBR) & 1u) ^ 1u)) {
+          ok = false;
+          break;
+        }
+        const int cnt = min(bg.spb, nsub - i);
+        if (elect_one()) {
+          const uint32_t bar = smem_addr(&sm.bfull[sbf]);
+          mbar_expect_tx(bar, (uint32_t)(cnt * nb) * bytes);
+          for (int j = 0; j < cnt; ++j)
+            for (int h = 0; h < nb; ++h)
+              bulk_g2s(smem_addr(sm.B[sbf] + (j * nb + h) * bg.nboxp * BOX_BYTES),
+                       wa.bmat + h * plane + ((size_t)(i + j) * wa.r_pad + brow0) * 128, bytes, bar);
+        }
+        __syncwarp();
+      }
+    }
+    // copies still in flight (only when a wait gave up) land before the CTA exits
     for (uint32_t h = gb > (uint32_t)SBR ? gb - SBR : 0; h < gb; ++h)
       for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
         if (mbar_try_wait(smem_addr(&sm.bfull[h % SBR]), (h / SBR) & 1u)) break;
   } else if (warp == MMA_WARP) {
-    uint32_t g = 0, gb = 0, np = 0;  // sub-stages (A ring), B tiles, passes (accumulator buffers)
+    uint32_t g = 0, gb = 0, np = 0;  // staging stages (A slots), B slots, passes (accumulator buffers)
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, wa.plan, blockIdx.x, nrb) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++np) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, wa.plan, item + gridDim.x, nrb);
-      const uint32_t n = (uint32_t)((pass_tokens(it) + 15) & ~15);
-      const uint32_t id = idesc_bf16(n);
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
+      const int pc = pass_tokens(it);
+      const BGeom bg = bgeom(pc, nb);
+      const bool fp4 = item_fmt(it) != FMT_FP8;
+      const int nstg = fp4 ? nst : nsub, spst = fp4 ? 2 : 1;   // staging stages, sub-stages per stage
+      const uint32_t n = (uint32_t)((pc + 15) & ~15);
+      const uint32_t id = item_fmt(it) == FMT_MXFP4 ? idesc_bf16(n) : idesc_f16(n);
       const uint32_t buf = np & 1u;
       const uint32_t tacc = tbase + buf * WN;
       if (!warp_wait(smem_addr(&sm.accempty[buf]), ((np >> 1) & 1u) ^ 1u)) break;
-      for (int i = 0; i < nsub && ok; ++i, ++g) {
+      int i = 0;   // sub-stage
+      for (int st = 0; st < nstg && ok; ++st, ++g) {
         const uint32_t sa = g % SAR;
+        const uint32_t ta = tbase + A_COL0 + sa * A_COLS;
         if (!warp_wait(smem_addr(&sm.afull[sa]), (g / SAR) & 1u)) {
           ok = false;
           break;
         }
-        const uint32_t abase = smem_addr(sm.A[sa]);
-        for (int h = 0; h < nb; ++h, ++gb) {
+        for (int u = 0; u < spst; ++u, ++i) {
           const uint32_t sbf = gb % SBR;
-          if (!warp_wait(smem_addr(&sm.bfull[sbf]), (gb / SBR) & 1u)) {
+          const int j = i % bg.spb;
+          if (j == 0 && !warp_wait(smem_addr(&sm.bfull[sbf]), (gb / SBR) & 1u)) {
             ok = false;
             break;
           }
           fence_after();
-          const uint32_t bbase = smem_addr(sm.B[sbf]);
+          const bool last_in_slot = j == bg.spb - 1 || i == nsub - 1;
           if (elect_one()) {
+            for (int h = 0; h < nb; ++h) {
+              const uint32_t bbase = smem_addr(sm.B[sbf] + (j * nb + h) * bg.nboxp * BOX_BYTES);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_f16(tacc, sdesc(abase + k * 32), sdesc(bbase + k * 32), id, (i > 0 || h > 0 || k > 0) ? 1u : 0u);
-            commit(smem_addr(&sm.bempty[sbf]));
+              for (int k = 0; k < 4; ++k)
+                mma_f16_ts(tacc, ta + 32 * u + 8 * k, sdesc(bbase + k * 32), id, (i > 0 || h > 0 || k > 0) ? 1u : 0u);
+            }
+            if (last_in_slot) commit(smem_addr(&sm.bempty[sbf]));
           }
           __syncwarp();
+          if (last_in_slot) ++gb;
         }
         if (!ok) break;
         if (elect_one()) {
           commit(smem_addr(&sm.aempty[sa]));
-          if (i == nsub - 1) commit(smem_addr(&sm.accfull[buf]));
+          if (st == nstg - 1) commit(smem_addr(&sm.accfull[buf]));
         }
         __syncwarp();
       }
@@ -345,39 +429,43 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
     for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
       if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
   } else {
-    // ── convert + epilogue (warps 0-3): thread r = weight row r = TMEM lane r ──
-    const int r = tid;
+    // ── convert + epilogue (warps 0-7): thread (row r = TMEM lane r, half hh) ──
+    const int r = tid & 127, hh = tid >> 7;
     uint32_t g = 0, c = 0, np = 0;
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, wa.plan, blockIdx.x, nrb) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++np) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, wa.plan, item + gridDim.x, nrb);
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
       const int fmt = item_fmt(it);
       const bool fp4 = fmt != FMT_FP8;
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pc = pass_tokens(it);
-      // the pass's tokens, 32 per chunk: lane t of chunk j holds token 32j + t's output row and weight
-      int my_orow[WN / 32];
-      float my_wgt[WN / 32];
+      const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
+      // this half's column chunks (32 tokens each, j = 2jj + hh): lane t holds token 32j + t's
+      // output row, weight and the power of two its B row was divided by
+      int my_orow[WN / 64];
+      float my_wgt[WN / 64], my_cb[WN / 64];
 #pragma unroll
-      for (int j = 0; j < WN / 32; ++j) {
-        my_orow[j] = 0;
-        my_wgt[j] = 1.f;
-        const int t = 32 * j + lane;
+      for (int jj = 0; jj < WN / 64; ++jj) {
+        my_orow[jj] = 0;
+        my_wgt[jj] = 1.f;
+        my_cb[jj] = 1.f;
+        const int t = 32 * (2 * jj + hh) + lane;
         if (t < pc) {
           const int i = it.pb + t;
-          if (it.shared) {
-            my_orow[j] = a.mode == MODE_DENSE ? i : P + i;
+          my_cb[jj] = wa.cvec[brow0 + t];
+          if (w13) {
+            my_orow[jj] = brow0 + t;   // h rows live in the padded row space of the W2 B operand
+            if (!it.shared) {
+              const int qp = it.base + i;
+              my_wgt[jj] = a.topk_w[(size_t)a.pair_tok[qp] * a.topk + a.pair_slot[qp]];
+            }
+          } else if (it.shared) {
+            my_orow[jj] = P + i;
           } else {
             const int qp = it.base + i;
-            const int tok = a.pair_tok[qp], slot = a.pair_slot[qp];
-            if (w13) {
-              my_orow[j] = qp;
-              my_wgt[j] = a.topk_w[(size_t)tok * a.topk + slot];
-            } else {
-              my_orow[j] = tok * a.topk + slot;
-            }
+            my_orow[jj] = a.pair_tok[qp] * a.topk + a.pair_slot[qp];
           }
         }
       }
@@ -386,64 +474,78 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
         const float* tsp = ws.ts + (it.shared ? 0 : (size_t)it.expert * ws.ts_stride);
         ts = (w13 && r >= 64) ? tsp[1] : tsp[0];
       }
-      // convert every sub-stage of the pass
-      for (int i = 0; i < nsub; ++i, ++g) {
+      float ca = 1.f, ica = 1.f;   // FP8: c_A and its reciprocal, from the item's first block scale
+      const int nstg = fp4 ? nst : nsub;
+      const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+      // convert every staging stage of the pass into the TMEM A ring
+      for (int st = 0; st < nstg; ++st, ++g, ++c) {
         const uint32_t s = c % SC, sa = g % SAR;
-        if (!fp4 || (i & 1) == 0) {
-          if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
-        }
+        if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
         if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.aempty[sa]), ((g / SAR) & 1u) ^ 1u));
-        if (ok) {
-          const uint8_t* stg = sm.stg[s];
-          uint8_t* dst = sm.A[sa] + r * 128;
-          if (fmt == FMT_FP8) {
-            const float* sw = reinterpret_cast<const float*>(stg + STG_W);
-            convert_row<FMT_FP8>(stg + r * 64, 0u, w13 ? sw[r >= 64 ? 1 : 0] : sw[0], dst, r);
-          } else if (fmt == FMT_NVFP4) {
-            const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(stg + STG_W + r * 8 + (i & 1) * 4);
-            convert_row<FMT_NVFP4>(stg + r * 64 + (i & 1) * 32, sc4, 0.f, dst, r);
-          } else {
-            const uint32_t sc2 = *reinterpret_cast<const uint16_t*>(stg + STG_W + r * 4 + (i & 1) * 2);
-            convert_row<FMT_MXFP4>(stg + r * 64 + (i & 1) * 32, sc2, 0.f, dst, r);
+        if (!ok) continue;
+        fence_after();
+        const uint8_t* stg = sm.stg[s];
+        const uint32_t ta = tbase + lanes + A_COL0 + sa * A_COLS;
+        if (fmt == FMT_FP8) {
+          const float sw = reinterpret_cast<const float*>(stg + STG_W)[w13 && r >= 64 ? 1 : 0];
+          if (st == 0) {
+            ca = sw > 0.f ? sw * 16.f : 1.f;
+            ica = 1.f / ca;
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) arrive(smem_addr(&sm.afull[sa]));
+          uint32_t v[16];
+          convert_fp8(stg, r, hh, f16_splat(sw * ica), v);
+          st16(ta + 16 * hh, v);
+        } else {
+          uint32_t v[32];
+          if (fmt == FMT_NVFP4)
+            convert_nvfp4(stg, r, hh, v);
+          else
+            convert_mxfp4(stg, r, hh, v);
+          st32(ta + 32 * hh, v);
         }
-        if (!fp4 || (i & 1) == 1) {
-          __syncwarp();
-          if (ok && lane == 0) arrive(smem_addr(&sm.sempty[s]));
-          ++c;
+        st_wait();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          arrive(smem_addr(&sm.afull[sa]));
+          arrive(smem_addr(&sm.sempty[s]));
         }
       }
-      // epilogue: this pass's accumulator -> h (W13, SwiGLU) or o (W2 / dense)
+      // epilogue: this pass's accumulator -> h (W13, SwiGLU) or o (W2); each half of the workers
+      // takes every other 32-column chunk
       const uint32_t buf = np & 1u;
       if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
-      if (bar1_any(!ok || *abort_flag)) break;
+      if (bar_any(1, 32 * NWORK, !ok || *abort_flag)) break;
       fence_after();
-      const uint32_t taddr = tbase + ((uint32_t)(warp * 32) << 16) + buf * WN;
+      const uint32_t taddr = tbase + ((uint32_t)((warp & 3) * 32) << 16) + buf * WN;
       const int I = a.n_rows / 2;
+      const float cab = ca * ts;
 #pragma unroll
-      for (int j = 0; j < WN / 32; ++j) {
-        if (32 * j >= pc) break;                       // uniform across the workers
+      for (int jj = 0; jj < WN / 64; ++jj) {
+        const int j = 2 * jj + hh;
+        if (32 * j >= pc) break;                       // uniform across this half's warps
         uint32_t d[32];
         ld32(taddr + 32 * j, d);
         ld_wait();
         if (w13) {
           if (r >= 64) {
 #pragma unroll
-            for (int t = 0; t < 32; ++t) sm.xchg[r - 64][t] = bf16_round(__uint_as_float(d[t]) * ts);
+            for (int t = 0; t < 32; ++t) {
+              const float cb = __shfl_sync(0xffffffffu, my_cb[jj], t);
+              sm.xchg[hh][r - 64][t] = __float2bfloat16_rn(__uint_as_float(d[t]) * cb * cab);
+            }
           }
-          asm volatile("bar.sync 1, 128;\n" ::: "memory");
+          bar_sync(2 + hh, 128);
           if (r < 64) {
             const float lim = a.swiglu_limit;
 #pragma unroll
             for (int t = 0; t < 32; ++t) {
-              const int orow = __shfl_sync(0xffffffffu, my_orow[j], t);
-              const float wgt = __shfl_sync(0xffffffffu, my_wgt[j], t);
+              const int orow = __shfl_sync(0xffffffffu, my_orow[jj], t);
+              const float wgt = __shfl_sync(0xffffffffu, my_wgt[jj], t);
+              const float cb = __shfl_sync(0xffffffffu, my_cb[jj], t);
               if (32 * j + t < pc) {
-                float gv = bf16_round(__uint_as_float(d[t]) * ts);
-                float uv = sm.xchg[r][t];
+                float gv = bf16_round(__uint_as_float(d[t]) * cb * cab);
+                float uv = __bfloat162float(sm.xchg[hh][r][t]);
                 if (lim > 0.f) {
                   uv = fminf(fmaxf(uv, -lim), lim);
                   gv = fminf(gv, lim);
@@ -454,13 +556,15 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
               }
             }
           }
-          asm volatile("bar.sync 1, 128;\n" ::: "memory");
+          bar_sync(2 + hh, 128);
         } else {
           const int n0 = it.rb * 128;
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
-            const int orow = __shfl_sync(0xffffffffu, my_orow[j], t);
-            if (32 * j + t < pc) a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(__uint_as_float(d[t]) * ts);
+            const int orow = __shfl_sync(0xffffffffu, my_orow[jj], t);
+            const float cb = __shfl_sync(0xffffffffu, my_cb[jj], t);
+            if (32 * j + t < pc)
+              a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(__uint_as_float(d[t]) * cb * cab);
           }
         }
       }
@@ -476,95 +580,167 @@ __global__ void __launch_bounds__(NTHREADS, 2) tcw_kernel(const __grid_constant_
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(TMEM_COLS));
 }
 
-// ── activation matrices of the wide path (B operands) ──
-// W13: row q < P = dequant(act_quant(x))[pair_tok[q]] (routed pairs in expert order), row P + i = the
-// same of token i (the shared expert). W2: row q = dequant(act_quant(h))[q] for every row of h.
-// dequant(act_quant(v)) = e4m3 code * its per-128 scale, formed in fp32. bf16 holds it exactly when
-// the scale is a power of two; otherwise (split) rows `rows + q` hold the residual bf16(v - hi).
-__device__ __forceinline__ void store_hi_lo(const float (&v)[8], __nv_bfloat16* hi, int64_t lo_off, int split) {
+// ── activation matrices of the wide path (B operands), one warp per row ──
+// Row space: routed pair q of expert e at pbase(offsets[e], e) + (q - offsets[e]), the shared
+// expert's token i at sb_row + i (W13: the same x row; W2: the rows of h, which the W13 epilogue
+// writes in this row space). Layout chunk-major: [plane][k/64][r_pad][64 values], the 16-byte chunk
+// c of a row's 64-K chunk stored at position c ^ (row & 7).
+// The values: dequant(act_quant(v)) = e4m3 code x its per-128 scale, formed in fp32 and divided by
+// the row's c_B (cvec[row]): f16 rows use c_B = 2^ceil(log2(max scale)) / 128, bf16 rows (routed
+// rows of MXFP4 layers) c_B = 1. Exact in 16 bits for power-of-two scales; otherwise (split) the
+// second plane holds the residuals v - hi.
+template <bool BF>
+__device__ __forceinline__ void store_hi_lo(const float (&v)[8], uint16_t* hi, int64_t lo_off, int split) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-    h[j] = *reinterpret_cast<const uint32_t*>(&b);
-    const float2 bf = __bfloat1622float2(b);
-    const __nv_bfloat162 r = __floats2bfloat162_rn(v[2 * j] - bf.x, v[2 * j + 1] - bf.y);
-    l[j] = *reinterpret_cast<const uint32_t*>(&r);
+    if (BF) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      const float2 back = __bfloat1622float2(b);
+      const __nv_bfloat162 rr = __floats2bfloat162_rn(v[2 * j] - back.x, v[2 * j + 1] - back.y);
+      h[j] = *reinterpret_cast<const uint32_t*>(&b);
+      l[j] = *reinterpret_cast<const uint32_t*>(&rr);
+    } else {
+      const __half2 b = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+      const float2 back = __half22float2(b);
+      const __half2 rr = __floats2half2_rn(v[2 * j] - back.x, v[2 * j + 1] - back.y);
+      h[j] = *reinterpret_cast<const uint32_t*>(&b);
+      l[j] = *reinterpret_cast<const uint32_t*>(&rr);
+    }
   }
   *reinterpret_cast<uint4*>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
   if (split) *reinterpret_cast<uint4*>(hi + lo_off) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// element offset of the 8-value chunk v (k = 8v .. 8v+7) of row `row`
+__device__ __forceinline__ int64_t cm_off(int64_t row, int v, int64_t r_pad) {
+  return ((int64_t)(v >> 3) * r_pad + row) * 64 + (((v & 7) ^ (int)(row & 7)) << 3);
+}
+
+__device__ __forceinline__ float row_c(float smax, bool bf) { return bf ? 1.f : pow2_ceil(smax) * (1.f / 128.f); }
+
 __global__ void __launch_bounds__(256) wide_x_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs,
-                                                     const int32_t* __restrict__ pair_tok, int m, int P, int h,
-                                                     int split, __nv_bfloat16* __restrict__ xw) {
+                                                     const int32_t* __restrict__ pair_tok,
+                                                     const int32_t* __restrict__ offsets, int n_experts, int m, int P,
+                                                     int h, int64_t r_pad, int sb_row, int split, int routed_bf16,
+                                                     uint16_t* __restrict__ xw, float* __restrict__ cvec) {
   pdl_wait();
   pdl_trigger();
-  const int nv = h / 8, nkb = h / 128;
-  const int64_t rows = (int64_t)(P + m), units = rows * nv;
-  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
-    const int row = (int)(u / nv), v = (int)(u % nv);
-    const int tok = row < P ? pair_tok[row] : row - P;
-    const uint2 qv = *reinterpret_cast<const uint2*>(xq + (size_t)tok * h + v * 8);
-    const float s = xs[(size_t)tok * nkb + (v * 8) / 128];
-    uint32_t hh[4];
-    e4m3x4_to_f16x2x2(qv.x, hh[0], hh[1]);
-    e4m3x4_to_f16x2x2(qv.y, hh[2], hh[3]);
-    float f[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hh[j]));
-      f[2 * j] = t.x * s;
-      f[2 * j + 1] = t.y * s;
+  const int lane = threadIdx.x & 31;
+  const int nkb = h / 128;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t q = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; q < P + m; q += nw) {
+    int tok, row;
+    if (q < P) {
+      int lo = 0, hi = n_experts;   // the expert of pair q: the last e with offsets[e] <= q
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (offsets[mid] <= q) lo = mid; else hi = mid;
+      }
+      tok = pair_tok[q];
+      row = pbase(offsets[lo], lo) + (int)(q - offsets[lo]);
+    } else {
+      tok = (int)(q - P);
+      row = sb_row + tok;
     }
-    store_hi_lo(f, xw + (size_t)row * h + v * 8, rows * h, split);
+    const bool bf = routed_bf16 && q < P;
+    const float* sr = xs + (size_t)tok * nkb;
+    float smax = 0.f;
+    for (int b = lane; b < nkb; b += 32) smax = fmaxf(smax, sr[b]);
+    const float cb = row_c(warp_max(smax), bf);
+    const float icb = 1.f / cb;   // a power of two
+    for (int v = lane; v < h / 8; v += 32) {
+      const uint2 qv = *reinterpret_cast<const uint2*>(xq + (size_t)tok * h + v * 8);
+      const float s = sr[v >> 4] * icb;
+      uint32_t hh[4];
+      e4m3x4_to_f16x2x2(qv.x, hh[0], hh[1]);
+      e4m3x4_to_f16x2x2(qv.y, hh[2], hh[3]);
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hh[j]));
+        f[2 * j] = t.x * s;
+        f[2 * j + 1] = t.y * s;
+      }
+      if (bf)
+        store_hi_lo<true>(f, xw + cm_off(row, v, r_pad), r_pad * h, split);
+      else
+        store_hi_lo<false>(f, xw + cm_off(row, v, r_pad), r_pad * h, split);
+    }
+    if (lane == 0) cvec[row] = cb;
   }
 }
 
-// one warp per (row, 128-block) of h: act_quant (kernel.py:40-125), then back to bf16 (hi, and the
-// residual plane at rows + row when the scales are fp32)
-__global__ void __launch_bounds__(256) wide_h_kernel(const __nv_bfloat16* __restrict__ hbf, int64_t rows, int k,
-                                                     int pow2, __nv_bfloat16* __restrict__ hw) {
+// act_quant (kernel.py:40-125) of row `row` of h (rows of the padded row space; padding rows hold
+// no data and their results are never read), block by block, then back to 16 bits: lane l holds
+// values 4l..4l+3 of each 128-block; a first sweep finds the row's largest scale (for c_B)
+__global__ void __launch_bounds__(256) wide_h_kernel(const __nv_bfloat16* __restrict__ hbf, int64_t rows,
+                                                     int64_t r_pad, int sb_row, int k, int pow2, int routed_bf16,
+                                                     uint16_t* __restrict__ hw, float* __restrict__ cvec) {
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int nkb = k / 128;
-  const int64_t units = rows * nkb;
-  for (int64_t u = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; u < units;
-       u += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-    const int64_t row = u / nkb;
-    const int b = (int)(u % nkb);
-    const uint2 raw = *reinterpret_cast<const uint2*>(hbf + row * k + b * 128 + lane * 4);
-    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
-    const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
-    float am = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
-    am = warp_max(am);
-    const float sc = act_scale(am, pow2 != 0);
-    float q[4];
-    if (pow2) {
-      const float inv = __frcp_rn(sc);   // exact: a power of two
-      q[0] = e4m3_to_f32(act_q_pow2(f0.x, inv));
-      q[1] = e4m3_to_f32(act_q_pow2(f0.y, inv));
-      q[2] = e4m3_to_f32(act_q_pow2(f1.x, inv));
-      q[3] = e4m3_to_f32(act_q_pow2(f1.y, inv));
-    } else {
-      q[0] = e4m3_to_f32(act_q(f0.x, sc));
-      q[1] = e4m3_to_f32(act_q(f0.y, sc));
-      q[2] = e4m3_to_f32(act_q(f1.x, sc));
-      q[3] = e4m3_to_f32(act_q(f1.y, sc));
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {
+    const bool bf = routed_bf16 && row < sb_row;
+    const __nv_bfloat16* hr = hbf + row * k;
+    // the block's 4 values of this lane, and the block's amax
+    auto load = [&](int b, float (&f)[4]) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(hr + b * 128 + lane * 4);
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
+      f[0] = f0.x;
+      f[1] = f0.y;
+      f[2] = f1.x;
+      f[3] = f1.y;
+      return warp_max(fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3]))));
+    };
+    float smax = 0.f;
+    for (int b = 0; b < nkb; ++b) {
+      float f[4];
+      smax = fmaxf(smax, act_scale(load(b, f), pow2 != 0));
     }
-    uint32_t hv[2], lv[2];
+    const float cb = row_c(smax, bf);
+    const float icb = 1.f / cb;
+    for (int b = 0; b < nkb; ++b) {
+      float f[4];
+      const float sc = act_scale(load(b, f), pow2 != 0);
+      float q[4];
+      if (pow2) {
+        const float inv = __frcp_rn(sc);   // exact: a power of two
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const float v0 = q[2 * j] * sc, v1 = q[2 * j + 1] * sc;
-      const __nv_bfloat162 hb = __floats2bfloat162_rn(v0, v1);
-      const float2 hf = __bfloat1622float2(hb);
-      const __nv_bfloat162 lb = __floats2bfloat162_rn(v0 - hf.x, v1 - hf.y);
-      hv[j] = *reinterpret_cast<const uint32_t*>(&hb);
-      lv[j] = *reinterpret_cast<const uint32_t*>(&lb);
+        for (int e = 0; e < 4; ++e) q[e] = e4m3_to_f32(act_q_pow2(f[e], inv));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) q[e] = e4m3_to_f32(act_q(f[e], sc));
+      }
+      const float s = sc * icb;
+      uint32_t hv[2], lv[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float v0 = q[2 * j] * s, v1 = q[2 * j + 1] * s;
+        if (bf) {
+          const __nv_bfloat162 hb = __floats2bfloat162_rn(v0, v1);
+          const float2 hf = __bfloat1622float2(hb);
+          const __nv_bfloat162 lb = __floats2bfloat162_rn(v0 - hf.x, v1 - hf.y);
+          hv[j] = *reinterpret_cast<const uint32_t*>(&hb);
+          lv[j] = *reinterpret_cast<const uint32_t*>(&lb);
+        } else {
+          const __half2 hb = __floats2half2_rn(v0, v1);
+          const float2 hf = __half22float2(hb);
+          const __half2 lb = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+          hv[j] = *reinterpret_cast<const uint32_t*>(&hb);
+          lv[j] = *reinterpret_cast<const uint32_t*>(&lb);
+        }
+      }
+      // values 4 lane .. 4 lane + 3 of block b: half of an 8-value chunk
+      const int v = b * 16 + (lane >> 1);
+      const int64_t off = cm_off(row, v, r_pad) + (lane & 1) * 4;
+      *reinterpret_cast<uint2*>(hw + off) = make_uint2(hv[0], hv[1]);
+      if (!pow2) *reinterpret_cast<uint2*>(hw + off + r_pad * k) = make_uint2(lv[0], lv[1]);
     }
-    *reinterpret_cast<uint2*>(hw + row * k + b * 128 + lane * 4) = make_uint2(hv[0], hv[1]);
-    if (!pow2) *reinterpret_cast<uint2*>(hw + (rows + row) * k + b * 128 + lane * 4) = make_uint2(lv[0], lv[1]);
+    if (lane == 0) cvec[row] = cb;
   }
 }
 
@@ -608,31 +784,41 @@ static cudaError_t launch_one(const WideArgs& a, int grid, cudaStream_t st) {
   return launch_pdl(tcw_kernel<F>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
 }
 
+static unsigned warp_grid(int64_t rows) {
+  const int64_t b = (rows + 7) / 8;   // one warp per row, 8 warps per block
+  return (unsigned)(b < 1 ? 1 : (b > 65535 ? 65535 : b));
+}
+
 }  // namespace tcw
 
-cudaError_t launch_tc_wide(const GroupedArgs& g, const TcPlan& plan, const void* bmat, int64_t b_rows, int split,
-                           int max_items, cudaStream_t st) {
+cudaError_t launch_tc_wide(const GroupedArgs& g, const TcPlan& plan, const void* bmat, const float* cvec,
+                           int64_t r_pad, int sb_row, int split, int max_items, cudaStream_t st) {
+  if (g.mode == MODE_DENSE) return cudaErrorInvalidValue;
   tcw::WideArgs a;
   a.g = g;
   a.plan = plan;
+  a.cvec = cvec;
+  a.r_pad = r_pad;
+  a.sb_row = sb_row;
   a.b_split = split ? 1 : 0;
-  a.b_lo_row = (int)b_rows;
   const uint64_t nst = (uint64_t)g.k / 128, nrb = (uint64_t)g.n_rows / 128;
-  cudaError_t e = tcw::encode(&a.map_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bmat, (uint64_t)g.k,
-                              (uint64_t)b_rows * (split ? 2 : 1), (uint64_t)g.k * 2, 64, tcw::BOX_ROWS,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint64_t bank_rows = (uint64_t)g.n_experts * nrb * nst * 128;
+  a.bmat = reinterpret_cast<const uint8_t*>(bmat);
+  cudaError_t e = cudaSuccess;
+  const bool r4 = g.routed.fmt != FMT_FP8;
+  e = tcw::encode(&a.map_w4, CU_TENSOR_MAP_DATA_TYPE_UINT8, r4 ? g.routed.w : nullptr, 128, bank_rows / 2, 128, 128,
+                  64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (e != cudaSuccess) return e;
-  const bool r8 = g.mode != MODE_DENSE && g.routed.fmt == FMT_FP8;
-  e = tcw::encode(&a.map_w8, CU_TENSOR_MAP_DATA_TYPE_UINT8, r8 ? g.routed.w : nullptr, 128,
-                  (uint64_t)g.n_experts * nrb * nst * 128, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  e = tcw::encode(&a.map_w8, CU_TENSOR_MAP_DATA_TYPE_UINT8, r4 ? nullptr : g.routed.w, 128, bank_rows, 128, 64, 128,
+                  CU_TENSOR_MAP_SWIZZLE_64B);
   if (e != cudaSuccess) return e;
-  const bool s8 = g.has_shared && (g.mode != MODE_DENSE || g.shared.fmt == FMT_FP8);
-  e = tcw::encode(&a.map_w8_sh, CU_TENSOR_MAP_DATA_TYPE_UINT8, s8 ? g.shared.w : nullptr, 128, nrb * nst * 128, 128,
-                  64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  e = tcw::encode(&a.map_w8_sh, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.has_shared ? g.shared.w : nullptr, 128,
+                  nrb * nst * 128, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B);
   if (e != cudaSuccess) return e;
-  a.use_w8 = r8 ? 1 : 0;
-  a.use_w8_sh = s8 ? 1 : 0;
-  int grid = 2 * num_sms();
+  a.use_w4 = r4 ? 1 : 0;
+  a.use_w8 = r4 ? 0 : 1;
+  a.use_w8_sh = g.has_shared ? 1 : 0;
+  int grid = num_sms();   // one CTA per SM (its shared memory), persistent over the items
   if (grid > max_items) grid = max_items;
   if (grid < 1) grid = 1;
   switch (g.routed.fmt) {
@@ -642,19 +828,18 @@ cudaError_t launch_tc_wide(const GroupedArgs& g, const TcPlan& plan, const void*
   }
 }
 
-cudaError_t launch_wide_x(const uint8_t* xq, const float* xs, const int32_t* pair_tok, int m, int P, int h, int split,
-                          __nv_bfloat16* xw, cudaStream_t st) {
-  const int64_t units = (int64_t)(P + m) * (h / 8);
-  const int64_t b = (units + 255) / 256;
-  const unsigned grid = (unsigned)(b < 1 ? 1 : (b > 65535 ? 65535 : b));
-  return launch_pdl(tcw::wide_x_kernel, dim3(grid), dim3(256), 0, st, xq, xs, pair_tok, m, P, h, split, xw);
+cudaError_t launch_wide_x(const uint8_t* xq, const float* xs, const int32_t* pair_tok, const int32_t* offsets,
+                          int n_experts, int m, int P, int h, int64_t r_pad, int sb_row, int split, int routed_bf16,
+                          void* xw, float* cvec, cudaStream_t st) {
+  return launch_pdl(tcw::wide_x_kernel, dim3(tcw::warp_grid((int64_t)P + m)), dim3(256), 0, st, xq, xs, pair_tok,
+                    offsets, n_experts, m, P, h, r_pad, sb_row, split, routed_bf16, reinterpret_cast<uint16_t*>(xw),
+                    cvec);
 }
 
-cudaError_t launch_wide_h(const __nv_bfloat16* hbf, int64_t rows, int k, int pow2, __nv_bfloat16* hw, cudaStream_t st) {
-  const int64_t warps = rows * (k / 128);
-  const int64_t b = (warps * 32 + 255) / 256;
-  const unsigned grid = (unsigned)(b < 1 ? 1 : (b > 65535 ? 65535 : b));
-  return launch_pdl(tcw::wide_h_kernel, dim3(grid), dim3(256), 0, st, hbf, rows, k, pow2, hw);
+cudaError_t launch_wide_h(const __nv_bfloat16* hbf, int64_t rows, int64_t r_pad, int sb_row, int k, int pow2,
+                          int routed_bf16, void* hw, float* cvec, cudaStream_t st) {
+  return launch_pdl(tcw::wide_h_kernel, dim3(tcw::warp_grid(rows)), dim3(256), 0, st, hbf, rows, r_pad, sb_row, k,
+                    pow2, routed_bf16, reinterpret_cast<uint16_t*>(hw), cvec);
 }
 
 }  // namespace sb

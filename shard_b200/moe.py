@@ -101,9 +101,9 @@ class MoELayer:
                 a, b = tile(F.FMT_FP8, _lib.MAT_W13, s13, s13s, 1, 2 * i, h, self.layout)
                 c, d = tile(F.FMT_FP8, _lib.MAT_PLAIN, s2, s2s, 1, h, i, self.layout)
                 self.shared = (a, b, c, d)
-        # The prefill kernel dequantises weights to bf16 operands: exact for NVFP4 / MXFP4 and for FP8
-        # with power-of-two block scales (ue8m0). Layers with other FP8 scales stay on the verify kernel
-        # unless the prefill kernel is asked for explicitly.
+        # The prefill kernel dequantises weights to 16-bit operands: exact for NVFP4 / MXFP4 and for
+        # FP8 with power-of-two block scales (ue8m0). Layers with other FP8 scales stay on the verify
+        # kernel unless the prefill kernel is asked for explicitly.
         fp8_scales = [self.shared[1], self.shared[3]] if self.shared is not None else []
         if expert_fmt == F.FMT_FP8:
             fp8_scales += [self.w13_s, self.w2_s]
@@ -135,7 +135,7 @@ class MoELayer:
     @property
     def prefill(self) -> int:
         """Expert-kernel choice on the tensor-core layout: 0 by batch size (the prefill kernel once
-        the batch routes >= 4 tokens per expert), 1 always the verify kernel, 2 always the prefill
+        the batch routes >= 16 tokens per expert), 1 always the verify kernel, 2 always the prefill
         kernel."""
         return int(self.desc.prefill)
 

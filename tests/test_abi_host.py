@@ -82,10 +82,10 @@ def test_workspace_serves_every_smaller_batch_across_the_prefill_switch():
         sizes = {}
         for mode in (0, 1, 2):
             d.prefill = mode
-            sizes[mode] = [L.sb_moe_workspace_bytes(ctypes.byref(d), m) for m in range(1, 4 * e // k + 40)]
+            sizes[mode] = [L.sb_moe_workspace_bytes(ctypes.byref(d), m) for m in range(1, 16 * e // k + 40)]
             assert all(s > 0 for s in sizes[mode])
             assert sizes[mode] == sorted(sizes[mode]), (e, k, mode)
-        switch = 4 * e // k                              # first m the default sends to the prefill kernel
+        switch = 16 * e // k                             # first m the default sends to the prefill kernel
         for m in range(1, len(sizes[0]) + 1):
             below = max(sizes[1][:min(m, switch - 1)])
             assert sizes[0][m - 1] >= below
