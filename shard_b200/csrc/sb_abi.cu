@@ -37,7 +37,8 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 // The forward's scratch regions, carved from one caller-provided workspace.
 struct Workspace {
-  int32_t* err;      // offset 0: device error flag (cleared by every forward; 1 = a bounded wait gave up)
+  int32_t* err;      // offset 0: device error flag (set afresh by every forward; 1 = a bounded wait gave up);
+                     // offset 4: the tensor-core gate's flag (cleared before it runs), folded into it
   float* logits;
   int32_t* topk_idx;
   float* topk_w;
@@ -111,7 +112,7 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
     off += align256(bytes);
     return p;
   };
-  w.err = (int32_t*)take(sizeof(int32_t));
+  w.err = (int32_t*)take(2 * sizeof(int32_t));
   // partial gate logits, one [M, E] slab per 512- (or 256-) wide K split
   w.logits = (float*)take(sizeof(float) * m * E * (H / (H % 512 == 0 ? 512 : 256)));
   w.topk_idx = (int32_t*)take(sizeof(int32_t) * P);
@@ -475,7 +476,18 @@ size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
 
 static int route_impl(const sb_moe_layer* L, const void* x, int64_t m, const int64_t* ids, float* out_w,
                       int64_t* out_idx, const Workspace& w, bool quant, cudaStream_t st) {
-  int rc = cuda_check(sb::launch_gate_logits(x, L->gate_w, w.logits, (int)m, L->n_experts, L->hidden, st), "gate_logits");
+  // the prefill kernel's batches take the tensor-core gate (a token's logits then come from the
+  // same kernel whether it runs alone or in its batch, under either kernel choice)
+  if (use_wide(L, m)) {
+    const int rc0 = cuda_check(cudaMemsetAsync(w.err + 1, 0, sizeof(int32_t), st), "gate flag");
+    if (rc0) return rc0;
+  }
+  int rc = use_wide(L, m)
+               ? cuda_check(sb::launch_gate_tc(x, L->gate_w, w.logits, (int)m, L->n_experts, L->hidden,
+                                               sb::gate_ksplit(L->hidden), w.err + 1, st),
+                            "gate_tc")
+               : cuda_check(sb::launch_gate_logits(x, L->gate_w, w.logits, (int)m, L->n_experts, L->hidden, st),
+                            "gate_logits");
   if (rc) return rc;
   sb::RouteArgs r;
   r.logits = w.logits;
@@ -552,6 +564,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.pair_tok = w.pair_tok;
   p.pair_slot = w.pair_slot;
   p.err = w.err;
+  p.gate_err = use_wide(L, m) ? w.err + 1 : nullptr;
   p.pass_max = L->layout == SB_LAYOUT_TC ? (int)routed_pass_max(L, m) : 0;
   p.pass_off = L->layout == SB_LAYOUT_TC ? w.pass_off : nullptr;
   p.pass_slot = w.pass_slot;

@@ -35,7 +35,8 @@ struct PermuteArgs {
   int32_t* n_active; // [1]
   int32_t* pair_tok; // [M*K]
   int32_t* pair_slot;// [M*K]
-  int32_t* err;      // cleared here, before the grouped kernels run
+  int32_t* err;      // set here, before the grouped kernels: 0, or 1 if *gate_err is set
+  const int32_t* gate_err;   // the tensor-core gate's flag when that gate ran, else null
   int pass_max;      // tensor-core path: tokens per pass of a routed expert (0: no pass table)
   int32_t* pass_off; // [E+1] by active slot: first pass of the slot, total passes at [n_active]
   int32_t* pass_slot;// [routed passes] active slot of each pass
@@ -116,7 +117,12 @@ struct PanelArgs {
 
 __host__ __device__ inline int tc_pass_max(int fmt) { return fmt == 1 ? 8 : 16; }
 
+// K-split width of the gate logits (both kernels): 512 when H allows it, else 256 (H % 256 == 0).
+__host__ __device__ inline int gate_ksplit(int h) { return h % 512 == 0 ? 512 : 256; }
 cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int m, int e, int h, cudaStream_t st);
+// the same partial logits on the tensor cores (sb_gate.cu), for prefill batches
+cudaError_t launch_gate_tc(const void* x, const void* w, float* part, int m, int e, int h, int kspl, int* err,
+                           cudaStream_t st);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
 cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t st);
 cudaError_t launch_grouped(const GroupedArgs& a, int max_items, int grid_cap, cudaStream_t st);

@@ -21,8 +21,6 @@ namespace sb {
 // products are exact in fp32; only the summation order differs from the reference's fp32 F.linear.
 constexpr int GATE_TOKENS = 32;
 
-// K-split width of the gate GEMV: 512 when H allows it, else 256 (H % 256 == 0 is required).
-__host__ __device__ inline int gate_ksplit(int h) { return h % 512 == 0 ? 512 : 256; }
 
 __global__ void __launch_bounds__(256) gate_logits_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ w,
@@ -338,7 +336,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   const bool staged = P <= PERMUTE_SMEM_PAIRS;
   pdl_wait();
   pdl_trigger();
-  if (threadIdx.x == 0 && a.err) *a.err = 0;
+  if (threadIdx.x == 0 && a.err) *a.err = (a.gate_err != nullptr && *a.gate_err != 0) ? 1 : 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
