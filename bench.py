@@ -41,6 +41,7 @@ import torch  # noqa: E402
 HEADLINE_M = 16
 LAYERS_PER_GPU = 6
 N_EXPERTS = None       # --experts: fewer routed experts per layer (the small case for ncu captures)
+PREFILL = 0            # --prefill: expert-kernel choice of the tensor-core layout (0 by batch size)
 CHUNKS_PER_STEP = 8
 METRIC = "MoE stage tokens/s (token-layers/s), verify M=16, c1/c2 V4-Flash MoE layer"
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum of one forward's W13 and W2 grouped
@@ -163,7 +164,8 @@ def build_layers(rank, n_layers, device):
         cfg = cfg.replace(n_experts=N_EXPERTS)
     layers = []
     for j in range(n_layers):
-        layers.append(S.device_layer(cfg, layer=rank * n_layers + j, device=device, seeded=[], fill="normal"))
+        layers.append(S.device_layer(cfg, layer=rank * n_layers + j, device=device, seeded=[], fill="normal",
+                                     prefill=PREFILL))
     return cfg, layers
 
 
@@ -474,7 +476,7 @@ def cfg_sweep(name, ms, reps=4, modes=(0,)):
 
 
 def main():
-    global LAYERS_PER_GPU, N_EXPERTS
+    global LAYERS_PER_GPU, N_EXPERTS, HEADLINE_M, PREFILL
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -490,6 +492,11 @@ def main():
                     help="stage-boundary activation wire at N > 1 (fp8: the reference's e4m3 + per-row scale)")
     ap.add_argument("--layout", choices=["tc", "fragment"], default=None,
                     help="weight layout / kernel family (default: the library default)")
+    ap.add_argument("--m", type=int, default=HEADLINE_M,
+                    help="tokens per chunk (default 16, the headline; larger M with fewer --experts is the "
+                         "small case for ncu captures of the prefill kernel)")
+    ap.add_argument("--prefill", type=int, choices=[0, 1, 2], default=0,
+                    help="expert kernel on the tensor-core layout: 0 by batch size, 1 verify, 2 prefill")
     args = ap.parse_args()
     if args.layout is not None:
         import shard_b200.moe as sbm
@@ -498,6 +505,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     LAYERS_PER_GPU = args.layers
     N_EXPERTS = args.experts
+    HEADLINE_M = args.m
+    PREFILL = args.prefill
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
     local_rank = env_int("LOCAL_RANK", 0)
