@@ -372,62 +372,71 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant_
       for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
         if (mbar_try_wait(smem_addr(&sm.bfull[h % SBR]), (h / SBR) & 1u)) break;
   } else if (warp == MMA_WARP) {
-    uint32_t g = 0, gb = 0, np = 0;  // staging stages (A slots), B slots, passes (accumulator buffers)
-    bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++np) {
-      const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
-      const int pc = pass_tokens(it);
-      const BGeom bg = bgeom(pc, nb);
-      const bool fp4 = item_fmt(it) != FMT_FP8;
-      const int nstg = fp4 ? nst : nsub, spst = fp4 ? 2 : 1;   // staging stages, sub-stages per stage
-      const uint32_t n = (uint32_t)((pc + 15) & ~15);
-      const uint32_t id = item_fmt(it) == FMT_MXFP4 ? idesc_bf16(n) : idesc_f16(n);
-      const uint32_t buf = np & 1u;
-      const uint32_t tacc = tbase + buf * WN;
-      if (!warp_wait(smem_addr(&sm.accempty[buf]), ((np >> 1) & 1u) ^ 1u)) break;
-      int i = 0;   // sub-stage
-      for (int st = 0; st < nstg && ok; ++st, ++g) {
-        const uint32_t sa = g % SAR;
-        const uint32_t ta = tbase + A_COL0 + sa * A_COLS;
-        if (!warp_wait(smem_addr(&sm.afull[sa]), (g / SAR) & 1u)) {
-          ok = false;
-          break;
-        }
-        for (int u = 0; u < spst; ++u, ++i) {
-          const uint32_t sbf = gb % SBR;
-          const int j = i % bg.spb;
-          if (j == 0 && !warp_wait(smem_addr(&sm.bfull[sbf]), (gb / SBR) & 1u)) {
+    // One thread issues everything (waits, MMAs, commits are single-thread operations); the other
+    // lanes idle until the CTA's final barrier. A tcgen05 fence follows each wait, and only waits.
+    if (lane == 0) {
+      uint32_t g = 0, gb = 0, np = 0;  // staging stages (A slots), B slots, passes (accumulator buffers)
+      bool ok = true;
+      Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++np) {
+        const Item it = nxt;
+        if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
+        const int pc = pass_tokens(it);
+        const BGeom bg = bgeom(pc, nb);
+        const bool fp4 = item_fmt(it) != FMT_FP8;
+        const int nstg = fp4 ? nst : nsub, spst = fp4 ? 2 : 1;   // staging stages, sub-stages per stage
+        const uint32_t n = (uint32_t)((pc + 15) & ~15);
+        const uint32_t id = item_fmt(it) == FMT_MXFP4 ? idesc_bf16(n) : idesc_f16(n);
+        const uint32_t buf = np & 1u;
+        const uint32_t tacc = tbase + buf * WN;
+        const uint32_t tile = (uint32_t)(nb * bg.nboxp * BOX_BYTES);   // one sub-stage's B tiles
+        if (!wait(smem_addr(&sm.accempty[buf]), ((np >> 1) & 1u) ^ 1u)) break;
+        int i = 0;   // sub-stage
+        for (int st = 0; st < nstg && ok; ++st, ++g) {
+          const uint32_t sa = g % SAR;
+          const uint32_t ta = tbase + A_COL0 + sa * A_COLS;
+          if (!wait(smem_addr(&sm.afull[sa]), (g / SAR) & 1u)) {
             ok = false;
             break;
           }
-          fence_after();
-          const bool last_in_slot = j == bg.spb - 1 || i == nsub - 1;
-          if (elect_one()) {
+          bool synced = true;   // a wait since the last tcgen05 fence
+          for (int u = 0; u < spst; ++u, ++i) {
+            const uint32_t sbf = gb % SBR;
+            const int j = i & (bg.spb - 1);
+            if (j == 0) {
+              if (!wait(smem_addr(&sm.bfull[sbf]), (gb / SBR) & 1u)) {
+                ok = false;
+                break;
+              }
+              synced = true;
+            }
+            if (synced) {
+              fence_after();
+              synced = false;
+            }
+            const bool last_in_slot = j == bg.spb - 1 || i == nsub - 1;
             for (int h = 0; h < nb; ++h) {
-              const uint32_t bbase = smem_addr(sm.B[sbf] + (j * nb + h) * bg.nboxp * BOX_BYTES);
+              // K advances 16 values = 32 bytes = 2 in the descriptor's start-address field
+              const uint64_t bd = sdesc(smem_addr(sm.B[sbf]) + (uint32_t)j * tile + (uint32_t)h * (tile / nb));
 #pragma unroll
               for (int k = 0; k < 4; ++k)
-                mma_f16_ts(tacc, ta + 32 * u + 8 * k, sdesc(bbase + k * 32), id, (i > 0 || h > 0 || k > 0) ? 1u : 0u);
+                mma_f16_ts(tacc, ta + 32 * u + 8 * k, bd + 2 * k, id, (i > 0 || h > 0 || k > 0) ? 1u : 0u);
             }
-            if (last_in_slot) commit(smem_addr(&sm.bempty[sbf]));
+            if (last_in_slot) {
+              commit(smem_addr(&sm.bempty[sbf]));
+              ++gb;
+            }
           }
-          __syncwarp();
-          if (last_in_slot) ++gb;
-        }
-        if (!ok) break;
-        if (elect_one()) {
+          if (!ok) break;
           commit(smem_addr(&sm.aempty[sa]));
           if (st == nstg - 1) commit(smem_addr(&sm.accfull[buf]));
         }
-        __syncwarp();
       }
+      commit(smem_addr(&sm.drain));
+      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
     }
-    if (elect_one()) commit(smem_addr(&sm.drain));
     __syncwarp();
-    for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-      if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
   } else {
     // ── convert + epilogue (warps 0-7): thread (row r = TMEM lane r, half hh) ──
     const int r = tid & 127, hh = tid >> 7;
