@@ -26,8 +26,9 @@
 // accumulator by the powers of two c_A c_B (exact) and the NVFP4 tensor scale.
 //
 // One CTA per SM (its shared memory holds deep rings), persistent over the items. Roles (352
-// threads): warps 0-7 convert, two threads per weight row r (each one 64-K half of a 128-K stage),
-// and after a pass's last stage run its epilogue (TMEM lanes = rows, the two halves taking
+// threads): warps 0-7 convert, two threads per weight row r (each one 64-K half of every 128-K
+// stage), handing the A ring over in 256-K super-stages (one mbarrier round trip per 256 K), and
+// after a pass's last super-stage run its epilogue (TMEM lanes = rows, the two halves taking
 // alternate 32-column chunks); warp 8 weight producer (TMA / bulk copies); warp 9 MMA issuer
 // (allocates TMEM); warp 10 B loader. The B ring's 16 KB slots hold the B tiles of 4, 2 or 1 sub-stages (passes of <= 32, <= 64,
 // <= 128 tokens), so narrow passes keep many sub-stages of activations in flight. Every wait is
@@ -50,7 +51,7 @@ constexpr int BLOAD_WARP = NWORK + 2;
 constexpr int BLAG = 3;                 // B slots the loader keeps in flight before releasing one
 constexpr int WN = TC_WIDE_PASS;        // tokens (B rows) per pass
 constexpr int SC = 12;                  // staging ring (compact weight stage + scales)
-constexpr int SAR = 4;                  // A slots in TMEM: one staging stage each (64 columns)
+constexpr int SAR = 2;                  // A slots in TMEM: one 256-K super-stage each (128 columns)
 constexpr int SBR = 6;                  // B slots of 16 KB: the B tiles of 1, 2 or 4 sub-stages
 constexpr int STG_W = 8192;             // fp4: 128 rows x 64 B (128 K); FP8: 128 rows x 64 B (64 K)
 constexpr int STG_S = 1024;             // NVFP4 [128][8 B], MXFP4 [128][4 B], FP8 16 B
@@ -58,7 +59,8 @@ constexpr int B_BYTES = WN * 128;       // WN rows x 64 16-bit values
 constexpr int BOX_ROWS = 32;
 constexpr int BOX_BYTES = BOX_ROWS * 128;
 constexpr int A_COL0 = 2 * WN;          // TMEM: accumulators in columns 0 .. 2 WN, then the A slots
-constexpr int A_COLS = 64;              // 128 K of 16-bit values, two per column
+constexpr int A_COLS = 128;             // 256 K of 16-bit values, two per column
+constexpr int SUP = 4;                  // 64-K sub-stages per super-stage (the A ring's hand-off unit)
 constexpr int TMEM_COLS = A_COL0 + SAR * A_COLS;
 static_assert(TMEM_COLS == 512, "TMEM columns of one CTA per SM");
 constexpr uint32_t WAIT_LIMIT = 1u << 16;
@@ -383,8 +385,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant_
         if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
         const int pc = pass_tokens(it);
         const BGeom bg = bgeom(pc, nb);
-        const bool fp4 = item_fmt(it) != FMT_FP8;
-        const int nstg = fp4 ? nst : nsub, spst = fp4 ? 2 : 1;   // staging stages, sub-stages per stage
         const uint32_t n = (uint32_t)((pc + 15) & ~15);
         const uint32_t id = item_fmt(it) == FMT_MXFP4 ? idesc_bf16(n) : idesc_f16(n);
         const uint32_t buf = np & 1u;
@@ -392,15 +392,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant_
         const uint32_t tile = (uint32_t)(nb * bg.nboxp * BOX_BYTES);   // one sub-stage's B tiles
         if (!wait(smem_addr(&sm.accempty[buf]), ((np >> 1) & 1u) ^ 1u)) break;
         int i = 0;   // sub-stage
-        for (int st = 0; st < nstg && ok; ++st, ++g) {
+        const int nsup = (nsub + SUP - 1) / SUP;
+        for (int ss = 0; ss < nsup && ok; ++ss, ++g) {
           const uint32_t sa = g % SAR;
           const uint32_t ta = tbase + A_COL0 + sa * A_COLS;
+          const int nsb = min(SUP, nsub - ss * SUP);
           if (!wait(smem_addr(&sm.afull[sa]), (g / SAR) & 1u)) {
             ok = false;
             break;
           }
           bool synced = true;   // a wait since the last tcgen05 fence
-          for (int u = 0; u < spst; ++u, ++i) {
+          for (int u = 0; u < nsb; ++u, ++i) {
             const uint32_t sbf = gb % SBR;
             const int j = i & (bg.spb - 1);
             if (j == 0) {
@@ -429,7 +431,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant_
           }
           if (!ok) break;
           commit(smem_addr(&sm.aempty[sa]));
-          if (st == nstg - 1) commit(smem_addr(&sm.accfull[buf]));
+          if (ss == nsup - 1) commit(smem_addr(&sm.accfull[buf]));
         }
       }
       commit(smem_addr(&sm.drain));
@@ -484,41 +486,47 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant_
         ts = (w13 && r >= 64) ? tsp[1] : tsp[0];
       }
       float ca = 1.f, ica = 1.f;   // FP8: c_A and its reciprocal, from the item's first block scale
-      const int nstg = fp4 ? nst : nsub;
       const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
-      // convert every staging stage of the pass into the TMEM A ring
-      for (int st = 0; st < nstg; ++st, ++g, ++c) {
-        const uint32_t s = c % SC, sa = g % SAR;
-        if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
+      const int nsup = (nsub + SUP - 1) / SUP;
+      // convert the pass's weights into the TMEM A ring, one 256-K super-stage per hand-off: its 2 fp4
+      // (or 4 FP8) staging stages, each released as soon as it is converted
+      for (int ss = 0; ss < nsup; ++ss, ++g) {
+        const uint32_t sa = g % SAR;
+        const int nsb = min(SUP, nsub - ss * SUP);            // sub-stages in this super-stage
+        const int nq = fp4 ? (nsb + 1) / 2 : nsb;              // its staging stages
         if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.aempty[sa]), ((g / SAR) & 1u) ^ 1u));
-        if (!ok) continue;
-        fence_after();
-        const uint8_t* stg = sm.stg[s];
+        if (ok) fence_after();
         const uint32_t ta = tbase + lanes + A_COL0 + sa * A_COLS;
-        if (fmt == FMT_FP8) {
-          const float sw = reinterpret_cast<const float*>(stg + STG_W)[w13 && r >= 64 ? 1 : 0];
-          if (st == 0) {
-            ca = sw > 0.f ? sw * 16.f : 1.f;
-            ica = 1.f / ca;
+        for (int q = 0; q < nq; ++q, ++c) {
+          const uint32_t s = c % SC;
+          if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
+          if (!ok) continue;
+          const uint8_t* stg = sm.stg[s];
+          if (fmt == FMT_FP8) {
+            const float sw = reinterpret_cast<const float*>(stg + STG_W)[w13 && r >= 64 ? 1 : 0];
+            if (ss == 0 && q == 0) {
+              ca = sw > 0.f ? sw * 16.f : 1.f;
+              ica = 1.f / ca;
+            }
+            uint32_t v[16];
+            convert_fp8(stg, r, hh, f16_splat(sw * ica), v);
+            st16(ta + 32 * q + 16 * hh, v);
+          } else {
+            uint32_t v[32];
+            if (fmt == FMT_NVFP4)
+              convert_nvfp4(stg, r, hh, v);
+            else
+              convert_mxfp4(stg, r, hh, v);
+            st32(ta + 64 * q + 32 * hh, v);
           }
-          uint32_t v[16];
-          convert_fp8(stg, r, hh, f16_splat(sw * ica), v);
-          st16(ta + 16 * hh, v);
-        } else {
-          uint32_t v[32];
-          if (fmt == FMT_NVFP4)
-            convert_nvfp4(stg, r, hh, v);
-          else
-            convert_mxfp4(stg, r, hh, v);
-          st32(ta + 32 * hh, v);
+          __syncwarp();
+          if (lane == 0) arrive(smem_addr(&sm.sempty[s]));   // the stage is in registers / TMEM
         }
+        if (!ok) continue;
         st_wait();
         fence_before();
         __syncwarp();
-        if (lane == 0) {
-          arrive(smem_addr(&sm.afull[sa]));
-          arrive(smem_addr(&sm.sempty[s]));
-        }
+        if (lane == 0) arrive(smem_addr(&sm.afull[sa]));
       }
       // epilogue: this pass's accumulator -> h (W13, SwiGLU) or o (W2); each half of the workers
       // takes every other 32-column chunk
