@@ -5,8 +5,9 @@
 //                        (model.py:571-589), hash routing through tid2eid (model.py:581-582), and
 //                        the per-128 e4m3 quantisation of x for the expert GEMVs (act_quant,
 //                        kernel.py:40-125)
-//   permute_kernel       per-expert (token, slot) lists in ascending expert id, tokens ascending
-//                        within an expert; the list of active experts; all on the device, so the
+//   permute_kernel       per-expert (token, slot) lists in ascending expert id (tokens ascending
+//                        within an expert up to 2048 pairs; any order above, which no output sees);
+//                        the list of active experts; all on the device, so the
 //                        forward never drains to the host (the reference's bincount().tolist(),
 //                        model.py:639, is the sync this replaces)
 #include "sb_device.cuh"
@@ -326,6 +327,9 @@ __global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
 // pairs whose expert ids are staged in shared memory (with 2 * 1024 ints of counters: < 48 KB)
 constexpr int PERMUTE_SMEM_PAIRS = 8192;
 
+// pairs up to which the placement is stable (tokens ascending within an expert, by one warp)
+constexpr int PERMUTE_STABLE_PAIRS = 2048;
+
 __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   extern __shared__ int smem[];
   int* cnt = smem;                       // [E]
@@ -412,6 +416,19 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
     }
   }
   __syncthreads();
+  if (P > PERMUTE_STABLE_PAIRS) {
+    // Large batches: every thread places pairs through the shared cursors. The order of an expert's
+    // pairs then varies between runs, but no output does: every grouped kernel computes each
+    // token's rows independently of the other tokens of its pass (row invariance, asserted
+    // bit-for-bit by the parity tests), and outputs are indexed by (token, slot), not by position.
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+      const int ex = staged ? tk[p] : a.topk_idx[p];
+      const int pos = atomicAdd(&cursor[ex], 1);
+      a.pair_tok[pos] = p / a.topk;
+      a.pair_slot[pos] = p % a.topk;
+    }
+    return;
+  }
   // stable placement by one warp, 32 pairs at a time in ascending p
   if (warp == 0) {
     for (int p0 = 0; p0 < P; p0 += 32) {

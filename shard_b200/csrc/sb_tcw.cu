@@ -545,33 +545,46 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant_
         ld32(taddr + 32 * j, d);
         ld_wait();
         if (w13) {
-          if (r >= 64) {
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              const float cb = __shfl_sync(0xffffffffu, my_cb[jj], t);
-              sm.xchg[hh][r - 64][t] = __float2bfloat16_rn(__uint_as_float(d[t]) * cb * cab);
-            }
-          }
-          bar_sync(2 + hh, 128);
-          if (r < 64) {
-            const float lim = a.swiglu_limit;
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              const int orow = __shfl_sync(0xffffffffu, my_orow[jj], t);
-              const float wgt = __shfl_sync(0xffffffffu, my_wgt[jj], t);
-              const float cb = __shfl_sync(0xffffffffu, my_cb[jj], t);
-              if (32 * j + t < pc) {
-                float gv = bf16_round(__uint_as_float(d[t]) * cb * cab);
-                float uv = __bfloat162float(sm.xchg[hh][r][t]);
-                if (lim > 0.f) {
-                  uv = fminf(fmaxf(uv, -lim), lim);
-                  gv = fminf(gv, lim);
-                }
-                float hv = silu(gv) * uv;
-                if (!it.shared) hv = wgt * hv;
-                a.hbf[(size_t)orow * I + it.rb * 64 + r] = __float2bfloat16_rn(hv);
+          // gate row i = r and up row i + 64 of intermediate index i each compute SwiGLU for 16 of
+          // the chunk's 32 tokens (gate rows tokens 0-15, up rows 16-31), exchanging the other half
+          // of their values through shared memory (bf16: the rounding point of both GEMM outputs)
+          const int i = r & 63;
+          const float lim = a.swiglu_limit;
+          // SwiGLU of token tt from this thread's value `own` and the partner's `other`
+          auto swiglu = [&](int tt, float own, float other, bool up) {
+            const int orow = __shfl_sync(0xffffffffu, my_orow[jj], tt);
+            const float wgt = __shfl_sync(0xffffffffu, my_wgt[jj], tt);
+            if (32 * j + tt < pc) {
+              float gv = up ? other : own, uv = up ? own : other;
+              if (lim > 0.f) {
+                uv = fminf(fmaxf(uv, -lim), lim);
+                gv = fminf(gv, lim);
               }
+              float hv = silu(gv) * uv;
+              if (!it.shared) hv = wgt * hv;
+              a.hbf[(size_t)orow * I + it.rb * 64 + i] = __float2bfloat16_rn(hv);
             }
+          };
+          if (r >= 64) {   // up rows (warp-uniform): park tokens 0-15, compute 16-31
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              sm.xchg[hh][i][t] =
+                  __float2bfloat16_rn(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab);
+            bar_sync(2 + hh, 128);
+#pragma unroll
+            for (int t = 16; t < 32; ++t)
+              swiglu(t, bf16_round(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab),
+                     __bfloat162float(sm.xchg[hh][i][t]), true);
+          } else {         // gate rows: park tokens 16-31, compute 0-15
+#pragma unroll
+            for (int t = 16; t < 32; ++t)
+              sm.xchg[hh][i][t] =
+                  __float2bfloat16_rn(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab);
+            bar_sync(2 + hh, 128);
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              swiglu(t, bf16_round(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab),
+                     __bfloat162float(sm.xchg[hh][i][t]), false);
           }
           bar_sync(2 + hh, 128);
         } else {
