@@ -610,6 +610,396 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant_
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(TMEM_COLS));
 }
 
+// ── the prefill kernel with the operands swapped (the default build) ──
+// tcx_kernel computes the same items with the pass's tokens as the MMA's M side (128, TMEM lanes) and
+// 256 weight rows — two 128-row blocks — as its N side: one tcgen05.mma covers twice the weight rows
+// of tcw_kernel's (the MMA issue rate is what bounds both), and an accumulator lane holds one
+// token's outputs, so the W13 epilogue pairs a gate column with its up column inside one thread and
+// writes 64-byte runs of h. The weights are converted into shared memory (the B operand must be
+// there); the token tiles come by bulk copy. Build with -DSB_WIDE_SWAP=0 for tcw_kernel.
+#ifndef SB_WIDE_SWAP
+#define SB_WIDE_SWAP 1
+#endif
+#if SB_WIDE_SWAP
+namespace x {
+constexpr int NTHREADS = 32 * (NWORK + 3);
+constexpr int PRODUCER_WARP = NWORK, MMA_WARP = NWORK + 1, TLOAD_WARP = NWORK + 2;
+constexpr int ROWS = 256;                    // weight rows per item (two 128-row blocks) = MMA N
+constexpr int SC = 3;                        // staging ring: one stage of both row blocks per slot
+constexpr int SW = 3;                        // f16 weight tiles (64 K each)
+constexpr int STT = 3;                       // token tiles: 16 KB slots of 4, 2 or 1 sub-stages
+constexpr int STG_RB = STG_W + STG_S;        // one row block's staging bytes (9 KB, 1024-aligned)
+constexpr int W_BYTES = ROWS * 128;
+constexpr int T_BYTES = WN * 128;
+constexpr int TMEM_COLS = 2 * ROWS;          // two accumulators of 128 token lanes x 256 columns
+
+struct Smem {
+  uint8_t W[SW][W_BYTES];                    // 1024-aligned (128B swizzle atoms)
+  uint8_t T[STT][T_BYTES];
+  uint8_t stg[SC][2 * STG_RB];
+  float ca[ROWS];                            // FP8: c_A of each weight row of the current item
+  uint64_t sfull[SC], sempty[SC], wfull[SW], wempty[SW], tfull[STT], tempty[STT], accfull[2], accempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory of one CTA per SM");
+
+template <int FMT_R>
+__global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant__ WideArgs wa) {
+  const GroupedArgs& a = wa.g;
+  extern __shared__ uint8_t dyn_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~(uintptr_t)1023);
+  int* err = a.err != nullptr ? a.err : &g_tcw_dense_err;
+  volatile int* abort_flag = &sm.abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < SC; ++s) {
+      mbar_init(smem_addr(&sm.sfull[s]), 1);
+      mbar_init(smem_addr(&sm.sempty[s]), NWORK);
+    }
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(smem_addr(&sm.wfull[s]), NWORK);
+      mbar_init(smem_addr(&sm.wempty[s]), 1);
+    }
+    for (int s = 0; s < STT; ++s) {
+      mbar_init(smem_addr(&sm.tfull[s]), 1);
+      mbar_init(smem_addr(&sm.tempty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_addr(&sm.accfull[s]), 1);
+      mbar_init(smem_addr(&sm.accempty[s]), NWORK);
+    }
+    mbar_init(smem_addr(&sm.drain), 1);
+    sm.abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(&sm.tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tbase = sm.tmem_base;
+  pdl_wait();
+  pdl_trigger();
+
+  const int P = a.m * a.topk;
+  const int K = a.k;
+  const int nsub = K / 64;
+  const int nst = K / 128;
+  const int nrb = a.n_rows / 128;
+  const int nrp = nrb / 2;                        // row-block pairs per matrix (nrb is even)
+  const int nb = wa.b_split ? 2 : 1;
+  const int wn = wa.b_split ? WN / 2 : WN;
+  const int n_pass = (a.has_shared ? wa.plan.n_sh_pass : 0) + wa.plan.pass_off[*a.n_active];
+  const int n_items = n_pass * nrp;
+  const bool w13 = a.mode == MODE_W13;
+  auto item_fmt = [&](const Item& it) { return it.shared ? FMT_FP8 : FMT_R; };
+  auto pass_tokens = [&](const Item& it) { return min(wn, it.cnt - it.pb); };
+  auto wait = [&](uint32_t bar, uint32_t parity) { return wait_bounded(abort_flag, err, bar, parity, WAIT_LIMIT); };
+  auto warp_wait = [&](uint32_t bar, uint32_t parity) { return __all_sync(0xffffffffu, wait(bar, parity)); };
+
+  if (warp == PRODUCER_WARP) {
+    // both row blocks' weight stages (TMA) and their scales (bulk copies) into one staging slot
+    if (elect_one()) {
+      if (wa.use_w4) prefetch_map(&wa.map_w4);
+      if (wa.use_w8) prefetch_map(&wa.map_w8);
+      if (wa.use_w8_sh) prefetch_map(&wa.map_w8_sh);
+    }
+    __syncwarp();
+    uint32_t c = 0;
+    bool ok = true;
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrp, wn) : Item{};
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const Item it = nxt;
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrp, wn);
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(err) != 0)) {
+        *abort_flag = 1;
+        break;
+      }
+      const int fmt = item_fmt(it);
+      const bool fp4 = fmt != FMT_FP8;
+      const WeightSet& ws = it.shared ? a.shared : a.routed;
+      const uint32_t sb = fmt == FMT_NVFP4 ? 1024u : (fmt == FMT_MXFP4 ? 512u : 16u);
+      const CUtensorMap* mapw = fp4 ? &wa.map_w4 : (it.shared ? &wa.map_w8_sh : &wa.map_w8);
+      const int nstg = fp4 ? nst : nsub;
+      for (int st = 0; st < nstg; ++st, ++c) {
+        const uint32_t s = c % SC;
+        if (!warp_wait(smem_addr(&sm.sempty[s]), ((c / SC) & 1u) ^ 1u)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
+          const uint32_t bar = smem_addr(&sm.sfull[s]);
+          mbar_expect_tx(bar, 2u * (8192u + sb));
+          for (int h = 0; h < 2; ++h) {
+            const int rb = 2 * it.rb + h;
+            const int row0 = ((it.shared ? 0 : it.expert) * nrb + rb) * nst * 128;
+            const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)rb * nst * sb;
+            const uint32_t dst = smem_addr(sm.stg[s] + h * STG_RB);
+            if (fp4)
+              tma_load_2d(dst, mapw, 0, (row0 >> 1) + st * 64, bar);
+            else
+              tma_load_2d(dst, mapw, (st & 1) * 64, row0 + (st >> 1) * 128, bar);
+            bulk_g2s(dst + STG_W, sbase + (size_t)(fp4 ? st : st >> 1) * sb, sb, bar);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    for (uint32_t h = c > (uint32_t)SC ? c - SC : 0; h < c; ++h)
+      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait(smem_addr(&sm.sfull[h % SC]), (h / SC) & 1u)) break;
+  } else if (warp == TLOAD_WARP) {
+    // token tiles: one bulk copy per sub-stage and plane (as tcw_kernel's B loader)
+    uint32_t gt = 0;
+    bool ok = true;
+    const size_t plane = (size_t)(K / 64) * (size_t)wa.r_pad * 128;
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrp, wn) : Item{};
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const Item it = nxt;
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrp, wn);
+      const int pc = pass_tokens(it);
+      const BGeom bg = bgeom(pc, nb);
+      const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
+      const uint32_t bytes = (uint32_t)((pc + 7) & ~7) * 128u;
+      for (int i = 0; i < nsub; i += bg.spb, ++gt) {
+        const uint32_t ts = gt % STT;
+        if (!warp_wait(smem_addr(&sm.tempty[ts]), ((gt / STT) & 1u) ^ 1u)) {
+          ok = false;
+          break;
+        }
+        const int cnt = min(bg.spb, nsub - i);
+        if (elect_one()) {
+          const uint32_t bar = smem_addr(&sm.tfull[ts]);
+          mbar_expect_tx(bar, (uint32_t)(cnt * nb) * bytes);
+          for (int j = 0; j < cnt; ++j)
+            for (int h = 0; h < nb; ++h)
+              bulk_g2s(smem_addr(sm.T[ts] + (j * nb + h) * bg.nboxp * BOX_BYTES),
+                       wa.bmat + h * plane + ((size_t)(i + j) * wa.r_pad + brow0) * 128, bytes, bar);
+        }
+        __syncwarp();
+      }
+    }
+    for (uint32_t h = gt > (uint32_t)STT ? gt - STT : 0; h < gt; ++h)
+      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait(smem_addr(&sm.tfull[h % STT]), (h / STT) & 1u)) break;
+  } else if (warp == MMA_WARP) {
+    // one thread: per sub-stage 4 tcgen05.mma M=128 (tokens) x N=256 (weight rows) x K=16
+    if (lane == 0) {
+      uint32_t gw = 0, gt = 0, np = 0;
+      bool ok = true;
+      Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrp, wn) : Item{};
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++np) {
+        const Item it = nxt;
+        if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrp, wn);
+        const int pc = pass_tokens(it);
+        const BGeom bg = bgeom(pc, nb);
+        const uint32_t id = item_fmt(it) == FMT_MXFP4 ? idesc_bf16(ROWS) : idesc_f16(ROWS);
+        const uint32_t buf = np & 1u;
+        const uint32_t tacc = tbase + buf * ROWS;
+        const uint32_t tile = (uint32_t)(nb * bg.nboxp * BOX_BYTES);
+        if (!wait(smem_addr(&sm.accempty[buf]), ((np >> 1) & 1u) ^ 1u)) break;
+        for (int i = 0; i < nsub && ok; ++i, ++gw) {
+          const uint32_t sws = gw % SW, ts = gt % STT;
+          const int j = i & (bg.spb - 1);
+          if (!wait(smem_addr(&sm.wfull[sws]), (gw / SW) & 1u) ||
+              (j == 0 && !wait(smem_addr(&sm.tfull[ts]), (gt / STT) & 1u))) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint64_t bd = sdesc(smem_addr(sm.W[sws]));
+          for (int h = 0; h < nb; ++h) {
+            const uint64_t ad = sdesc(smem_addr(sm.T[ts]) + (uint32_t)j * tile + (uint32_t)h * (tile / nb));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_f16(tacc, ad + 2 * k, bd + 2 * k, id, (i > 0 || h > 0 || k > 0) ? 1u : 0u);
+          }
+          commit(smem_addr(&sm.wempty[sws]));
+          if (j == bg.spb - 1 || i == nsub - 1) {
+            commit(smem_addr(&sm.tempty[ts]));
+            ++gt;
+          }
+          if (i == nsub - 1) commit(smem_addr(&sm.accfull[buf]));
+        }
+      }
+      commit(smem_addr(&sm.drain));
+      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+        if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
+    }
+    __syncwarp();
+  } else {
+    // ── convert (thread t = weight row t of the item's 256) + epilogue (lane = token) ──
+    const int t = tid, hb = t >> 7, r = t & 127;
+    uint32_t c = 0, gw = 0, np = 0;
+    bool ok = true;
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrp, wn) : Item{};
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++np) {
+      const Item it = nxt;
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrp, wn);
+      const int fmt = item_fmt(it);
+      const bool fp4 = fmt != FMT_FP8;
+      const WeightSet& ws = it.shared ? a.shared : a.routed;
+      const int pc = pass_tokens(it);
+      const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
+      float ica = 1.f;
+      if (fmt != FMT_FP8) sm.ca[t] = 1.f;
+      const int nstg = fp4 ? nst : nsub;
+      for (int st = 0; st < nstg; ++st, ++c) {
+        const uint32_t s = c % SC;
+        if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
+        const uint8_t* stg = sm.stg[s] + hb * STG_RB;
+        uint32_t s2 = 0;
+        if (ok && fmt == FMT_FP8) {
+          const float sw = reinterpret_cast<const float*>(stg + STG_W)[w13 && r >= 64 ? 1 : 0];
+          if (st == 0) {
+            const float ca = sw > 0.f ? sw * 16.f : 1.f;
+            ica = 1.f / ca;
+            sm.ca[t] = ca;
+          }
+          s2 = f16_splat(sw * ica);
+        }
+        for (int u = 0; u < (fp4 ? 2 : 1); ++u, ++gw) {
+          const uint32_t sws = gw % SW;
+          if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.wempty[sws]), ((gw / SW) & 1u) ^ 1u));
+          if (!ok) continue;
+          uint32_t o[32];
+          if (fmt == FMT_FP8) {
+            uint32_t o0[16], o1[16];
+            convert_fp8(stg, r, 0, s2, o0);
+            convert_fp8(stg, r, 1, s2, o1);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              o[e] = o0[e];
+              o[16 + e] = o1[e];
+            }
+          } else if (fmt == FMT_NVFP4) {
+            convert_nvfp4(stg, r, u, o);
+          } else {
+            convert_mxfp4(stg, r, u, o);
+          }
+          uint8_t* dst = sm.W[sws] + t * 128;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<uint4*>(dst + ((k ^ (t & 7)) << 4)) = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) arrive(smem_addr(&sm.wfull[sws]));
+        }
+        __syncwarp();
+        if (ok && lane == 0) arrive(smem_addr(&sm.sempty[s]));
+      }
+      // epilogue: TMEM lane = token (32 (warp & 3) + lane), the warp half hh takes row block 2 rb + hh
+      const uint32_t buf = np & 1u;
+      if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
+      if (bar_any(1, 32 * NWORK, !ok || *abort_flag)) break;
+      fence_after();
+      const int hh = warp >> 2;
+      const int tok = (warp & 3) * 32 + lane;
+      const bool valid = tok < pc;
+      const int rb = 2 * it.rb + hh;
+      const uint32_t taddr = tbase + ((uint32_t)((warp & 3) * 32) << 16) + buf * ROWS + 128 * hh;
+      float cb = 1.f, wgt = 1.f;
+      int orow = 0;
+      if (valid) {
+        const int i = it.pb + tok;
+        cb = wa.cvec[brow0 + tok];
+        if (w13) {
+          orow = brow0 + tok;
+          if (!it.shared) {
+            const int qp = it.base + i;
+            wgt = a.topk_w[(size_t)a.pair_tok[qp] * a.topk + a.pair_slot[qp]];
+          }
+        } else if (it.shared) {
+          orow = P + i;
+        } else {
+          const int qp = it.base + i;
+          orow = a.pair_tok[qp] * a.topk + a.pair_slot[qp];
+        }
+      }
+      float ts0 = 1.f, ts1 = 1.f;   // NVFP4 tensor scales: w1 (or w2) rows, w3 rows
+      if (fmt == FMT_NVFP4 && ws.ts != nullptr) {
+        const float* tsp = ws.ts + (it.shared ? 0 : (size_t)it.expert * ws.ts_stride);
+        ts0 = tsp[0];
+        ts1 = w13 ? tsp[1] : tsp[0];
+      }
+      const float* cav = sm.ca + 128 * hh;
+      if (w13) {
+        const int I = a.n_rows / 2;
+        const float lim = a.swiglu_limit;
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 32) {
+          uint32_t gd[32], ud[32];
+          ld32(taddr + c0, gd);
+          ld32(taddr + 64 + c0, ud);
+          ld_wait();
+          uint32_t hv[16];
+#pragma unroll
+          for (int q = 0; q < 32; q += 2) {
+            float h2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              float gv = bf16_round(__uint_as_float(gd[q + e]) * cb * (cav[c0 + q + e] * ts0));
+              float uv = bf16_round(__uint_as_float(ud[q + e]) * cb * (cav[64 + c0 + q + e] * ts1));
+              if (lim > 0.f) {
+                uv = fminf(fmaxf(uv, -lim), lim);
+                gv = fminf(gv, lim);
+              }
+              float hvv = silu(gv) * uv;
+              if (!it.shared) hvv = wgt * hvv;
+              h2[e] = hvv;
+            }
+            const __nv_bfloat162 b = __floats2bfloat162_rn(h2[0], h2[1]);
+            hv[q / 2] = *reinterpret_cast<const uint32_t*>(&b);
+          }
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(a.hbf + (size_t)orow * I + rb * 64 + c0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(hv[4 * v], hv[4 * v + 1], hv[4 * v + 2], hv[4 * v + 3]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t d[32];
+          ld32(taddr + c0, d);
+          ld_wait();
+          uint32_t ov[16];
+#pragma unroll
+          for (int q = 0; q < 32; q += 2) {
+            const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(d[q]) * cb * (cav[c0 + q] * ts0),
+                                                           __uint_as_float(d[q + 1]) * cb * (cav[c0 + q + 1] * ts0));
+            ov[q / 2] = *reinterpret_cast<const uint32_t*>(&b);
+          }
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(a.o + (size_t)orow * a.n_rows + rb * 128 + c0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(ov[4 * v], ov[4 * v + 1], ov[4 * v + 2], ov[4 * v + 3]);
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) arrive(smem_addr(&sm.accempty[buf]));
+      // the next item's converters overwrite ca: every thread has read it
+      bar_sync(1, 32 * NWORK);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == MMA_WARP)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(TMEM_COLS));
+}
+}  // namespace x
+#endif
+
 // ── activation matrices of the wide path (B operands), one warp per row ──
 // Row space: routed pair q of expert e at pbase(offsets[e], e) + (q - offsets[e]), the shared
 // expert's token i at sb_row + i (W13: the same x row; W2: the rows of h, which the W13 epilogue
@@ -806,12 +1196,21 @@ static cudaError_t encode(CUtensorMap* map, CUtensorMapDataType dt, const void* 
 template <int F>
 static cudaError_t launch_one(const WideArgs& a, int grid, cudaStream_t st) {
   static bool configured = false;
+#if SB_WIDE_SWAP
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(x::tcx_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, x::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return launch_pdl(x::tcx_kernel<F>, dim3(grid), dim3(x::NTHREADS), x::SMEM_BYTES, st, a);
+#else
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(tcw_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   return launch_pdl(tcw_kernel<F>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
+#endif
 }
 
 static unsigned warp_grid(int64_t rows) {
