@@ -30,6 +30,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -311,8 +312,7 @@ def run_gpu(args, rank, world, local_rank):
     def step_dev():
         pipe.run(C, xs_dev, outs_dev)
 
-    clk = ClockSampler(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
-                                    f"clocks_bench_r{rank}.csv"))
+    clk = ClockSampler(os.path.join(tempfile.gettempdir(), f"clocks_bench_r{rank}.csv"))   # scratch log
     clk.__enter__()   # sampling spans both timed regions (device-resident and end to end)
     t = timed(step_dev, args.steps, args.warmup, clk)
     tok_layers = args.steps * C * HEADLINE_M * LAYERS_PER_GPU * world
