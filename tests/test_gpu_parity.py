@@ -176,9 +176,11 @@ def test_merged_chunks_equal_unmerged(prefill):
     assert torch.equal(torch.cat([ya, yb]), yab)
 
 
-def test_hash_routing_drops_earlier_duplicate_slots():
+@pytest.mark.parametrize("prefill", [1, 2])
+def test_hash_routing_drops_earlier_duplicate_slots(prefill):
     """Hash layers (model.py:581-582): ids from tid2eid, repeated ids keep only the last slot
-    (the reference's `y[idx] +=` semantics, v4_moe_grouped.py:98-118)."""
+    (the reference's `y[idx] +=` semantics, v4_moe_grouped.py:98-118); through the verify kernel
+    and through the prefill kernel (whose batches take the tensor-core gate for the weights)."""
     cfg = S.CONFIGS["c0"]
     sl = SeededLayer(cfg)
     lay = S.device_layer(cfg, 0, "cuda")
@@ -189,7 +191,7 @@ def test_hash_routing_drops_earlier_duplicate_slots():
     hl = MoELayer(hidden=lay.hidden, inter=lay.inter, n_experts=lay.n_experts, topk=lay.topk,
                   expert_fmt=lay.expert_fmt, gate_w=lay.gate_w, gate_bias=None, tid2eid=tab.cuda(),
                   score_func="sqrtsoftplus", route_scale=1.5, w13=lay.w13, w13_s=lay.w13_s, w13_ts=lay.w13_ts,
-                  w2=lay.w2, w2_s=lay.w2_s, w2_ts=lay.w2_ts, shared=lay.shared, tiled=True)
+                  w2=lay.w2, w2_s=lay.w2_s, w2_ts=lay.w2_ts, shared=lay.shared, tiled=True, prefill=prefill)
     x, _ = S.make_inputs(cfg, 8)
     ids = torch.tensor([5, 1, 2, 5, 7, 9, 11, 63])
     y, w, idx = hl.forward(x.cuda(), ids.cuda(), routing=True)
