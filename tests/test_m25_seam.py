@@ -113,5 +113,16 @@ def test_m25_mlp_matches_the_oracle(dims, norm, scale, m):
         assert err < TOL, f"max rel err {err:.3e}"
         assert torch.equal(y, yb)
         assert lay.device_error() == 0
+        # the same tokens through the prefill kernel and the tensor-core gate (bf16 router logits,
+        # NORM_TOPK / ROUTED_SCALE, no shared expert)
+        lay.prefill = 2
+        y2, w2, idx2 = lay.forward(x.reshape(m, h).cuda(), routing=True)
+        torch.cuda.synchronize()
+        lay.prefill = 0
+        assert np.array_equal(idx2.cpu().numpy(), ridx), "prefill path: router top-k must be bit-exact"
+        assert np.abs(w2.cpu().numpy() - rw).max() < 1e-5
+        err2 = O.max_rel_err(y2.float().cpu().numpy(), ref)
+        assert err2 < TOL, f"prefill path: max rel err {err2:.3e}"
+        assert lay.device_error() == 0
     finally:
         m25.uninstall(mod)
