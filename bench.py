@@ -158,16 +158,19 @@ class ClockSampler:
 
 # ── workload ─────────────────────────────────────────────────────────────────────────────────────
 
-def build_layers(rank, n_layers, device):
+def build_layers(rank, n_layers, device, cname="c1", first_layer=None, distinct=None):
+    """This rank's layers of config `cname`. Layers past `distinct` alias the first `distinct`
+    banks (a stack that does not fit in HBM cycles through as many distinct layers as fit; each bank
+    is many times the L2, so every forward still streams its weights from HBM)."""
     from shard_b200 import synth as S
-    cfg = S.CONFIGS["c1"]
+    cfg = S.CONFIGS[cname]
     if N_EXPERTS:
         cfg = cfg.replace(n_experts=N_EXPERTS)
-    layers = []
-    for j in range(n_layers):
-        layers.append(S.device_layer(cfg, layer=rank * n_layers + j, device=device, seeded=[], fill="normal",
-                                     prefill=PREFILL))
-    return cfg, layers
+    first = rank * n_layers if first_layer is None else first_layer
+    nd = n_layers if distinct is None else max(1, min(distinct, n_layers))
+    banks = [S.device_layer(cfg, layer=first + j, device=device, seeded=[], fill="normal", prefill=PREFILL)
+             for j in range(nd)]
+    return cfg, [banks[j % nd] for j in range(n_layers)]
 
 
 def chunk_inputs(cfg, n, device, seed_step=0):
@@ -271,6 +274,8 @@ def run_gpu(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    if args.config == "c4":
+        return run_c4_pipeline(args, rank, world, device)
     cfg, layers = build_layers(rank, LAYERS_PER_GPU, device)
     pipe = Pipeline(StageStack(layers), HEADLINE_M, cfg.hidden, rank, world, device, wire=args.wire)
     C = CHUNKS_PER_STEP
@@ -333,6 +338,8 @@ def run_gpu(args, rank, world, local_rank):
 
     t_e2e = timed(step_e2e, args.steps, max(args.warmup, 3), clk)
     clk.__exit__(None, None, None)
+    pipe.flush()
+    torch.cuda.synchronize()
     e2e_value = tok_layers / t_e2e
     bytes_io = C * HEADLINE_M * cfg.hidden * 2
 
@@ -365,7 +372,7 @@ def run_gpu(args, rank, world, local_rank):
             sweep = m_sweep(layers, cfg)
             if not N_EXPERTS:
                 sweep.update(cfg_sweep("c3", (1, 16, 64)))
-                sweep.update(cfg_sweep("c4", (256, 1024), modes=(0, 1)))
+                sweep.update(cfg_sweep("c4", (256, 1024), modes=(0, 1, 2)))
     clocks = clk.summary(set(range(world)) if world > 1 else {local_rank}) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -388,6 +395,80 @@ def run_gpu(args, rank, world, local_rank):
                         "d2h_bytes_per_step": bytes_io},
                 "gpu_launches": args.steps * C * LAYERS_PER_GPU * 6 * world,
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clocks, "sweep": sweep}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+C4_LAYERS = 61
+
+
+def run_c4_pipeline(args, rank, world, device):
+    """Config c4's stack: 61 Kimi-K3-scale layers (H=7168, 384 NVFP4 experts top-8, FP8 shared
+    expert, Zipf routing) split over the ranks by even_tiling (8,8,8,8,8,7,7,7 at 8 GPUs), prefill
+    chunks of M tokens (default 256) streamed through the stages. Strong scaling: the whole stack's
+    work per step is fixed. value = tokens through all 61 layers per second (max over ranks)."""
+    import datetime  # noqa: F401
+    import torch.distributed as dist
+    from shard_b200.pipeline import Pipeline, StageStack, even_tiling
+    blocks = even_tiling(C4_LAYERS, world)
+    mine = blocks[rank]
+    free, _ = torch.cuda.mem_get_info(device)
+    from shard_b200 import formats as F
+    from shard_b200 import synth as S
+    cfg0 = S.CONFIGS["c4"]
+    per_layer = cfg0.n_experts * (F.weight_bytes(cfg0.expert_fmt, 2 * cfg0.inter, cfg0.hidden) +
+                                  F.weight_bytes(cfg0.expert_fmt, cfg0.hidden, cfg0.inter)) * 2   # + staging
+    distinct = args.distinct or max(1, int(0.6 * free // per_layer))
+    cfg, layers = build_layers(rank, len(mine), device, "c4", first_layer=mine.start, distinct=distinct)
+    m = args.m if args.m != HEADLINE_M else 256
+    C = CHUNKS_PER_STEP
+    for lay in layers:
+        lay.reserve(m)
+    pipe = Pipeline(StageStack(layers), m, cfg.hidden, rank, world, device)
+    xs = [S.make_inputs(cfg, m, step=j)[0].to(device) for j in range(C)] if rank == 0 else None
+    outs = [torch.empty(m, cfg.hidden, dtype=torch.bfloat16, device=device) for _ in range(C)] \
+        if rank == world - 1 else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[device.index])
+
+    for _ in range(args.warmup):
+        pipe.run(C, xs, outs)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(os.path.join(tempfile.gettempdir(), f"clocks_c4_r{rank}.csv"))
+    clk.__enter__()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with clk.region():
+        e0.record()
+        for _ in range(args.steps):
+            pipe.run(C, xs, outs)
+        e1.record()
+        torch.cuda.synchronize()
+    barrier()
+    clk.__exit__(None, None, None)
+    t = e0.elapsed_time(e1) / 1000.0
+    if world > 1:
+        tt = torch.tensor([t], dtype=torch.float64, device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    pipe.flush()
+    torch.cuda.synchronize()
+    if rank == 0:
+        tokens = args.steps * C * m
+        line = {"metric": "c4 MoE stack tokens/s (61 layers, prefill chunks)", "value": tokens / t, "unit": "tokens/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": t / args.steps * 1000.0, "higher_is_better": True, "scaling": "strong",
+                "token_layers_per_s": tokens * C4_LAYERS / t, "dtype": "nvfp4", "data": "synthetic",
+                "config": {"workload": f"c4 61-layer MoE stack, pp{world} (even_tiling: "
+                                       f"{[len(b) for b in blocks]}), M={m} chunks, {C} chunks per step",
+                           "m": m, "layers": C4_LAYERS, "layers_per_rank": [len(b) for b in blocks],
+                           "distinct_banks_per_rank": min(distinct, len(mine)), "chunks_per_step": C,
+                           "pipeline_depth": pipe.depth, "parallelism": f"pp{world}",
+                           "l2": "no flush: each forward streams GBs of distinct expert weights"},
+                "clocks": clk.summary(set(range(world)) if world > 1 else {device.index})}
         print(json.dumps(line), flush=True)
     return 0
 
@@ -497,6 +578,11 @@ def main():
                          "small case for ncu captures of the prefill kernel)")
     ap.add_argument("--prefill", type=int, choices=[0, 1, 2], default=0,
                     help="expert kernel on the tensor-core layout: 0 by batch size, 1 verify, 2 prefill")
+    ap.add_argument("--config", choices=["c1", "c4"], default="c1",
+                    help="c1: the headline (c1 layers, verify chunks, weak scaling); c4: the 61-layer "
+                         "Kimi-K3-scale stack split over the GPUs with prefill chunks (--m, default 256)")
+    ap.add_argument("--distinct", type=int, default=None,
+                    help="c4: distinct layer banks per rank (default: as many as fit in 60%% of free HBM)")
     args = ap.parse_args()
     if args.layout is not None:
         import shard_b200.moe as sbm

@@ -60,9 +60,10 @@ enum sb_layout { SB_LAYOUT_FRAGMENT = 0, SB_LAYOUT_TC = 1 };
 #define SB_KIND_TC 4
 
 /* One MoE layer as the forward reads it. All pointers are device pointers; weights are in the
- * TILED layout produced by sb_tile_weights / sb_tile_scales: 16-row tiles, each stored as the
- * per-lane tensor-core fragments of consecutive 32-wide K chunks, so a warp streams a tile with
- * one coalesced 16-byte load per lane per 64 K (fp4) or 32 K (fp8).
+ * layout `layout` names, produced by sb_tile_weights / sb_tile_scales: SB_LAYOUT_TC (the default of
+ * the Python host, the tcgen05 kernels) stores 128-row blocks x 128-K stages, one TMA box per stage;
+ * SB_LAYOUT_FRAGMENT stores 16-row tiles of mma.sync register fragments for the mma.sync kernel
+ * family. See enum sb_layout.
  * Mirrors the state MoE.forward reads, model.py:614-649: self.gate.{weight,bias,tid2eid,
  * score_func,route_scale,topk}, the expert bank, self.shared_experts, Expert.swiglu_limit. */
 typedef struct sb_moe_layer {
@@ -146,13 +147,17 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
  * error flag (cleared by every call before its kernels run) and the activation panel of
  * ceil(m / p) passes x k/128 stages, 2112 bytes each (p = 8 for NVFP4, 16 otherwise). Shapes that
  * need more return SB_ERR_SHAPE with the byte count (at k = 7168: m <= 272, or m <= 136 for NVFP4).
- * The first call on a device looks up the region's address (cudaGetSymbolAddress, with that device
- * current); make that first call before any stream capture. Every call on a device uses the same
- * region: calls that overlap in time (other streams, other threads) race on it and must be
- * serialised by the caller. */
+ * Every call looks up the region's address on the current device (cudaGetSymbolAddress); the first
+ * call on a device also loads the library's module there, so make that first call before any stream
+ * capture. Every call on a device uses the same region: calls that overlap in time (other streams,
+ * other threads) race on it and must be serialised by the caller. */
 #define SB_QGEMM_STATIC_SCRATCH_BYTES (2u << 20)
 int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
                     const void* q, const float* s, int64_t m, void* y, void* stream);
+/* The error flag of the last sb_qgemm_static call on the current device: *host_out = 0, or 1 if one of
+ * its kernels gave up a bounded wait (its y is then incomplete). Enqueues the read on `stream`
+ * after that call and synchronises the stream. The next sb_qgemm_static call clears the flag. */
+int sb_qgemm_static_error(int* host_out, void* stream);
 
 /* ── the MoE stage forward (MoE.forward, model.py:634-649; Gate.forward :569-589;
  *    Expert.forward :601-611; grouped decode v4_moe_grouped.py:634-709) ──────────────────────── */
@@ -190,6 +195,13 @@ int sb_wire_unpack(const void* q, const void* scale, int64_t rows, int64_t dim, 
 int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,
                  float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes,
                  void* stream);
+
+/* Test hook of the timeout path. Sets, for every later launch in this process, the number of polls
+ * the tensor-core kernels' consumer-side waits (on operands and accumulators) make before they give
+ * up: the kernel then sets the workspace error flag, drains its copies and MMAs in flight, frees its
+ * tensor memory and returns, and the forward's output is incomplete. Waits for free slots and the
+ * final drains keep their normal limits. polls = 0 restores each kernel's default. */
+int sb_debug_set_wait_limit(int64_t polls);
 
 /* Format self-test: decodes a fixed set of e2m1 / e4m3 / e8m0 codes on the device into out
  * (fp32 [64]) so a test can compare them with the host tables. */

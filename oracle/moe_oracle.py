@@ -118,8 +118,59 @@ def unpack_fp4(packed: np.ndarray) -> np.ndarray:
     return np.stack([lo, hi], axis=-1).reshape(packed.shape[0], -1)
 
 
+_CLIB = None
+
+
+def _clib():
+    """oracle/dequant.c through ctypes (built on first use), or None without a C compiler."""
+    global _CLIB
+    if _CLIB is None:
+        import ctypes
+        import os
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+        try:
+            import build_oracle
+            lib = ctypes.CDLL(build_oracle.build())
+        except Exception:  # noqa: BLE001  (the numpy path below is the same arithmetic)
+            _CLIB = False
+            return None
+        finally:
+            sys.path.pop(0)
+        vp, i64 = ctypes.c_void_p, ctypes.c_int64
+        lib.oracle_dequant_fp4.argtypes = [ctypes.c_int, vp, vp, ctypes.c_float, i64, i64, vp]
+        lib.oracle_dequant_fp8.argtypes = [vp, vp, i64, i64, vp]
+        lib.oracle_qgemm.argtypes = [ctypes.c_int, vp, vp, ctypes.c_float, i64, i64, vp, i64, vp, vp]
+        _CLIB = lib
+    return _CLIB or None
+
+
 def dequant_weight(fmt: int, packed: np.ndarray, scale: np.ndarray, ts: float = 1.0) -> np.ndarray:
-    """One weight matrix -> fp32 [N, K], in the reference dequant order."""
+    """One weight matrix -> fp32 [N, K], in the reference dequant order (v4_kernels_cpu.py:141-173).
+
+    Runs oracle/dequant.c when it is available (the same products in fp32, computed per element),
+    else the numpy expression below it."""
+    lib = _clib()
+    if lib is not None:
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        n = packed.shape[0]
+        k = packed.shape[1] * (1 if fmt == FMT_FP8 else 2)
+        out = np.empty((n, k), dtype=np.float32)
+        if fmt == FMT_FP8:
+            sc = np.ascontiguousarray(scale, dtype=np.float32)
+            rc = lib.oracle_dequant_fp8(packed.ctypes.data, sc.ctypes.data, n, k, out.ctypes.data)
+        else:
+            sc = np.ascontiguousarray(scale, dtype=np.uint8)
+            rc = lib.oracle_dequant_fp4(fmt, packed.ctypes.data, sc.ctypes.data, float(np.float32(ts)), n, k,
+                                        out.ctypes.data)
+        if rc != 0:
+            raise ValueError(fmt)
+        return out
+    return dequant_weight_np(fmt, packed, scale, ts)
+
+
+def dequant_weight_np(fmt: int, packed: np.ndarray, scale: np.ndarray, ts: float = 1.0) -> np.ndarray:
+    """dequant_weight in numpy."""
     if fmt == FMT_FP8:
         n, k = packed.shape
         s = np.repeat(np.repeat(scale.astype(np.float32), 128, 0)[:n], 128, 1)[:, :k]
@@ -140,6 +191,33 @@ def qlinear(x: np.ndarray, wdq: np.ndarray, pow2: bool = True) -> np.ndarray:
     q, s = act_quant(x, 128, pow2)
     da = dequant_act(q, s)
     return bf16_round((da @ wdq.T).astype(np.float32))
+
+
+# Activation batches up to this many rows take oracle/dequant.c's fused dequant-and-dot (no
+# dequantised copy of the weight); wider ones dequantise once and multiply with BLAS.
+QGEMM_C_ROWS = 64
+
+
+def qlinear_packed(x: np.ndarray, fmt: int, packed: np.ndarray, scale: np.ndarray, ts: float = 1.0,
+                   pow2: bool = True) -> np.ndarray:
+    """qlinear with the weight still quantised: the same arithmetic, the dequantisation done per
+    weight row inside the GEMM for narrow batches."""
+    lib = _clib()
+    if lib is None or x.shape[0] > QGEMM_C_ROWS:
+        return qlinear(x, dequant_weight(fmt, packed, scale, ts), pow2)
+    q, s = act_quant(x, 128, pow2)
+    da = np.ascontiguousarray(dequant_act(q, s), dtype=np.float32)
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    n = packed.shape[0]
+    k = da.shape[1]
+    sc = np.ascontiguousarray(scale, dtype=np.float32 if fmt == FMT_FP8 else np.uint8)
+    y = np.empty((da.shape[0], n), dtype=np.float32)
+    row = np.empty(k, dtype=np.float32)
+    rc = lib.oracle_qgemm(fmt, packed.ctypes.data, sc.ctypes.data, float(np.float32(ts)), n, k, da.ctypes.data,
+                          da.shape[0], y.ctypes.data, row.ctypes.data)
+    if rc != 0:
+        raise ValueError(fmt)
+    return bf16_round(y)
 
 
 # ── the MoE ────────────────────────────────────────────────────────────────────────────────────
@@ -189,14 +267,11 @@ def expert_forward(x: np.ndarray, fmt: int, ew, swiglu_limit: float, weight=None
     inter = i2 // 2
     if fmt == FMT_FP8:
         bi = inter // 128
-        w1 = dequant_weight(fmt, w13[:inter], w13_s[:bi])
-        w3 = dequant_weight(fmt, w13[inter:], w13_s[bi:])
+        g = qlinear_packed(x, fmt, w13[:inter], w13_s[:bi], 1.0, pow2)
+        u = qlinear_packed(x, fmt, w13[inter:], w13_s[bi:], 1.0, pow2)
     else:
-        w1 = dequant_weight(fmt, w13[:inter], w13_s[:inter], float(w13_ts[0]))
-        w3 = dequant_weight(fmt, w13[inter:], w13_s[inter:], float(w13_ts[1]))
-    wd2 = dequant_weight(fmt, w2, w2_s, float(w2_ts[0]))
-    g = qlinear(x, w1, pow2)
-    u = qlinear(x, w3, pow2)
+        g = qlinear_packed(x, fmt, w13[:inter], w13_s[:inter], float(w13_ts[0]), pow2)
+        u = qlinear_packed(x, fmt, w13[inter:], w13_s[inter:], float(w13_ts[1]), pow2)
     if swiglu_limit > 0:
         lim = np.float32(swiglu_limit)
         u = np.clip(u, -lim, lim)
@@ -206,7 +281,7 @@ def expert_forward(x: np.ndarray, fmt: int, ew, swiglu_limit: float, weight=None
     if weight is not None:
         h = (weight.astype(np.float32) * h).astype(np.float32)
     h = bf16_round(h)
-    return qlinear(h, wd2, pow2)
+    return qlinear_packed(h, fmt, w2, w2_s, float(w2_ts[0]), pow2)
 
 
 class OracleLayer:

@@ -55,6 +55,7 @@ SIGNATURES = {
     "sb_qgemm_workspace_bytes": (_sz, [_int, _int, _i64, _i64, _i64]),
     "sb_qgemm": (_int, [_int, _int, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _sz, _vp]),
     "sb_qgemm_static": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
+    "sb_qgemm_static_error": (_int, [ctypes.POINTER(ctypes.c_int), _vp]),
     "sb_moe_workspace_bytes": (_sz, [ctypes.POINTER(SbMoeLayer), _i64]),
     "sb_moe_forward": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sb_moe_forward_profiled": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp,
@@ -65,6 +66,7 @@ SIGNATURES = {
     "sb_wire_pack": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "sb_wire_unpack": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "sb_selftest_formats": (_int, [_vp, _vp]),
+    "sb_debug_set_wait_limit": (_int, [_i64]),
 }
 
 _LIB = None

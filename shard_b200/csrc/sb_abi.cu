@@ -6,7 +6,7 @@
 #include <stdio.h>
 #include <string.h>
 
-#include <mutex>
+#include <atomic>
 #include <string>
 
 #include "../../include/shard_b200.h"
@@ -15,6 +15,10 @@
 namespace {
 
 thread_local std::string g_err;
+
+// Consumer-side wait limit of the tensor-core kernels (polls; 0 = each kernel's default), set by
+// sb_debug_set_wait_limit for tests of the timeout path.
+std::atomic<uint32_t> g_wait_limit{0};
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -346,6 +350,7 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
     a.shared.s_stride = 0;
     a.routed = a.shared;
     a.err = err;
+    a.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
     a.items_per_expert = (int)(n / 128);
     return cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert, st), "qgemm");
   }
@@ -362,25 +367,15 @@ static __device__ __align__(256) uint8_t g_qgemm_static_scratch[SB_QGEMM_STATIC_
 
 namespace {
 
-constexpr int kStaticMaxDevices = 64;
-std::mutex g_static_mu;
-void* g_static_ptr[kStaticMaxDevices];
-
-// Device address of this device's static scratch, looked up once per device (with the device
-// current) by the first call on it.
+// Device address of the current device's static scratch. It is looked up on every call (a host-side
+// table lookup once the module is loaded on the device), so a device reset or a new primary context
+// never leaves a stale address behind. The first call on a device loads the module there: that
+// first call comes before any stream capture.
 int static_scratch(void** out) {
-  int dev = 0;
-  int rc = cuda_check(cudaGetDevice(&dev), "qgemm_static: cudaGetDevice");
+  void* p = nullptr;
+  const int rc = cuda_check(cudaGetSymbolAddress(&p, g_qgemm_static_scratch), "qgemm_static: cudaGetSymbolAddress");
   if (rc) return rc;
-  if (dev < 0 || dev >= kStaticMaxDevices) return fail(SB_ERR_UNSUPPORTED, "qgemm_static: device %d", dev);
-  std::lock_guard<std::mutex> lock(g_static_mu);
-  if (g_static_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    rc = cuda_check(cudaGetSymbolAddress(&p, g_qgemm_static_scratch), "qgemm_static: cudaGetSymbolAddress");
-    if (rc) return rc;
-    g_static_ptr[dev] = p;
-  }
-  *out = g_static_ptr[dev];
+  *out = p;
   return SB_OK;
 }
 
@@ -456,6 +451,17 @@ int sb_qgemm_static(int fmt, const void* w, const void* w_s, const float* ts, in
   a.err = err;
   a.items_per_expert = (int)(n / 128);
   return cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert, st), "qgemm_static");
+}
+
+int sb_qgemm_static_error(int* host_out, void* stream) {
+  if (!host_out) return fail(SB_ERR_ARG, "qgemm_static_error: NULL pointer");
+  void* base = nullptr;
+  int rc = static_scratch(&base);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  rc = cuda_check(cudaMemcpyAsync(host_out, base, sizeof(int), cudaMemcpyDeviceToHost, st), "qgemm_static_error");
+  if (rc) return rc;
+  return cuda_check(cudaStreamSynchronize(st), "qgemm_static_error");
 }
 
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
@@ -590,6 +596,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   g.pair_slot = w.pair_slot;
   g.topk_w = w.topk_w;
   g.err = w.err;
+  g.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
   const int n_units = (int)(max_active + (L->has_shared ? 1 : 0));
   if (L->layout == SB_LAYOUT_TC && w.wide) {
     // prefill kernel: x (act-quantised, bf16) in expert order, w13 (+ SwiGLU -> h), h act-quantised
@@ -775,6 +782,12 @@ int sb_wire_unpack(const void* q, const void* scale, int64_t rows, int64_t dim, 
   if (!aligned16(y) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(SB_ERR_ARG, "wire_unpack: y 16-byte, q 8-byte aligned");
   if (rows == 0) return SB_OK;
   return cuda_check(sb::launch_wire_unpack((const uint8_t*)q, scale, rows, dim, y, (cudaStream_t)stream), "wire_unpack");
+}
+
+int sb_debug_set_wait_limit(int64_t polls) {
+  if (polls < 0 || polls > (int64_t)UINT32_MAX) return fail(SB_ERR_ARG, "debug_set_wait_limit: %lld", (long long)polls);
+  g_wait_limit.store((uint32_t)polls, std::memory_order_relaxed);
+  return SB_OK;
 }
 
 int sb_selftest_formats(float* out, void* stream) {

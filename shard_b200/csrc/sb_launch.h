@@ -81,6 +81,7 @@ struct GroupedArgs {
   int* err;            // device flag: set to 1 if a bounded wait gave up (must start at 0)
   __nv_bfloat16* hbf;  // tensor-core path: h in bf16 (W13 writes it, the W2 panel quantises it)
   int n_experts;       // tensor-core path: matrices in the routed bank
+  uint32_t wait_limit; // tensor-core path: polls of the consumer-side waits (0: the kernel's default)
 };
 
 // Tensor-core path: the activation operand of every pass, prepared before the grouped launch.

@@ -132,12 +132,13 @@ __device__ __forceinline__ void set_abort(Smem& sm, int* err, bool flag_err) {
   *reinterpret_cast<volatile int*>(&sm.abort) = 1;
 }
 
-// bounded wait; on timeout flag the CTA (and the launch) and return false
-__device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t parity) {
-  // poll without a suspend hint first (most waits end within a few hundred cycles), then sleep
-  for (uint32_t i = 0; i < 256; ++i)
+// bounded wait; on timeout flag the CTA (and the launch) and return false. `limit` polls: up to 256
+// without a suspend hint first (most waits end within a few hundred cycles), then, for limits of
+// 256 and more, `limit` polls that may each sleep up to ~1 us.
+__device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t parity, uint32_t limit = WAIT_LIMIT) {
+  for (uint32_t i = 0; i < 256u && i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+  for (uint32_t i = 0; limit >= 256u && i < limit; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
     if ((i & 63u) == 63u && aborted(sm)) return false;
   }
@@ -146,8 +147,9 @@ __device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t 
 }
 
 // bounded wait by a whole warp; true only if every lane saw the phase complete (reconverges the warp)
-__device__ __forceinline__ bool warp_wait(Smem& sm, int* err, uint32_t bar, uint32_t parity) {
-  const bool ok = wait(sm, err, bar, parity);
+__device__ __forceinline__ bool warp_wait(Smem& sm, int* err, uint32_t bar, uint32_t parity,
+                                          uint32_t limit = WAIT_LIMIT) {
+  const bool ok = wait(sm, err, bar, parity, limit);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -259,6 +261,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
                      (a.mode == MODE_DENSE ? 0 : ta.plan.pass_off[*a.n_active]);
   const int n_items = n_pass * nrb;
   const bool w13 = a.mode == MODE_W13;
+  // the limit of the consumer-side waits (the MMA issuer's and the readback's); the producer's waits
+  // for free slots and the final drains keep WAIT_LIMIT
+  const uint32_t clim = a.wait_limit ? a.wait_limit : WAIT_LIMIT;
 
   // per-item constants shared by the roles
   auto item_fmt = [&](const Item& it) { return it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R; };
@@ -346,13 +351,13 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         for (int j = 0; j < nst && ok; j += UNIT, ++u) {
           const int ns = min(UNIT, nst - j);
           const uint32_t q = u % SA;
-          if (!warp_wait(sm, err, smem_addr(&sm.gempty[q]), ((u / SA) & 1u) ^ 1u)) {
+          if (!warp_wait(sm, err, smem_addr(&sm.gempty[q]), ((u / SA) & 1u) ^ 1u, clim)) {
             ok = false;
             break;
           }
           for (int t = 0; t < ns; ++t, ++g) {
             const uint32_t s = g % ST;
-            if (!warp_wait(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u)) {
+            if (!warp_wait(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u, clim)) {
               ok = false;
               break;
             }
@@ -434,7 +439,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
           const int ns = min(UNIT, nst - j);
           const uint32_t us = u % SS, q = u % SA;
           // this unit's scales first (they landed long ago), so their loads overlap the MMA wait
-          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u);
+          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u, clim);
           if (!ok) continue;
           float sc[UNIT][8];
 #pragma unroll
@@ -464,7 +469,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
               for (int c = 4; c < 8; ++c) sc[t][c] = 0.f;
             }
           }
-          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.gfull[q]), (u / SA) & 1u);
+          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.gfull[q]), (u / SA) & 1u, clim);
           if (!ok) continue;
           fence_after();
           const uint32_t taddr = tbase + ((uint32_t)(warp * 32) << 16) + q * GCOLS;

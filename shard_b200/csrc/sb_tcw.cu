@@ -703,6 +703,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
   auto pass_tokens = [&](const Item& it) { return min(wn, it.cnt - it.pb); };
   auto wait = [&](uint32_t bar, uint32_t parity) { return wait_bounded(abort_flag, err, bar, parity, WAIT_LIMIT); };
   auto warp_wait = [&](uint32_t bar, uint32_t parity) { return __all_sync(0xffffffffu, wait(bar, parity)); };
+  // consumer-side waits (the MMA issuer's on its operands, the converters' on the staging copies and
+  // the epilogue's on the accumulator) take the launch's limit; waits for free slots and the final
+  // drains keep WAIT_LIMIT
+  const uint32_t clim = a.wait_limit ? a.wait_limit : WAIT_LIMIT;
+  auto cwait = [&](uint32_t bar, uint32_t parity) { return wait_bounded(abort_flag, err, bar, parity, clim); };
 
   if (warp == PRODUCER_WARP) {
     // both row blocks' weight stages (TMA) and their scales (bulk copies) into one staging slot
@@ -808,8 +813,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
         for (int i = 0; i < nsub && ok; ++i, ++gw) {
           const uint32_t sws = gw % SW, ts = gt % STT;
           const int j = i & (bg.spb - 1);
-          if (!wait(smem_addr(&sm.wfull[sws]), (gw / SW) & 1u) ||
-              (j == 0 && !wait(smem_addr(&sm.tfull[ts]), (gt / STT) & 1u))) {
+          if (!cwait(smem_addr(&sm.wfull[sws]), (gw / SW) & 1u) ||
+              (j == 0 && !cwait(smem_addr(&sm.tfull[ts]), (gt / STT) & 1u))) {
             ok = false;
             break;
           }
@@ -853,7 +858,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
       const int nstg = fp4 ? nst : nsub;
       for (int st = 0; st < nstg; ++st, ++c) {
         const uint32_t s = c % SC;
-        if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
+        if (ok) ok = __all_sync(0xffffffffu, cwait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
         const uint8_t* stg = sm.stg[s] + hb * STG_RB;
         uint32_t s2 = 0;
         if (ok && fmt == FMT_FP8) {
@@ -897,7 +902,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
       }
       // epilogue: TMEM lane = token (32 (warp & 3) + lane), the warp half hh takes row block 2 rb + hh
       const uint32_t buf = np & 1u;
-      if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
+      if (ok) ok = __all_sync(0xffffffffu, cwait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
       if (bar_any(1, 32 * NWORK, !ok || *abort_flag)) break;
       fence_after();
       const int hh = warp >> 2;

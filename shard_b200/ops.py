@@ -6,8 +6,11 @@ otherwise), the wrapper allocates its output, the result is in torch's default d
 bf16, the dtype the reference runs in. Installing this module as `sys.modules["kernel"]` before the
 reference model.py is executed routes every quantised `linear()` through these kernels.
 
-Weights arrive in the reference's canonical layout and are tiled on first use (cached per tensor):
-the tiled copy is what the GEMV streams.
+Weights arrive in the reference's canonical layout and are tiled on first use. The tiled copy (and,
+for NVFP4, the tensor scale as a device scalar) is cached as an attribute of the weight tensor
+itself, so it lives and dies with that tensor: a new tensor that happens to reuse a freed weight's
+address never sees the old copy, and an in-place change of the weight (its version counter) or a
+different scale tensor retiles it.
 """
 from __future__ import annotations
 
@@ -16,8 +19,6 @@ import torch
 from . import _lib
 from . import formats as F
 from ._lib import check, lib, ptr, stream_ptr
-
-_TILED = {}
 
 
 def act_quant(x: torch.Tensor, block_size: int = 128, scale_fmt=None, scale_dtype=torch.float32,
@@ -40,19 +41,30 @@ def act_quant(x: torch.Tensor, block_size: int = 128, scale_fmt=None, scale_dtyp
     return y, s
 
 
-def _tiled(fmt, b, b_s, layout):
-    key = (fmt, layout, b.data_ptr(), b_s.data_ptr(), tuple(b.shape), b._version)
-    t = _TILED.get(key)
-    if t is None:
-        from .moe import tile
-        n = b.size(0)
-        k = b.size(1) * (2 if fmt != F.FMT_FP8 else 1)
-        if fmt == F.FMT_FP8:
-            s = F.e8m0_decode(b_s.view(torch.uint8)) if b_s.dtype == torch.float8_e8m0fnu else b_s.float()
-        else:
-            s = b_s.view(torch.uint8)
-        t = _TILED[key] = tile(fmt, _lib.MAT_PLAIN, b.view(torch.uint8), s, 1, n, k, layout)
-    return t
+_CACHE_ATTR = "_sb_tiled"
+
+
+def _tiled(fmt, b, b_s, layout, tensor_scale=None):
+    """(tiled values, tiled scales, NVFP4 tensor scale on the device or None), cached on `b`."""
+    key = (fmt, layout, b.data_ptr(), b._version, id(b_s), b_s.data_ptr(), b_s._version, tuple(b.shape),
+           None if tensor_scale is None else float(tensor_scale))
+    hit = getattr(b, _CACHE_ATTR, None)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    from .moe import tile
+    n = b.size(0)
+    k = b.size(1) * (2 if fmt != F.FMT_FP8 else 1)
+    if fmt == F.FMT_FP8:
+        s = F.e8m0_decode(b_s.view(torch.uint8)) if b_s.dtype == torch.float8_e8m0fnu else b_s.float()
+    else:
+        s = b_s.view(torch.uint8)
+    wt, st = tile(fmt, _lib.MAT_PLAIN, b.view(torch.uint8), s, 1, n, k, layout)
+    ts = None
+    if fmt == F.FMT_NVFP4:
+        ts = torch.tensor([float(tensor_scale)], dtype=torch.float32).to(b.device)
+    val = (wt, st, ts)
+    setattr(b, _CACHE_ATTR, (key, val))
+    return val
 
 
 def _act_scales_f32(a_s):
@@ -67,10 +79,7 @@ def quantised_gemm(fmt: int, w, w_s, tensor_scale, a, a_s, layout=None):
     k = a.size(-1)
     m = a.numel() // k
     n = w.size(0)
-    wt, st = _tiled(fmt, w, w_s, layout)
-    ts = None
-    if fmt == F.FMT_NVFP4:
-        ts = torch.tensor([float(tensor_scale)], dtype=torch.float32, device=a.device)
+    wt, st, ts = _tiled(fmt, w, w_s, layout, tensor_scale if fmt == F.FMT_NVFP4 else None)
     sa = _act_scales_f32(a_s).contiguous()
     y = torch.empty(*a.shape[:-1], n, dtype=torch.bfloat16, device=a.device)
     L = lib()

@@ -181,6 +181,12 @@ def _random_canonical(fmt, n_mat, n, k, device, gen):
     return w, s
 
 
+def normal_expert(cfg: MoEConfig, layer: int, expert: int, device="cuda") -> ExpertWeights:
+    """The canonical bytes of one expert of a fill="normal" device layer (regenerated: the same
+    generator seeds give the same draws and the same quantisation)."""
+    return _normal_expert_on_device(cfg, layer, expert, cfg.expert_fmt, device)
+
+
 def _normal_expert_on_device(cfg, layer, expert, fmt, device):
     """N(0, 0.02) draws quantised on the device (fast path for benchmark layers)."""
     h, i = cfg.hidden, cfg.inter

@@ -51,7 +51,14 @@ CASES = {
                                       "zipf_s": 1.1, "gate_init": "normal", "seed": 7}, 16, 1.0, "ue8m0"),
     "c1_nvfp4_m4": ("c1", {}, 4, 1.0, "ue8m0"),
     "c3_fp8_m2": ("c3", {}, 2, 1.0, "ue8m0"),
+    # a c4-shaped layer with 16 experts: 128 routed tokens per expert on average (Zipf-skewed, some
+    # experts over one 128-token pass), the shape where the prefill kernel is the default choice
+    "c4e16_nvfp4_m256": ("c4", {"n_experts": 16}, 256, 1.0, "ue8m0"),
 }
+
+# Cases whose reference module is also recorded as a seam fixture (seam_<case>.json): the module's
+# structure, attributes, parameter dtypes and shapes, and the SHA-256 of every parameter's bytes.
+SEAM_CASES = ("c0_mxfp4_m8", "c0_nvfp4_m8", "small_fp8_noshared_m16")
 
 
 def case_config(name):
@@ -120,6 +127,42 @@ def _fill_expert(expert, fmt, ew, inter):
     _fill_linear(expert.w2, fmt, ew.w2, ew.w2_s, ew.w2_ts[0])
 
 
+def _sha(t):
+    import hashlib
+    return hashlib.sha256(t.detach().contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def seam_record(mod, moe):
+    """What shard_b200.moe.layer_from_module and b200_moe_forward read from a reference MoE module
+    (model.py:129-158 Linear, :569-589 Gate, :592-611 Expert, :614-632 MoE) and from the module that
+    defines it, with every parameter's dtype, shape and byte hash."""
+    def lin(l):
+        return {"in_features": l.in_features, "out_features": l.out_features,
+                "weight_scale_is_scale": getattr(l.weight, "scale", None) is l.scale,
+                "tensor_scale": getattr(l.weight, "tensor_scale", None)}
+
+    g = moe.gate
+    rec = {
+        "module": {"world_size": mod.world_size, "rank": mod.rank, "scale_fmt": mod.scale_fmt,
+                   "scale_dtype": str(mod.scale_dtype), "block_size": mod.block_size,
+                   "fp4_block_size": mod.fp4_block_size},
+        "moe": {"layer_id": moe.layer_id, "dim": moe.dim, "n_routed_experts": moe.n_routed_experts,
+                "n_activated_experts": moe.n_activated_experts, "experts_start_idx": moe.experts_start_idx,
+                "experts_end_idx": moe.experts_end_idx},
+        "gate": {"dim": g.dim, "topk": g.topk, "score_func": g.score_func, "route_scale": g.route_scale,
+                 "hash": g.hash},
+        "swiglu_limit": moe.shared_experts.swiglu_limit,
+        "linears": {},
+        "params": {},
+    }
+    for name, sub in moe.named_modules():
+        if hasattr(sub, "in_features") and hasattr(sub, "weight"):
+            rec["linears"][name] = lin(sub)
+    for name, p in moe.named_parameters():
+        rec["params"][name] = {"dtype": str(p.dtype), "shape": list(p.shape), "sha": _sha(p)}
+    return rec
+
+
 def run_case(mod, K, name, out_dir):
     cfg, m, xscale, sfmt = case_config(name)
     x, ids = case_inputs(cfg, m, xscale)
@@ -174,6 +217,11 @@ def run_case(mod, K, name, out_dir):
             y = moe(x.view(1, m, h), ids.view(1, m)).view(m, h)
     finally:
         torch.set_default_dtype(prev)
+    if name in SEAM_CASES:
+        rec = seam_record(mod, moe)
+        rec["case"] = name
+        with open(os.path.join(out_dir, f"seam_{name}.json"), "w") as f:
+            json.dump(rec, f, indent=1, sort_keys=True)
     meta = dict(case=name, config=cfg.name, overrides=CASES[name][1], m=m, x_scale=xscale,
                 scale_fmt=sfmt, layer=0, reference="leyten/shard model.py MoE.forward on v4_kernels_cpu")
     np.savez_compressed(

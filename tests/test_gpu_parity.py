@@ -128,7 +128,7 @@ def test_forward_matches_oracle(name):
 @pytest.mark.parametrize("cname,m", [("c1", 1), ("c1", 8), ("c1", 32), ("c1", 64), ("c3", 16), ("c3", 64),
                                      ("c4", 256), ("c4", 1024)])
 def test_full_size_forward(cname, m, layout):
-    """Full BASELINE shapes. The oracle checks a sample of tokens (its cost grows with the experts
+    """Full configuration shapes. The oracle checks a sample of tokens (its cost grows with the experts
     they route to); the whole batch is checked for row invariance: every token's output equals the
     same token run alone through the same kernel, bit for bit. The tensor-core layout runs both of
     its expert kernels (verify and prefill), and the default choice must equal the one it picks."""
@@ -162,6 +162,45 @@ def test_full_size_forward(cname, m, layout):
         assert torch.equal(auto, ys[2 if wide else 1])
         # the two kernels sum in different orders; they agree to well within the parity bar
         assert O.max_rel_err(_np(ys[1]), _np(ys[2])) < TOL
+
+
+@pytest.mark.parametrize("cname,m", [("c1", 64), ("c3", 64), ("c4", 256), ("c4", 1024)])
+def test_full_size_forward_every_token(cname, m):
+    """Every token of a full-size batch against the oracle, through both tensor-core expert kernels.
+    The layer's experts are N(0, 0.02) draws quantised on the device (the benchmark's layers); the
+    oracle regenerates the bytes of each routed expert it needs and runs its C dequant-GEMM."""
+    import threading
+    cfg = S.CONFIGS[cname]
+    x, ids = S.make_inputs(cfg, m)
+    lay = S.device_layer(cfg, 0, "cuda", seeded=[], fill="normal")
+    gw, gb = S.make_gate(cfg)
+    lock = threading.Lock()
+
+    def expert(e):
+        with lock:
+            ew = S.normal_expert(cfg, 0, e, "cuda")
+            return tuple(t.cpu().numpy() for t in (ew.w13, ew.w13_s, ew.w13_ts, ew.w2, ew.w2_s, ew.w2_ts))
+
+    sh = S.make_expert(cfg, 0, -1, F.FMT_FP8) if cfg.n_shared else None
+    ol = O.OracleLayer(hidden=cfg.hidden, inter=cfg.inter, topk=cfg.topk, score_func=cfg.score_func,
+                       route_scale=cfg.route_scale, swiglu_limit=cfg.swiglu_limit, expert_fmt=cfg.expert_fmt,
+                       gate_w=gw.float().numpy(), gate_b=gb.numpy(), expert=expert,
+                       shared=None if sh is None else tuple(t.numpy() for t in (sh.w13, sh.w13_s, sh.w13_ts, sh.w2,
+                                                                                   sh.w2_s, sh.w2_ts)))
+    yo, wo, io = O.moe_forward(ol, x.float().numpy(), workers=16)
+    for mode in (1, 2):
+        lay.prefill = mode
+        y, w, idx = lay.forward(x.cuda(), ids.cuda(), routing=True)
+        torch.cuda.synchronize()
+        assert np.array_equal(idx.cpu().numpy(), io), "router top-k indices must be bit-exact"
+        assert np.abs(w.cpu().numpy() - wo).max() < 1e-5
+        yg = _np(y)
+        err = O.max_rel_err(yg, yo)
+        assert err < TOL, f"{cname} M={m} prefill={mode}: max rel err {err:.3e}"
+        rows = [O.max_rel_err(yg[t], yo[t]) for t in range(m)]
+        worst = int(np.argmax(rows))
+        assert rows[worst] < TOL, f"{cname} M={m} prefill={mode}: token {worst} max rel err {rows[worst]:.3e}"
+        assert lay.device_error() == 0
 
 
 @pytest.mark.parametrize("prefill", [1, 2])
@@ -213,3 +252,45 @@ def test_hash_routing_drops_earlier_duplicate_slots(prefill):
         yo[rows] = yo[rows] + out                          # repeated rows: the last write wins
     yo = O.bf16_round(yo + O.expert_forward(x.float().numpy(), F.FMT_FP8, ol.shared, 0.0))
     assert O.max_rel_err(_np(y), yo) < TOL
+
+
+@pytest.mark.parametrize("fmt", [F.FMT_FP8, F.FMT_NVFP4])
+def test_kernel_seam_retiles_a_new_weight_at_a_freed_address(fmt):
+    """The kernel seam caches each weight's tiled copy on the weight tensor. A weight freed and
+    replaced by a same-shape tensor (which the caching allocator hands the same address) must give
+    the new weight's result, not the old tiled copy's; an in-place change of a weight retiles too."""
+    from shard_b200 import ops
+    n, k, m = 512, 1024, 4
+    g = torch.Generator().manual_seed(99 + fmt)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    qx, sx = ops.act_quant(x.cuda(), 128, "ue8m0")
+
+    def quant(seed):
+        w = (torch.randn(n, k, generator=torch.Generator().manual_seed(seed)) * 0.02).to(torch.bfloat16)
+        if fmt == F.FMT_NVFP4:
+            p, s, ts = F.quant_nvfp4(w)
+            return p, s, ts, O.dequant_weight(O.FMT_NVFP4, p.numpy(), s.numpy(), ts)
+        p, s = F.quant_fp8_block(w)
+        return p, s, 1.0, O.dequant_weight(O.FMT_FP8, p.numpy(), s.numpy())
+
+    def run(pw, ps, ts):
+        return ops.quantised_gemm(fmt, pw, ps, ts, qx, sx)
+
+    p1, s1, t1, d1 = quant(1)
+    w1, ws1 = p1.cuda(), s1.cuda()
+    y1 = run(w1, ws1, t1)
+    addr = w1.data_ptr()
+    del w1, ws1
+    p2, s2, t2, d2 = quant(2)
+    w2, ws2 = p2.cuda(), s2.cuda()
+    y2 = run(w2, ws2, t2)
+    r1 = O.qlinear(x.float().numpy(), d1, True)
+    r2 = O.qlinear(x.float().numpy(), d2, True)
+    assert O.max_rel_err(_np(y1), r1) < TOL
+    assert O.max_rel_err(_np(y2), r2) < TOL, \
+        f"stale tiled copy (same address: {addr == w2.data_ptr()})"
+    # in place: the weight's version counter moves and the next call retiles
+    w2.copy_(p1.cuda())
+    ws2.copy_(s1.cuda())
+    y3 = run(w2, ws2, t1)
+    assert O.max_rel_err(_np(y3), r1) < TOL

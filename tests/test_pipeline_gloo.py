@@ -79,7 +79,7 @@ def _expected_fp8(world):
     return outs
 
 
-def _rank_main(rank, world, port, out_path, wire="bf16"):
+def _rank_main(rank, world, port, out_path, wire="bf16", depth=4, runs=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -87,12 +87,15 @@ def _rank_main(rank, world, port, out_path, wire="bf16"):
     try:
         block = even_tiling(N_LAYERS, world)[rank]
         pipe = Pipeline(StageStack([Affine(l) for l in block]), M, HIDDEN, rank, world, torch.device("cpu"),
-                        wire=wire, codec=_oracle_codec() if wire == "fp8" else None)
-        chunks = _inputs() if rank == 0 else None
-        outs = [torch.empty(M, HIDDEN, dtype=torch.bfloat16) for _ in range(CHUNKS)] if rank == world - 1 else None
-        pipe.run(CHUNKS, chunks, outs)
+                        depth=depth, wire=wire, codec=_oracle_codec() if wire == "fp8" else None)
+        all_outs = []
+        for r in range(runs):
+            chunks = [(x.float() + r).to(torch.bfloat16) for x in _inputs()] if rank == 0 else None
+            outs = [torch.empty(M, HIDDEN, dtype=torch.bfloat16) for _ in range(CHUNKS)] if rank == world - 1 else None
+            pipe.run(CHUNKS, chunks, outs)
+            all_outs.append(outs)
         if rank == world - 1:
-            torch.save(outs, out_path)
+            torch.save(all_outs[0] if runs == 1 else all_outs, out_path)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -135,3 +138,20 @@ def test_two_stage_gloo_pipeline_with_the_fp8_wire():
     for g, e in zip(got, exp):
         assert torch.equal(g, e)
     assert any(not torch.equal(g, e) for g, e in zip(got, _expected()))
+
+
+def test_three_stage_pipeline_streams_runs_back_to_back():
+    """The middle stage both receives (posted `depth` chunks ahead into a ring of 2) and sends; two
+    runs follow each other with no barrier between them, and every chunk of both arrives in order."""
+    runs = 2
+    with tempfile.TemporaryDirectory() as d:
+        out_path = os.path.join(d, "outs.pt")
+        mp.start_processes(_rank_main, args=(3, _free_port(), out_path, "bf16", 2, runs), nprocs=3, join=True,
+                           start_method="spawn")
+        got = torch.load(out_path)
+    for r in range(runs):
+        for j, x in enumerate(_inputs()):
+            x = (x.float() + r).to(torch.bfloat16)
+            for l in range(N_LAYERS):
+                x = Affine(l).forward(x)
+            assert torch.equal(got[r][j], x), f"run {r} chunk {j}"

@@ -66,12 +66,49 @@ def test_static_scratch_matches_workspace_entry(fmt, m, n, k):
         y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
         _lib.check(L.sb_qgemm_static(fmt, wt.data_ptr(), ws_.data_ptr(), _lib.ptr(ts), n, k, q.data_ptr(),
                                      s.data_ptr(), m, y.data_ptr(), st), "sb_qgemm_static")
+        assert _static_error() == 0, "a kernel of sb_qgemm_static gave up a bounded wait"
         outs.append(y)
     torch.cuda.synchronize()
     for y in outs:
         assert torch.isfinite(y.float()).all()
         assert _rel(y, ref) < TOL
     assert torch.equal(outs[0], outs[1])
+
+
+def _static_error():
+    flag = ctypes.c_int(-1)
+    _lib.check(_lib.lib().sb_qgemm_static_error(ctypes.byref(flag), _lib.stream_ptr()), "sb_qgemm_static_error")
+    return flag.value
+
+
+def _run_both(fmt, m, n, k):
+    """(static result, workspace result) for one shape."""
+    L = _lib.lib()
+    st = _lib.stream_ptr()
+    wt, ws_, ts = _weights(fmt, n, k, seed=3 * n + k + fmt)
+    q, s = _acts(m, k, seed=7 * m + k)
+    wsb = L.sb_qgemm_workspace_bytes(fmt, _lib.LAYOUT_TC, n, k, m)
+    work = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    ref = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _lib.check(L.sb_qgemm(fmt, _lib.LAYOUT_TC, wt.data_ptr(), ws_.data_ptr(), _lib.ptr(ts), n, k,
+                          q.data_ptr(), s.data_ptr(), m, ref.data_ptr(), work.data_ptr(), wsb, st), "sb_qgemm")
+    y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    _lib.check(L.sb_qgemm_static(fmt, wt.data_ptr(), ws_.data_ptr(), _lib.ptr(ts), n, k, q.data_ptr(),
+                                 s.data_ptr(), m, y.data_ptr(), st), "sb_qgemm_static")
+    assert _static_error() == 0
+    return y, ref
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", [F.FMT_NVFP4, F.FMT_FP8])
+def test_static_scratch_smaller_call_after_larger(fmt):
+    """A call with fewer passes and a shorter K right after a larger one: the region still holds the
+    larger call's panel, and the smaller call must read only what it wrote."""
+    for m, n, k in [(40, 384, 4096), (13, 512, 2048), (1, 256, 512)]:
+        y, ref = _run_both(fmt, m, n, k)
+        torch.cuda.synchronize()
+        assert torch.isfinite(y.float()).all()
+        assert _rel(y, ref) < TOL
 
 
 def test_static_scratch_rejects_oversize():
@@ -86,3 +123,20 @@ def test_static_scratch_rejects_oversize():
     msg = L.sb_last_error()
     msg = msg.decode() if isinstance(msg, bytes) else msg
     assert "static region" in msg and str(need) in msg
+
+
+@pytest.mark.parametrize("fmt,m_max", [(F.FMT_FP8, 272), (F.FMT_MXFP4, 272), (F.FMT_NVFP4, 136)])
+def test_static_scratch_limits_at_k7168(fmt, m_max):
+    """The stated limits at k = 7168 (m <= 272, NVFP4 m <= 136), pinned from both sides on the host:
+    the largest allowed m fits the region, the next pass (one more pass of 16 or 8 tokens) is refused."""
+    L = _lib.lib()
+    n, k = 256, 7168
+    step = 8 if fmt == F.FMT_NVFP4 else 16
+    assert L.sb_qgemm_workspace_bytes(fmt, _lib.LAYOUT_TC, n, k, m_max) <= 2 << 20
+    assert L.sb_qgemm_workspace_bytes(fmt, _lib.LAYOUT_TC, n, k, m_max + step) > 2 << 20
+    p = ctypes.c_void_p(256)
+    ts = p if fmt == F.FMT_NVFP4 else None
+    rc = L.sb_qgemm_static(fmt, p, p, ts, n, k, p, p, m_max + step, p, None)
+    assert rc == -2, "one pass beyond the limit must be refused"
+    rc = L.sb_qgemm_static(fmt, p, p, ts, n, k, p, p, m_max + 1, p, None)
+    assert rc == -2
