@@ -132,11 +132,14 @@ __device__ __forceinline__ void set_abort(Smem& sm, int* err, bool flag_err) {
   *reinterpret_cast<volatile int*>(&sm.abort) = 1;
 }
 
-// bounded wait; on timeout flag the CTA (and the launch) and return false. `limit` polls: up to 256
-// without a suspend hint first (most waits end within a few hundred cycles), then, for limits of
-// 256 and more, `limit` polls that may each sleep up to ~1 us.
+// bounded wait; on timeout flag the CTA (and the launch) and return false. `limit` polls: 256
+// without a suspend hint first (most waits end within a few hundred cycles), then `limit` polls
+// that may each sleep up to ~1 us. A limit below 256 (the timeout-path test) makes `limit`
+// non-blocking probes instead, so a phase not complete at that moment runs the wait out.
 __device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t parity, uint32_t limit = WAIT_LIMIT) {
-  for (uint32_t i = 0; i < 256u && i < limit; ++i)
+  for (uint32_t i = 0; limit < 256u && i < limit; ++i)
+    if (mbar_test_wait(bar, parity)) return true;
+  for (uint32_t i = 0; limit >= 256u && i < 256u; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   for (uint32_t i = 0; limit >= 256u && i < limit; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
