@@ -161,7 +161,10 @@ int sb_qgemm_static_error(int* host_out, void* stream);
 
 /* ── the MoE stage forward (MoE.forward, model.py:634-649; Gate.forward :569-589;
  *    Expert.forward :601-611; grouped decode v4_moe_grouped.py:634-709) ──────────────────────── */
-/* Bytes of workspace for a forward of up to m tokens (the size serves every m' <= m). */
+/* Bytes of workspace for a forward of up to m tokens (the size serves every m' <= m). A new
+ * workspace's first 16 bytes must be zero before its first forward (one cudaMemsetAsync after
+ * allocating it): they hold the error flags and the routing kernel's completion counter, which every
+ * forward leaves zero again. Forwards that share a workspace must not overlap on the GPU. */
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m);
 /* x bf16 [M, H] -> y bf16 [M, H]. input_ids int64 [M] (read only for hash routing; may be NULL
  * otherwise). Optional outputs (NULL to skip): routing weights fp32 [M, k] and top-k indices

@@ -24,6 +24,8 @@ struct RouteArgs {
   const __nv_bfloat16* x;    // [M, H]
   uint8_t* xq;               // [M, H] e4m3 (null: skip the quantisation)
   float* xs;                 // [M, H/128]
+  int32_t* done;             // with a permutation: CTAs finished (zero before the launch; the
+                             // last CTA resets it)
 };
 
 struct PermuteArgs {
@@ -124,8 +126,8 @@ cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int 
 // the same partial logits on the tensor cores (sb_gate.cu), for prefill batches
 cudaError_t launch_gate_tc(const void* x, const void* w, float* part, int m, int e, int h, int kspl, int* err,
                            cudaStream_t st);
-cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
-cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t st);
+// routing; with perm non-null also the permutation, run by the routing kernel's last CTA to finish
+cudaError_t launch_route(const RouteArgs& a, const PermuteArgs* perm, cudaStream_t st);
 cudaError_t launch_grouped(const GroupedArgs& a, int max_items, int grid_cap, cudaStream_t st);
 cudaError_t launch_combine(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h,
                            int has_shared, __nv_bfloat16* y, cudaStream_t st);

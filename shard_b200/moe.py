@@ -130,6 +130,7 @@ class MoELayer:
         d.no_renorm = 0 if renormalize else 1
         self.prefill = prefill     # 0 auto, 1 verify kernel, 2 prefill kernel
         self._ws = None
+        self._ws_need = {}
         self.score_func, self.route_scale, self.swiglu_limit, self.act_pow2 = score_func, route_scale, swiglu_limit, act_pow2
 
     @property
@@ -156,9 +157,12 @@ class MoELayer:
 
     def reserve(self, m: int):
         """Pre-size the workspace for up to m tokens (do this before capturing a CUDA graph)."""
-        need = self.workspace_bytes(m)
+        need = self._ws_need.get(m)
+        if need is None:
+            need = self._ws_need[m] = self.workspace_bytes(m)
         if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            # zeroed: the forward's flags and its routing completion counter start at zero
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
     def device_error(self) -> int:
