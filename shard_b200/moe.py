@@ -157,9 +157,10 @@ class MoELayer:
 
     def reserve(self, m: int):
         """Pre-size the workspace for up to m tokens (do this before capturing a CUDA graph)."""
-        need = self._ws_need.get(m)
+        key = (m, int(self.desc.prefill))
+        need = self._ws_need.get(key)
         if need is None:
-            need = self._ws_need[m] = self.workspace_bytes(m)
+            need = self._ws_need[key] = self.workspace_bytes(m)
         if self._ws is None or self._ws.numel() < need:
             # zeroed: the forward's flags and its routing completion counter start at zero
             self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
