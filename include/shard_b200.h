@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define SB_ABI_VERSION 5
+#define SB_ABI_VERSION 6
 
 enum sb_status {
   SB_OK = 0,
@@ -108,6 +108,13 @@ typedef struct sb_moe_layer {
    * prefill kernel's dequantised weights are exact for NVFP4, MXFP4 and for FP8 whose 128x128
    * block scales are powers of two; pick SB_PREFILL_VERIFY for FP8 banks with other scales. */
   int32_t prefill;
+  /* 1: every FP8 128x128 block scale of the layer (the shared expert's and, for FP8 experts, the
+   * routed bank's) is a power of two, as in ue8m0-scaled checkpoints (the reference stores them as
+   * float8_e8m0fnu, model.py:143-147). With power-of-two activation scales (act_pow2) the verify
+   * kernel then runs FP8 items on the block-scaled tensor-core MMA (ue8m0 scale factors, the whole K
+   * accumulated in tensor memory); MXFP4 items run it whenever act_pow2. 0: FP8 items keep the
+   * per-stage readback, which applies any fp32 scale. */
+  int32_t fp8_pow2;
 } sb_moe_layer;
 
 enum sb_prefill { SB_PREFILL_AUTO = 0, SB_PREFILL_VERIFY = 1, SB_PREFILL_WIDE = 2 };
@@ -161,10 +168,8 @@ int sb_qgemm_static_error(int* host_out, void* stream);
 
 /* ── the MoE stage forward (MoE.forward, model.py:634-649; Gate.forward :569-589;
  *    Expert.forward :601-611; grouped decode v4_moe_grouped.py:634-709) ──────────────────────── */
-/* Bytes of workspace for a forward of up to m tokens (the size serves every m' <= m). A new
- * workspace's first 16 bytes must be zero before its first forward (one cudaMemsetAsync after
- * allocating it): they hold the error flags and the routing kernel's completion counter, which every
- * forward leaves zero again. Forwards that share a workspace must not overlap on the GPU. */
+/* Bytes of workspace for a forward of up to m tokens (the size serves every m' <= m). Forwards that
+ * share a workspace must not overlap on the GPU. */
 size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m);
 /* x bf16 [M, H] -> y bf16 [M, H]. input_ids int64 [M] (read only for hash routing; may be NULL
  * otherwise). Optional outputs (NULL to skip): routing weights fp32 [M, k] and top-k indices

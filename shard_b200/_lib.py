@@ -15,7 +15,7 @@ SB_OK = 0
 STATUS = {0: "SB_OK", -1: "SB_ERR_ARG", -2: "SB_ERR_SHAPE", -3: "SB_ERR_FORMAT", -4: "SB_ERR_WORKSPACE",
           -5: "SB_ERR_CUDA", -6: "SB_ERR_UNSUPPORTED"}
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 SCORE = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 MAT_PLAIN, MAT_W13 = 0, 1
 KIND_TC = 4                      # OR'ed into a tiling kind: the tensor-core (tcgen05) layout
@@ -39,7 +39,7 @@ class SbMoeLayer(ctypes.Structure):
         ("w13", _vp), ("w13_s", _vp), ("w13_ts", _vp), ("w2", _vp), ("w2_s", _vp), ("w2_ts", _vp),
         ("sh_w13", _vp), ("sh_w13_s", _vp), ("sh_w2", _vp), ("sh_w2_s", _vp),
         ("layout", ctypes.c_int32), ("logits_bf16", ctypes.c_int32), ("no_renorm", ctypes.c_int32),
-        ("prefill", ctypes.c_int32),
+        ("prefill", ctypes.c_int32), ("fp8_pow2", ctypes.c_int32),
     ]
 
 

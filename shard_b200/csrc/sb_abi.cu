@@ -42,9 +42,7 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 // The forward's scratch regions, carved from one caller-provided workspace.
 struct Workspace {
   int32_t* err;      // offset 0: device error flag (set afresh by every forward; 1 = a bounded wait gave up);
-                     // offset 4: the tensor-core gate's flag (cleared before it runs), folded into it;
-                     // offset 8: routing CTAs finished (zero in a fresh workspace; every forward
-                     // leaves it zero)
+                     // offset 4: the tensor-core gate's flag (cleared before it runs), folded into it
   float* logits;
   int32_t* topk_idx;
   float* topk_w;
@@ -118,7 +116,7 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
     off += align256(bytes);
     return p;
   };
-  w.err = (int32_t*)take(4 * sizeof(int32_t));
+  w.err = (int32_t*)take(2 * sizeof(int32_t));
   // partial gate logits, one [M, E] slab per 512- (or 256-) wide K split
   w.logits = (float*)take(sizeof(float) * m * E * (H / (H % 512 == 0 ? 512 : 256)));
   w.topk_idx = (int32_t*)take(sizeof(int32_t) * P);
@@ -483,8 +481,7 @@ size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
 }
 
 static int route_impl(const sb_moe_layer* L, const void* x, int64_t m, const int64_t* ids, float* out_w,
-                      int64_t* out_idx, const Workspace& w, bool quant, const sb::PermuteArgs* perm,
-                      cudaStream_t st) {
+                      int64_t* out_idx, const Workspace& w, bool quant, cudaStream_t st) {
   // the prefill kernel's batches take the tensor-core gate (a token's logits then come from the
   // same kernel whether it runs alone or in its batch, under either kernel choice)
   if (use_wide(L, m)) {
@@ -519,8 +516,7 @@ static int route_impl(const sb_moe_layer* L, const void* x, int64_t m, const int
   r.x = (const __nv_bfloat16*)x;
   r.xq = quant ? w.xq : nullptr;
   r.xs = w.xs;
-  r.done = w.err + 2;
-  return cuda_check(sb::launch_route(r, perm, st), "route");
+  return cuda_check(sb::launch_route(r, st), "route");
 }
 
 int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, float* out_weights,
@@ -534,7 +530,7 @@ int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int6
   Workspace w = carve(layer, m, (uint8_t*)workspace);
   if (!workspace || workspace_bytes < w.bytes)
     return fail(SB_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, w.bytes);
-  return route_impl(layer, x, m, input_ids, out_weights, out_indices, w, false, nullptr, (cudaStream_t)stream);
+  return route_impl(layer, x, m, input_ids, out_weights, out_indices, w, false, (cudaStream_t)stream);
 }
 
 static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
@@ -559,6 +555,9 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   if (!workspace || workspace_bytes < w.bytes)
     return fail(SB_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, w.bytes);
   mark(0);
+  rc = route_impl(L, x, m, input_ids, out_weights, out_indices, w, true, st);
+  if (rc) return rc;
+  mark(1);
   sb::PermuteArgs p;
   p.topk_idx = w.topk_idx;
   p.m = (int)m;
@@ -576,10 +575,8 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.pass_off = L->layout == SB_LAYOUT_TC ? w.pass_off : nullptr;
   p.pass_slot = w.pass_slot;
   p.pass_pb = w.pass_pb;
-  // routing, with the permutation run by the routing kernel's last CTA
-  rc = route_impl(L, x, m, input_ids, out_weights, out_indices, w, true, &p, st);
+  rc = cuda_check(sb::launch_permute(p, st), "permute");
   if (rc) return rc;
-  mark(1);
   mark(2);
 
   const int64_t H = L->hidden, I = L->inter, P = m * L->topk;
@@ -600,6 +597,9 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   g.topk_w = w.topk_w;
   g.err = w.err;
   g.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+  // the verify kernel's block-scaled items: MXFP4 with power-of-two activation scales, FP8 when its
+  // block scales are powers of two as well
+  g.bs_mask = L->act_pow2 ? ((1 << SB_FMT_MXFP4) | (L->fp8_pow2 ? (1 << SB_FMT_FP8) : 0)) : 0;
   const int n_units = (int)(max_active + (L->has_shared ? 1 : 0));
   if (L->layout == SB_LAYOUT_TC && w.wide) {
     // prefill kernel: x (act-quantised, bf16) in expert order, w13 (+ SwiGLU -> h), h act-quantised

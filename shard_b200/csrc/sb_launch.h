@@ -24,8 +24,6 @@ struct RouteArgs {
   const __nv_bfloat16* x;    // [M, H]
   uint8_t* xq;               // [M, H] e4m3 (null: skip the quantisation)
   float* xs;                 // [M, H/128]
-  int32_t* done;             // with a permutation: CTAs finished (zero before the launch; the
-                             // last CTA resets it)
 };
 
 struct PermuteArgs {
@@ -84,6 +82,8 @@ struct GroupedArgs {
   __nv_bfloat16* hbf;  // tensor-core path: h in bf16 (W13 writes it, the W2 panel quantises it)
   int n_experts;       // tensor-core path: matrices in the routed bank
   uint32_t wait_limit; // tensor-core path: polls of the consumer-side waits (0: the kernel's default)
+  int bs_mask;         // verify kernel: bit f set = items of weight format f run block-scaled
+                       // (FMT_MXFP4, FMT_FP8; only with power-of-two activation and weight scales)
 };
 
 // Tensor-core path: the activation operand of every pass, prepared before the grouped launch.
@@ -120,14 +120,19 @@ struct PanelArgs {
 
 __host__ __device__ inline int tc_pass_max(int fmt) { return fmt == 1 ? 8 : 16; }
 
+// Byte offset of weight row r's four e8m0 scales within a tensor-core-layout MXFP4 scale stage
+// (128 rows x 4 per-32 scales): 16 (r % 32) + 4 (r / 32), the source order of the scale-factor copy
+// into tensor memory (sb_tc.cu).
+__host__ __device__ inline int mx_scale_off(int r) { return 16 * (r & 31) + 4 * (r >> 5); }
+
 // K-split width of the gate logits (both kernels): 512 when H allows it, else 256 (H % 256 == 0).
 __host__ __device__ inline int gate_ksplit(int h) { return h % 512 == 0 ? 512 : 256; }
 cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int m, int e, int h, cudaStream_t st);
 // the same partial logits on the tensor cores (sb_gate.cu), for prefill batches
 cudaError_t launch_gate_tc(const void* x, const void* w, float* part, int m, int e, int h, int kspl, int* err,
                            cudaStream_t st);
-// routing; with perm non-null also the permutation, run by the routing kernel's last CTA to finish
-cudaError_t launch_route(const RouteArgs& a, const PermuteArgs* perm, cudaStream_t st);
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
+cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t st);
 cudaError_t launch_grouped(const GroupedArgs& a, int max_items, int grid_cap, cudaStream_t st);
 cudaError_t launch_combine(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h,
                            int has_shared, __nv_bfloat16* y, cudaStream_t st);

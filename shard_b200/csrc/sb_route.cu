@@ -5,14 +5,11 @@
 //                        (model.py:571-589), hash routing through tid2eid (model.py:581-582), and
 //                        the per-128 e4m3 quantisation of x for the expert GEMVs (act_quant,
 //                        kernel.py:40-125)
-//   permute_block        (run by route_kernel's last CTA to finish) per-expert (token, slot) lists
-//                        in ascending expert id (tokens ascending within an expert up to 2048 pairs;
-//                        any order above, which no output sees); the list of active experts and the
-//                        pass tables; all on the device, so the forward never drains to the host
-//                        (the reference's bincount().tolist(), model.py:639, is the sync this
-//                        replaces)
-#include <string.h>
-
+//   permute_kernel       per-expert (token, slot) lists in ascending expert id (tokens ascending
+//                        within an expert up to 2048 pairs; any order above, which no output sees);
+//                        the list of active experts; all on the device, so the
+//                        forward never drains to the host (the reference's bincount().tolist(),
+//                        model.py:639, is the sync this replaces)
 #include "sb_device.cuh"
 #include "sb_launch.h"
 
@@ -158,7 +155,16 @@ __device__ __forceinline__ void quant_row(const RouteArgs& a, int t, int w, int 
 }
 
 template <int SPL>
-__device__ __forceinline__ void route_token(const RouteArgs& a, int t, int lane) {
+__global__ void __launch_bounds__(128) route_kernel(RouteArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  if (t >= a.m) return;
+  if (warp != 0) {
+    if (a.xq != nullptr) quant_row(a, t, warp - 1, 3, lane);
+    return;
+  }
   const int E = a.n_experts;
   const int nsplit = a.hidden / gate_ksplit(a.hidden);
   // logits: split 0 + split 1 + ... in ascending split order; the loads of 4 splits are issued
@@ -316,76 +322,40 @@ __device__ __forceinline__ void route_token(const RouteArgs& a, int t, int lane)
   }
 }
 
-__device__ void permute_block(const PermuteArgs& a, int* smem);
-
-// One CTA per token: warp 0 routes the token, warps 1-3 quantise its row of x. With `permute`, the
-// CTA that finishes last (a device-wide counter, fenced, so every CTA's top-k ids are visible to it)
-// then builds the permutation for the whole batch and resets the counter for the next forward.
-template <int SPL>
-__global__ void __launch_bounds__(128) route_kernel(RouteArgs a, PermuteArgs pa, int permute) {
-  extern __shared__ int smem[];
-  __shared__ int last;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x;
-  pdl_wait();
-  pdl_trigger();
-  if (warp != 0) {
-    if (a.xq != nullptr) quant_row(a, t, warp - 1, 3, lane);
-  } else {
-    route_token<SPL>(a, t, lane);
-  }
-  if (!permute) return;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(a.done, 1) == (int)gridDim.x - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  permute_block(pa, smem);
-  if (threadIdx.x == 0) *a.done = 0;
-}
-
 // Single CTA. counts -> exclusive offsets -> stable placement (pair p = t*K + j, ascending p
 // within each expert, i.e. ascending token) -> active expert list. Deterministic.
-// pairs whose expert ids are staged in shared memory (with 2 * 1024 ints of counters: <= 40 KB)
+// pairs whose expert ids are staged in shared memory (with 2 * 1024 ints of counters: < 48 KB)
 constexpr int PERMUTE_SMEM_PAIRS = 8192;
 
 // pairs up to which the placement is stable (tokens ascending within an expert, by one warp)
 constexpr int PERMUTE_STABLE_PAIRS = 2048;
 
-// Counting sort of the batch's (token, slot) pairs by expert, by one CTA of any size (a multiple of
-// 32 threads, up to 1024): thread i owns experts [i * per, (i + 1) * per), per = ceil(E / threads).
-// smem: cnt [E], cursor [E], then the pairs' expert ids when P <= PERMUTE_SMEM_PAIRS. The ids were
-// written by other CTAs of the same grid: they are read through L2 (ld.global.cg).
-__device__ void permute_block(const PermuteArgs& a, int* smem) {
-  int* cnt = smem;
-  int* cursor = smem + a.n_experts;
-  int* tk = smem + 2 * a.n_experts;
-  __shared__ int warp_tot[32], warp_ftot[32], warp_ptot[32];
+__global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
+  extern __shared__ int smem[];
+  int* cnt = smem;                       // [E]
+  int* cursor = smem + a.n_experts;      // [E]
+  int* tk = smem + 2 * a.n_experts;      // [P] copy of topk_idx when it fits (PERMUTE_SMEM_PAIRS)
+  __shared__ int warp_tot[32];
   const int E = a.n_experts, P = a.m * a.topk;
   const bool staged = P <= PERMUTE_SMEM_PAIRS;
-  const int nt = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
-  if (tid == 0 && a.err) *a.err = (a.gate_err != nullptr && __ldcg(a.gate_err) != 0) ? 1 : 0;
-  for (int e = tid; e < E; e += nt) cnt[e] = 0;
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0 && a.err) *a.err = (a.gate_err != nullptr && *a.gate_err != 0) ? 1 : 0;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int p = tid; p < P; p += nt) {
-    const int e = __ldcg(a.topk_idx + p);
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int e = a.topk_idx[p];
     if (staged) tk[p] = e;
     atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  // per-thread totals over its experts: pairs, active experts, passes
-  const int per = (E + nt - 1) / nt;
-  const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
-  int c = 0, f = 0, np = 0;
-  for (int e = e0; e < e1; ++e) {
-    const int ce = cnt[e];
-    c += ce;
-    f += ce > 0;
-    np += a.pass_max > 0 ? (ce + a.pass_max - 1) / a.pass_max : 0;
-  }
-  // exclusive scans of the three totals across the block
-  int incl = c, fincl = f, pincl = np;
+  // exclusive scan of cnt over E (E <= 1024 = blockDim), and of the active flags
+  const int e = threadIdx.x;
+  const int c = e < E ? cnt[e] : 0;
+  const int flag = c > 0 ? 1 : 0;
+  const int np = a.pass_max > 0 ? (c + a.pass_max - 1) / a.pass_max : 0;  // passes of expert e
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = c, fincl = flag, pincl = np;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int v = __shfl_up_sync(0xffffffffu, incl, o);
@@ -397,6 +367,7 @@ __device__ void permute_block(const PermuteArgs& a, int* smem) {
       pincl += pv;
     }
   }
+  __shared__ int warp_ftot[32], warp_ptot[32];
   if (lane == 31) {
     warp_tot[warp] = incl;
     warp_ftot[warp] = fincl;
@@ -404,8 +375,7 @@ __device__ void permute_block(const PermuteArgs& a, int* smem) {
   }
   __syncthreads();
   if (warp == 0) {
-    int v = lane < nw ? warp_tot[lane] : 0, fv = lane < nw ? warp_ftot[lane] : 0,
-        pv = lane < nw ? warp_ptot[lane] : 0;
+    int v = warp_tot[lane], fv = warp_ftot[lane], pv = warp_ptot[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int u = __shfl_up_sync(0xffffffffu, v, o);
@@ -417,40 +387,33 @@ __device__ void permute_block(const PermuteArgs& a, int* smem) {
         pv += pu;
       }
     }
-    if (lane < nw) {
-      warp_tot[lane] = v;
-      warp_ftot[lane] = fv;
-      warp_ptot[lane] = pv;
-    }
+    warp_tot[lane] = v;
+    warp_ftot[lane] = fv;
+    warp_ptot[lane] = pv;
   }
   __syncthreads();
-  int off = (warp > 0 ? warp_tot[warp - 1] : 0) + incl - c;
-  int slot = (warp > 0 ? warp_ftot[warp - 1] : 0) + fincl - f;
-  int pass = (warp > 0 ? warp_ptot[warp - 1] : 0) + pincl - np;
-  for (int e = e0; e < e1; ++e) {
-    const int ce = cnt[e];
+  const int base = warp > 0 ? warp_tot[warp - 1] : 0;
+  const int fbase = warp > 0 ? warp_ftot[warp - 1] : 0;
+  const int pbase = warp > 0 ? warp_ptot[warp - 1] : 0;
+  if (e < E) {
+    const int off = base + incl - c;
     a.offsets[e] = off;
-    a.counts[e] = ce;
+    a.counts[e] = c;
     cursor[e] = off;
-    off += ce;
-    if (ce > 0) {
-      a.active[slot] = e;
-      if (a.pass_off) {
-        const int npe = (ce + a.pass_max - 1) / a.pass_max;
-        a.pass_off[slot] = pass;
-        for (int i = 0; i < npe; ++i) {   // the pass table: every routed pass's slot and first token
-          a.pass_slot[pass + i] = slot;
-          a.pass_pb[pass + i] = i * a.pass_max;
-        }
-        pass += npe;
+    if (flag) a.active[fbase + fincl - 1] = e;
+    if (flag && a.pass_off) {
+      const int slot = fbase + fincl - 1, p0 = pbase + pincl - np;
+      a.pass_off[slot] = p0;
+      for (int i = 0; i < np; ++i) {   // the pass table: every routed pass's slot and first token
+        a.pass_slot[p0 + i] = slot;
+        a.pass_pb[p0 + i] = i * a.pass_max;
       }
-      ++slot;
     }
-  }
-  if (tid == 0) {   // the block totals
-    a.offsets[E] = warp_tot[nw - 1];
-    *a.n_active = warp_ftot[nw - 1];
-    if (a.pass_off) a.pass_off[warp_ftot[nw - 1]] = warp_ptot[nw - 1];
+    if (e == E - 1) {
+      a.offsets[E] = base + incl;
+      *a.n_active = fbase + fincl;
+      if (a.pass_off) a.pass_off[fbase + fincl] = pbase + pincl;
+    }
   }
   __syncthreads();
   if (P > PERMUTE_STABLE_PAIRS) {
@@ -458,8 +421,8 @@ __device__ void permute_block(const PermuteArgs& a, int* smem) {
     // pairs then varies between runs, but no output does: every grouped kernel computes each
     // token's rows independently of the other tokens of its pass (row invariance, asserted
     // bit-for-bit by the parity tests), and outputs are indexed by (token, slot), not by position.
-    for (int p = tid; p < P; p += nt) {
-      const int ex = staged ? tk[p] : __ldcg(a.topk_idx + p);
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+      const int ex = staged ? tk[p] : a.topk_idx[p];
       const int pos = atomicAdd(&cursor[ex], 1);
       a.pair_tok[pos] = p / a.topk;
       a.pair_slot[pos] = p % a.topk;
@@ -470,7 +433,7 @@ __device__ void permute_block(const PermuteArgs& a, int* smem) {
   if (warp == 0) {
     for (int p0 = 0; p0 < P; p0 += 32) {
       const int p = p0 + lane;
-      const int ex = p < P ? (staged ? tk[p] : __ldcg(a.topk_idx + p)) : -1 - lane;
+      const int ex = p < P ? (staged ? tk[p] : a.topk_idx[p]) : -1 - lane;
       const unsigned same = __match_any_sync(0xffffffffu, ex);
       const int rank = __popc(same & ((1u << lane) - 1u));
       const int leader = __ffs(same) - 1;
@@ -494,36 +457,21 @@ cudaError_t launch_gate_logits(const void* x, const void* w, float* logits, int 
                     logits, m, e, h);
 }
 
-template <int SPL>
-static cudaError_t launch_route_spl(const RouteArgs& a, const PermuteArgs& p, int permute, size_t smem,
-                                    cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(route_kernel<SPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  return launch_pdl(route_kernel<SPL>, dim3(a.m), dim3(128), smem, st, a, p, permute);
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
+  const int spl = (a.n_experts + 31) / 32;
+  const dim3 grid(a.m), block(128);
+  if (spl <= 1) return launch_pdl(route_kernel<1>, grid, block, 0, st, a);
+  if (spl <= 2) return launch_pdl(route_kernel<2>, grid, block, 0, st, a);
+  if (spl <= 4) return launch_pdl(route_kernel<4>, grid, block, 0, st, a);
+  if (spl <= 8) return launch_pdl(route_kernel<8>, grid, block, 0, st, a);
+  if (spl <= 16) return launch_pdl(route_kernel<16>, grid, block, 0, st, a);
+  return launch_pdl(route_kernel<32>, grid, block, 0, st, a);
 }
 
-cudaError_t launch_route(const RouteArgs& a, const PermuteArgs* perm, cudaStream_t st) {
-  const int spl = (a.n_experts + 31) / 32;
-  PermuteArgs p;
-  memset(&p, 0, sizeof p);
-  size_t smem = 0;
-  if (perm) {
-    p = *perm;
-    const int P = p.m * p.topk;
-    smem = (size_t)(2 * p.n_experts + (P <= PERMUTE_SMEM_PAIRS ? P : 0)) * sizeof(int);
-  }
-  const int permute = perm != nullptr;
-  if (spl <= 1) return launch_route_spl<1>(a, p, permute, smem, st);
-  if (spl <= 2) return launch_route_spl<2>(a, p, permute, smem, st);
-  if (spl <= 4) return launch_route_spl<4>(a, p, permute, smem, st);
-  if (spl <= 8) return launch_route_spl<8>(a, p, permute, smem, st);
-  if (spl <= 16) return launch_route_spl<16>(a, p, permute, smem, st);
-  return launch_route_spl<32>(a, p, permute, smem, st);
+cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t st) {
+  const int P = a.m * a.topk;
+  const size_t smem = (size_t)(2 * a.n_experts + (P <= PERMUTE_SMEM_PAIRS ? P : 0)) * sizeof(int);
+  return launch_pdl(permute_kernel, dim3(1), dim3(1024), smem, st, a);
 }
 
 }  // namespace sb

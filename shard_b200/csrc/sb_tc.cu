@@ -51,18 +51,25 @@ constexpr int B_BYTES = NB * 128;
 constexpr int SCL_BYTES = 1024;
 constexpr uint32_t WAIT_LIMIT = 1u << 16;  // polls; each may sleep up to ~1 us
 
+constexpr int SF_SRC = 512;      // one scale-factor copy source: 32 rows x 16 B
+constexpr int SF_A_COL = 64;     // block-scaled items: TMEM columns of the group holding the weight
+constexpr int SF_B_COL = 68;     // and activation scale factors (the accumulator is columns 0-15)
+
 struct Smem {
   uint8_t A[ST][A_BYTES];       // 1024-aligned (128B swizzle atoms)
   uint8_t B[ST][B_BYTES];
+  uint8_t sfa[ST][SF_SRC];      // block-scaled FP8 items: the stage's weight scale factors
+  uint8_t sfb[ST][SF_SRC];      // block-scaled items: the stage's activation scale factors
   uint8_t scl[SS][UNIT * SCL_BYTES];
   float asc[SS][UNIT * NB];
   uint64_t full[ST], aempty[ST], sfull[SS], sempty[SS], gfull[SA], gempty[SA];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float xchg[64][17];
+  __nv_bfloat16 xchg[64][18];   // W13 epilogue: the up rows' bf16 values
 };
 constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
+static_assert(2 * (SMEM_BYTES + 1024) <= 233472, "two CTAs per SM (1 KB reserved per CTA)");
 
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   uint64_t d = 0;
@@ -85,6 +92,38 @@ __device__ __forceinline__ void mma(uint32_t tmem, uint64_t ad, uint64_t bd, uin
       " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
       "l"(ad), "l"(bd), "r"(id), "r"(acc));
 }
+
+// Block-scaled MMA (kind::mxf8f6f4.block_scale, one ue8m0 scale per 32 K for A and for B): the
+// instruction descriptor names the A format (0 e4m3, 5 e2m1), B e4m3, M=128, N=NB, E8M0 scale
+// factors, and which byte (32-K block kb of the stage) of the scale-factor words both operands use.
+__device__ __forceinline__ uint32_t idesc_bs(uint32_t afmt, uint32_t kb) {
+  return (kb << 4) | (afmt << 7) | (0u << 10) | ((uint32_t)(NB >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+         (kb << 29);
+}
+
+// sfa / sfb: TMEM addresses of the scale factors, the byte within their 32-bit columns in bits 30-31
+__device__ __forceinline__ void mma_bs(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t id, uint32_t sfa, uint32_t sfb,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(tmem),
+      "l"(ad), "l"(bd), "r"(id), "r"(acc), "r"(sfa), "r"(sfb));
+}
+
+// Scale factors of 128 rows into TMEM: a 32-row x 16-byte shared-memory source (row i = the four
+// scale words of rows i, 32 + i, 64 + i, 96 + i) lands in lane i of every 32-lane sub-partition,
+// columns taddr .. taddr + 3 (column c = rows 32c + i, byte b = 32-K block b).
+__device__ __forceinline__ void cp_sf(uint32_t taddr, uint32_t src) {
+  uint64_t d = 0;
+  d |= (uint64_t)((src >> 4) & 0x3FFFu);
+  d |= (uint64_t)(128 >> 4) << 16;       // leading byte offset (one core matrix along K: unused)
+  d |= (uint64_t)(128 >> 4) << 32;       // stride byte offset: 8 rows x 16 B core matrices
+  d |= (uint64_t)1 << 46;                // descriptor version (sm100); no swizzle
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n" ::"r"(taddr), "l"(d) : "memory");
+}
+
+// a power-of-two fp32 scale as its e8m0 byte (0 -> 2^-127, only for empty activation rows)
+__device__ __forceinline__ uint32_t e8m0_of(float v) { return (__float_as_uint(v) >> 23) & 0xFFu; }
 
 __device__ __forceinline__ void commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
@@ -132,14 +171,21 @@ __device__ __forceinline__ void set_abort(Smem& sm, int* err, bool flag_err) {
   *reinterpret_cast<volatile int*>(&sm.abort) = 1;
 }
 
-// bounded wait; on timeout flag the CTA (and the launch) and return false. `limit` polls: 256
-// without a suspend hint first (most waits end within a few hundred cycles), then `limit` polls
-// that may each sleep up to ~1 us. A limit below 256 (the timeout-path test) makes `limit`
-// non-blocking probes instead, so a phase not complete at that moment runs the wait out.
+// bounded wait; on timeout flag the CTA (and the launch) and return false. `limit` polls: up to 256
+// without a suspend hint first (most waits end within a few hundred cycles), then `limit` polls that
+// may each sleep up to ~1 us. PROBE (the kernel variant of the timeout-path test, launched only when
+// a test wait limit is set) makes `limit` non-blocking probes instead, so a phase not complete at
+// that moment runs the wait out; the production variant compiles only the polling loops.
+template <bool PROBE = false>
 __device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t parity, uint32_t limit = WAIT_LIMIT) {
-  for (uint32_t i = 0; limit < 256u && i < limit; ++i)
-    if (mbar_test_wait(bar, parity)) return true;
-  for (uint32_t i = 0; limit >= 256u && i < 256u; ++i)
+  if constexpr (PROBE) {
+#pragma unroll 1
+    for (uint32_t i = 0; i < limit; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+    set_abort(sm, err, true);
+    return false;
+  }
+  for (uint32_t i = 0; i < 256u && i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   for (uint32_t i = 0; limit >= 256u && i < limit; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
@@ -150,9 +196,10 @@ __device__ __forceinline__ bool wait(Smem& sm, int* err, uint32_t bar, uint32_t 
 }
 
 // bounded wait by a whole warp; true only if every lane saw the phase complete (reconverges the warp)
+template <bool PROBE = false>
 __device__ __forceinline__ bool warp_wait(Smem& sm, int* err, uint32_t bar, uint32_t parity,
                                           uint32_t limit = WAIT_LIMIT) {
-  const bool ok = wait(sm, err, bar, parity, limit);
+  const bool ok = wait<PROBE>(sm, err, bar, parity, limit);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -218,7 +265,7 @@ struct TcArgs {
   TcPlan plan;
 };
 
-template <int FMT_R>
+template <int FMT_R, bool PROBE>
 __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_constant__ TcArgs ta) {
   const GroupedArgs& a = ta.g;
   extern __shared__ uint8_t dyn_raw[];
@@ -270,6 +317,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
 
   // per-item constants shared by the roles
   auto item_fmt = [&](const Item& it) { return it.shared ? (a.mode == MODE_DENSE ? FMT_R : FMT_FP8) : FMT_R; };
+  // items whose weights and activations both carry power-of-two scales run block-scaled
+  auto block_scaled = [&](int fmt) { return ((a.bs_mask >> fmt) & 1) != 0; };
 
   // Stages are grouped in UNITS of up to UNIT consecutive stages of one pass: one side-ring slot
   // (scales), one accumulator group and one readback per unit. g counts stages, u units.
@@ -341,26 +390,95 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
       for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
         if (mbar_try_wait(smem_addr(&sm.sfull[h % SS]), (h / SS) & 1u)) break;
   } else if (warp == MMA_WARP) {
-    // the whole warp runs the loop (uniform control flow); one elected lane issues MMAs and commits
-    uint32_t g = 0, u = 0;
+    // the whole warp runs the loop (uniform control flow); one elected lane issues MMAs and commits.
+    // g counts stages, u units, gq accumulator groups (one per unit, or one per block-scaled item)
+    uint32_t g = 0, u = 0, gq = 0;
     bool ok = true;
     Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item it = nxt;
       if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb);
       const int fmt = item_fmt(it);
-      const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
-      {
+      if (block_scaled(fmt)) {
+        // the whole K into one 16-column accumulator; per stage the weight and activation scale
+        // factors are copied into the group's scale-factor columns ahead of the stage's 4 MMAs (the
+        // copies and MMAs of this thread execute in issue order)
+        const uint32_t q = gq % SA;
+        if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.gempty[q]), ((gq / SA) & 1u) ^ 1u, clim)) {
+          ok = false;
+          break;
+        }
+        const uint32_t cacc = tbase + q * GCOLS, csfa = cacc + SF_A_COL, csfb = cacc + SF_B_COL;
+        const uint32_t afmt = fmt == FMT_FP8 ? 0u : 5u;
         for (int j = 0; j < nst && ok; j += UNIT, ++u) {
           const int ns = min(UNIT, nst - j);
-          const uint32_t q = u % SA;
-          if (!warp_wait(sm, err, smem_addr(&sm.gempty[q]), ((u / SA) & 1u) ^ 1u, clim)) {
+          const uint32_t us = u % SS;
+          if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u, clim)) {
             ok = false;
             break;
           }
           for (int t = 0; t < ns; ++t, ++g) {
             const uint32_t s = g % ST;
-            if (!warp_wait(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u, clim)) {
+            if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u, clim)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            // scale-factor sources: FP8 weights' two 128x128 block scales (rows 0-63, 64-127) spread
+            // over the 128 rows; MXFP4 weights' scales are already in copy order in the side slot;
+            // the pass's 16 activation scales (one per 128 K, the same for the stage's 4 blocks)
+            uint32_t sfa_src;
+            if (fmt == FMT_FP8) {
+              const float* rec = reinterpret_cast<const float*>(sm.scl[us] + t * 16);
+              const uint32_t lo = e8m0_of(rec[0]) * 0x01010101u, hi = e8m0_of(rec[1]) * 0x01010101u;
+              *reinterpret_cast<uint4*>(sm.sfa[s] + lane * 16) = make_uint4(lo, lo, hi, hi);
+              sfa_src = smem_addr(sm.sfa[s]);
+            } else {
+              sfa_src = smem_addr(sm.scl[us] + t * 512);
+            }
+            if (lane < NB) {
+              const uint32_t e = e8m0_of(sm.asc[us][t * NB + lane]) * 0x01010101u;
+              *reinterpret_cast<uint4*>(sm.sfb[s] + lane * 16) = make_uint4(e, e, e, e);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            const uint32_t abase = smem_addr(sm.A[s]), bbase = smem_addr(sm.B[s]);
+            if (elect_one()) {
+              cp_sf(csfa, sfa_src);
+              cp_sf(csfb, smem_addr(sm.sfb[s]));
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                mma_bs(cacc, sdesc(abase + c * 32), sdesc(bbase + c * 32), idesc_bs(afmt, (uint32_t)c),
+                       csfa | ((uint32_t)c << 30), csfb | ((uint32_t)c << 30), (j + t > 0 || c > 0) ? 1u : 0u);
+              commit(smem_addr(&sm.aempty[s]));   // operand slot and its scale-factor sources
+            }
+            __syncwarp();
+          }
+          if (!ok) break;
+          // the side slot is free once the copies that read it have completed (4 arrivals expected)
+          if (elect_one())
+#pragma unroll
+            for (int i = 0; i < 4; ++i) commit(smem_addr(&sm.sempty[us]));
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (elect_one()) commit(smem_addr(&sm.gfull[q]));
+        __syncwarp();
+        ++gq;
+        continue;
+      }
+      const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
+      {
+        for (int j = 0; j < nst && ok; j += UNIT, ++u, ++gq) {
+          const int ns = min(UNIT, nst - j);
+          const uint32_t q = gq % SA;
+          if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.gempty[q]), ((gq / SA) & 1u) ^ 1u, clim)) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < ns; ++t, ++g) {
+            const uint32_t s = g % ST;
+            if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.full[s]), (g / ST) & 1u, clim)) {
               ok = false;
               break;
             }
@@ -395,7 +513,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   } else {
     // ── readback + epilogue (warps 0-3) ──
     const int r = tid;  // weight row of the item = TMEM lane
-    uint32_t u = 0;
+    uint32_t u = 0, gq = 0;
     bool ok = true;
     Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -438,11 +556,29 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         float acc[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) acc[t] = 0.f;
-        for (int j = 0; j < nst; j += UNIT, ++u) {
+        if (block_scaled(fmt)) {
+          // one readback of the fully scaled accumulator per pass; the side slots went to the MMA warp
+          const uint32_t q = gq % SA;
+          u += (uint32_t)((nst + UNIT - 1) / UNIT);
+          if (ok) ok = warp_wait<PROBE>(sm, err, smem_addr(&sm.gfull[q]), (gq / SA) & 1u, clim);
+          if (ok) {
+            fence_after();
+            uint32_t d[16];
+            ld16(tbase + ((uint32_t)(warp * 32) << 16) + q * GCOLS, d);
+            ld_wait();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) arrive(smem_addr(&sm.gempty[q]));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = __uint_as_float(d[i]);
+          }
+          ++gq;
+        } else
+        for (int j = 0; j < nst; j += UNIT, ++u, ++gq) {
           const int ns = min(UNIT, nst - j);
-          const uint32_t us = u % SS, q = u % SA;
+          const uint32_t us = u % SS, q = gq % SA;
           // this unit's scales first (they landed long ago), so their loads overlap the MMA wait
-          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u, clim);
+          if (ok) ok = warp_wait<PROBE>(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u, clim);
           if (!ok) continue;
           float sc[UNIT][8];
 #pragma unroll
@@ -465,14 +601,14 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
               sc[t][0] = f01.x; sc[t][1] = f01.y; sc[t][2] = f23.x; sc[t][3] = f23.y;
               sc[t][4] = f45.x; sc[t][5] = f45.y; sc[t][6] = f67.x; sc[t][7] = f67.y;
             } else {
-              const uint32_t sv = t < ns ? *reinterpret_cast<const uint32_t*>(sp + r * 4) : 0u;
+              const uint32_t sv = t < ns ? *reinterpret_cast<const uint32_t*>(sp + mx_scale_off(r)) : 0u;
 #pragma unroll
               for (int c = 0; c < 4; ++c) sc[t][c] = e8m0_to_f32(sv >> (8 * c));
 #pragma unroll
               for (int c = 4; c < 8; ++c) sc[t][c] = 0.f;
             }
           }
-          if (ok) ok = warp_wait(sm, err, smem_addr(&sm.gfull[q]), (u / SA) & 1u, clim);
+          if (ok) ok = warp_wait<PROBE>(sm, err, smem_addr(&sm.gfull[q]), (gq / SA) & 1u, clim);
           if (!ok) continue;
           fence_after();
           const uint32_t taddr = tbase + ((uint32_t)(warp * 32) << 16) + q * GCOLS;
@@ -596,7 +732,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
             const int I = a.n_rows / 2;
             if (r >= 64) {
 #pragma unroll
-              for (int t = 0; t < 16; ++t) sm.xchg[r - 64][t] = bf16_round(acc[t] * ts);
+              for (int t = 0; t < 16; ++t) sm.xchg[r - 64][t] = __float2bfloat16_rn(acc[t] * ts);
             }
             asm volatile("bar.sync 1, 128;\n" ::: "memory");
             if (r < 64) {
@@ -607,7 +743,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
                   const int orow = __shfl_sync(0xffffffffu, my_orow, t);
                   const float wgt = __shfl_sync(0xffffffffu, my_wgt, t);
                   float gv = bf16_round(acc[t] * ts);
-                  float uv = sm.xchg[r][t];
+                  float uv = __bfloat162float(sm.xchg[r][t]);
                   if (lim > 0.f) {
                     uv = fminf(fmaxf(uv, -lim), lim);
                     gv = fminf(gv, lim);
@@ -800,15 +936,22 @@ static cudaError_t make_map(CUtensorMap* map, const void* base, int fmt, uint64_
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int F>
-static cudaError_t launch_tc_one(const TcArgs& a, int grid, cudaStream_t st) {
+template <int F, bool PROBE>
+static cudaError_t launch_tc_variant(const TcArgs& a, int grid, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e =
+        cudaFuncSetAttribute(tc_grouped_kernel<F, PROBE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  return launch_pdl(tc_grouped_kernel<F>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
+  return launch_pdl(tc_grouped_kernel<F, PROBE>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
+}
+
+// the probing variant only when a test wait limit is set
+template <int F>
+static cudaError_t launch_tc_one(const TcArgs& a, int grid, cudaStream_t st) {
+  return a.g.wait_limit ? launch_tc_variant<F, true>(a, grid, st) : launch_tc_variant<F, false>(a, grid, st);
 }
 
 }  // namespace tc
@@ -844,7 +987,9 @@ cudaError_t launch_tc_grouped(const GroupedArgs& g, const TcPlan& plan, int max_
 // fp4 values   [128 rows][64 B]                  (128 K packed, low nibble first)
 // FP8 values   [128 rows][128 B]
 // NVFP4 scales [128 rows][8 B]                   (the row's 8 group scales of the stage)
-// MXFP4 scales [128 rows][4 B]
+// MXFP4 scales [32][4 rows][4 B]: row r's four per-32 scales at 16 (r % 32) + 4 (r / 32), the order in
+//              which tcgen05.cp .32x128b.warpx4 lands them as the block-scaled MMA's scale factors
+//              (TMEM lane r % 32 of every sub-partition, column r / 32, byte = 32-K block)
 // FP8 scales   [4] fp32: block scale of rows 0-63, of rows 64-127, 2 zero pads (16-byte copies)
 // W13 row-blocks hold 64 w1 rows then the same 64 w3 rows (rb covers intermediate 64*rb..+63).
 __device__ __forceinline__ int64_t tc_row(int kind, int64_t n, int64_t rb, int r) {
@@ -896,7 +1041,7 @@ __global__ void tc_tile_scales_kernel(const uint8_t* __restrict__ src, uint8_t* 
       const int r = (int)(u & 127);
       const int64_t j = (u >> 7) % nst, rb = ((u >> 7) / nst) % nrb, mat = ((u >> 7) / nst) / nrb;
       const uint8_t* s = src + (mat * n + tc_row(kind, n, rb, r)) * rowb + j * per;
-      uint8_t* d = dst + u * per;
+      uint8_t* d = dst + (u - r) * per + (fmt == FMT_MXFP4 ? mx_scale_off(r) : r * per);
       for (int i = 0; i < per; ++i) d[i] = s[i];
     }
   }

@@ -135,15 +135,22 @@ __device__ __forceinline__ void bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
-// Bounded mbarrier wait of a CTA with an abort flag in shared memory: 256 polls without a suspend
-// hint first, then `limit` polls with one; on timeout it sets *err and the abort flag and returns
-// false. It returns false early once another role has set the abort flag. A limit below 256 (the
-// timeout-path test) makes `limit` non-blocking probes instead.
+// Bounded mbarrier wait of a CTA with an abort flag in shared memory: up to 256 polls without a
+// suspend hint first, then (for limits of 256 and more) `limit` polls with one; on timeout it sets
+// *err and the abort flag and returns false. It returns false early once another role has set the
+// abort flag. PROBE (the kernel variant of the timeout-path test) makes `limit` non-blocking probes.
+template <bool PROBE = false>
 __device__ __forceinline__ bool wait_bounded(volatile int* abort_flag, int* err, uint32_t bar, uint32_t parity,
                                              uint32_t limit) {
-  for (uint32_t i = 0; limit < 256u && i < limit; ++i)
-    if (mbar_test_wait(bar, parity)) return true;
-  for (uint32_t i = 0; limit >= 256u && i < 256u; ++i)
+  if constexpr (PROBE) {
+#pragma unroll 1
+    for (uint32_t i = 0; i < limit; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+    atomicExch(err, 1);
+    *abort_flag = 1;
+    return false;
+  }
+  for (uint32_t i = 0; i < 256u && i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   for (uint32_t i = 0; limit >= 256u && i < limit; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;

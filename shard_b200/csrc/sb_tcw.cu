@@ -182,7 +182,7 @@ __device__ __forceinline__ void convert_nvfp4(const uint8_t* stg, int r, int hh,
 __device__ __forceinline__ void convert_mxfp4(const uint8_t* stg, int r, int hh, uint32_t (&o)[32]) {
 #pragma unroll
   for (int cc = 0; cc < 2; ++cc) {
-    const uint32_t eb = stg[STG_W + r * 4 + hh * 2 + cc];
+    const uint32_t eb = stg[STG_W + mx_scale_off(r) + hh * 2 + cc];
     const uint32_t sbits = eb ? (eb << 7) : 0x0040u;          // 2^(eb-127) as bf16
     const uint32_t s2 = sbits | (sbits << 16);
     const uint4 v = stg_chunk4(stg, r, 2 * hh + cc);
@@ -646,7 +646,7 @@ struct Smem {
 constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory of one CTA per SM");
 
-template <int FMT_R>
+template <int FMT_R, bool PROBE>
 __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant__ WideArgs wa) {
   const GroupedArgs& a = wa.g;
   extern __shared__ uint8_t dyn_raw[];
@@ -707,7 +707,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
   // the epilogue's on the accumulator) take the launch's limit; waits for free slots and the final
   // drains keep WAIT_LIMIT
   const uint32_t clim = a.wait_limit ? a.wait_limit : WAIT_LIMIT;
-  auto cwait = [&](uint32_t bar, uint32_t parity) { return wait_bounded(abort_flag, err, bar, parity, clim); };
+  auto cwait = [&](uint32_t bar, uint32_t parity) { return wait_bounded<PROBE>(abort_flag, err, bar, parity, clim); };
 
   if (warp == PRODUCER_WARP) {
     // both row blocks' weight stages (TMA) and their scales (bulk copies) into one staging slot
@@ -1198,17 +1198,25 @@ static cudaError_t encode(CUtensorMap* map, CUtensorMapDataType dt, const void* 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int F>
-static cudaError_t launch_one(const WideArgs& a, int grid, cudaStream_t st) {
+template <int F, bool PROBE>
+static cudaError_t launch_variant(const WideArgs& a, int grid, cudaStream_t st) {
   static bool configured = false;
-#if SB_WIDE_SWAP
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(x::tcx_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, x::SMEM_BYTES);
+    cudaError_t e =
+        cudaFuncSetAttribute(x::tcx_kernel<F, PROBE>, cudaFuncAttributeMaxDynamicSharedMemorySize, x::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  return launch_pdl(x::tcx_kernel<F>, dim3(grid), dim3(x::NTHREADS), x::SMEM_BYTES, st, a);
+  return launch_pdl(x::tcx_kernel<F, PROBE>, dim3(grid), dim3(x::NTHREADS), x::SMEM_BYTES, st, a);
+}
+
+template <int F>
+static cudaError_t launch_one(const WideArgs& a, int grid, cudaStream_t st) {
+#if SB_WIDE_SWAP
+  // the probing variant only when a test wait limit is set
+  return a.g.wait_limit ? launch_variant<F, true>(a, grid, st) : launch_variant<F, false>(a, grid, st);
 #else
+  static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(tcw_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;

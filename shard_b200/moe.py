@@ -128,6 +128,7 @@ class MoELayer:
         d.layout = self.layout
         d.logits_bf16 = 1 if logits_bf16 else 0
         d.no_renorm = 0 if renormalize else 1
+        d.fp8_pow2 = 1 if self.prefill_exact else 0
         self.prefill = prefill     # 0 auto, 1 verify kernel, 2 prefill kernel
         self._ws = None
         self._ws_need = {}
