@@ -115,7 +115,24 @@ typedef struct sb_moe_layer {
    * accumulated in tensor memory); MXFP4 items run it whenever act_pow2. 0: FP8 items keep the
    * per-stage readback, which applies any fp32 scale. */
   int32_t fp8_pow2;
+  /* Which MoE call site the layer serves (enum sb_moe_mode):
+   * SB_MODE_V4  MoE.forward of DeepSeek-V4 (model.py:634-649): the gate routes, activations are
+   *             act_quant'ed to e4m3 per 128, SwiGLU, the routing weight scales h before w2, the
+   *             combine sums in ascending expert id with the shared expert last.
+   * SB_MODE_K3  KimiSparseMoeBlock.moe_infer of Kimi-K3 (vendor/kimi_k3_ref/modeling_kimi_linear.py:
+   *             850-876, the seam engines/kimi_k3/k3_moe_mxfp4.py:405-412 replaces): the caller routes
+   *             (sb_moe_forward_routed), activations stay bf16 (4-bit weights, 16-bit activations),
+   *             the activation is situ (below), each expert's bf16 output is scaled by its routing
+   *             weight in fp32 and the slots are summed in slot order. MXFP4 experts, no shared
+   *             expert, tensor-core layout; the prefill kernel runs every batch size. */
+  int32_t mode;
+  /* SB_MODE_K3's SituAndMul (modeling_kimi_linear.py:64-82): (beta tanh(g / beta)) sigmoid(g) times
+   * up, up replaced by linear_beta tanh(up / linear_beta) when linear_beta > 0. */
+  float situ_beta;
+  float situ_linear_beta;
 } sb_moe_layer;
+
+enum sb_moe_mode { SB_MODE_V4 = 0, SB_MODE_K3 = 1 };
 
 enum sb_prefill { SB_PREFILL_AUTO = 0, SB_PREFILL_VERIFY = 1, SB_PREFILL_WIDE = 2 };
 
@@ -177,6 +194,13 @@ size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m);
 int sb_moe_forward(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,
                    void* y, float* out_weights, int64_t* out_indices, void* workspace,
                    size_t workspace_bytes, void* stream);
+
+/* The forward with the caller's routing, for SB_MODE_K3 layers (KimiSparseMoeBlock.moe_infer(x,
+ * topk_ids, topk_weight), modeling_kimi_linear.py:850-876): x bf16 [M, H], topk_idx int64 [M, k]
+ * (distinct ids per token, as topk returns them), topk_w fp32 [M, k] -> y bf16 [M, H]. An id outside
+ * [0, E) is replaced by 0 and sets the workspace error flag. gate_w may be NULL for such layers. */
+int sb_moe_forward_routed(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* topk_idx,
+                          const float* topk_w, void* y, void* workspace, size_t workspace_bytes, void* stream);
 
 /* sb_moe_forward that also records up to six CUDA events (cudaEvent_t, NULL entries skipped) on
  * the stream: before routing, after routing, after the permutation, after the grouped w13 pass,

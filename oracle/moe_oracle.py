@@ -13,6 +13,9 @@ What it restates, and from where (paths are relative to the leyten/shard tree):
   Expert.forward    model.py:601-611
   MoE.forward       model.py:634-649 (fp32 accumulator, ascending expert id, shared expert last)
   linear dispatch   model.py:114-126
+  K3 moe_infer      vendor/kimi_k3_ref/modeling_kimi_linear.py:64-82 (situ), :242-270 (expert),
+                    :850-876 (moe_infer), with MXFP4 experts in bf16 (the engine's W4A16 seam,
+                    engines/kimi_k3/k3_moe_mxfp4.py:405-412)
 NVFP4 (no in-tree reference): the weight dequant is e2m1[nibble] * e4m3(scale per 16) * fp32 tensor
 scale, left to right; everything around it is the reference's order of operations.
 
@@ -351,3 +354,49 @@ def max_rel_err(got: np.ndarray, ref: np.ndarray) -> float:
     d = np.abs(got.astype(np.float64) - ref.astype(np.float64)).max()
     r = np.abs(ref.astype(np.float64)).max()
     return float(d / r) if r > 0 else float(d)
+
+
+# ── Kimi-K3's routed experts (KimiSparseMoeBlock.moe_infer) ─────────────────────────────────────
+
+def situ(g: np.ndarray, u: np.ndarray, beta: float, linear_beta) -> np.ndarray:
+    """SituAndMul (vendor/kimi_k3_ref/modeling_kimi_linear.py:64-82) on fp32 gate / up values:
+    beta * tanh(gate / beta) * sigmoid(gate) * up, up -> linear_beta * tanh(up / linear_beta) when
+    linear_beta is set."""
+    b = np.float32(beta)
+    a = (b * np.tanh((g / b).astype(np.float32)).astype(np.float32)).astype(np.float32)
+    a = (a * _sigmoid(g)).astype(np.float32)
+    if linear_beta:
+        lb = np.float32(linear_beta)
+        u = (lb * np.tanh((u / lb).astype(np.float32))).astype(np.float32)
+    return (a * u).astype(np.float32)
+
+
+def bf16_linear(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """nn.Linear on bf16 tensors: the products of bf16 values summed in fp32, the result in bf16."""
+    return bf16_round((x.astype(np.float32) @ w.astype(np.float32).T).astype(np.float32))
+
+
+def k3_moe_infer(x: np.ndarray, topk_ids: np.ndarray, topk_weight: np.ndarray, expert, beta: float,
+                 linear_beta=None) -> np.ndarray:
+    """KimiSparseMoeBlock.moe_infer (modeling_kimi_linear.py:850-876) for x [T, D] (bf16 values as
+    fp32), distinct topk_ids [T, k] per token, topk_weight [T, k] fp32, with MXFP4 experts:
+    expert(e) = (w13 packed [2I, D/2], w13 e8m0 [2I, D/32], w2 packed [D, I/2], w2 e8m0 [D, I/32]),
+    w1 rows then w3 rows. Each expert (KimiBlockSparseMLP.forward, :262-270): w1 and w3 in bf16,
+    situ in fp32 -> bf16, w2 in bf16; then, per token, the fp32 sum over its slots of the bf16
+    expert output times the slot's weight, rounded to bf16."""
+    t, k = topk_ids.shape
+    out = np.zeros((t, k, x.shape[1]), dtype=np.float32)
+    for e in sorted(set(topk_ids.ravel().tolist())):
+        rows, slots = np.nonzero(topk_ids == e)
+        w13, w13_s, w2, w2_s = expert(e)
+        inter = w13.shape[0] // 2
+        w1 = dequant_weight(FMT_MXFP4, w13[:inter], w13_s[:inter])
+        w3 = dequant_weight(FMT_MXFP4, w13[inter:], w13_s[inter:])
+        g = bf16_linear(x[rows], w1)
+        u = bf16_linear(x[rows], w3)
+        h = bf16_round(situ(g, u, beta, linear_beta))
+        out[rows, slots] = bf16_linear(h, dequant_weight(FMT_MXFP4, w2, w2_s))
+    acc = np.zeros((t, x.shape[1]), dtype=np.float32)
+    for j in range(k):                      # the slots in order
+        acc = (acc + out[:, j] * topk_weight[:, j:j + 1].astype(np.float32)).astype(np.float32)
+    return bf16_round(acc)

@@ -20,6 +20,7 @@ SCORE = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 MAT_PLAIN, MAT_W13 = 0, 1
 KIND_TC = 4                      # OR'ed into a tiling kind: the tensor-core (tcgen05) layout
 LAYOUT_FRAGMENT, LAYOUT_TC = 0, 1
+MODE_V4, MODE_K3 = 0, 1
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -39,7 +40,8 @@ class SbMoeLayer(ctypes.Structure):
         ("w13", _vp), ("w13_s", _vp), ("w13_ts", _vp), ("w2", _vp), ("w2_s", _vp), ("w2_ts", _vp),
         ("sh_w13", _vp), ("sh_w13_s", _vp), ("sh_w2", _vp), ("sh_w2_s", _vp),
         ("layout", ctypes.c_int32), ("logits_bf16", ctypes.c_int32), ("no_renorm", ctypes.c_int32),
-        ("prefill", ctypes.c_int32), ("fp8_pow2", ctypes.c_int32),
+        ("prefill", ctypes.c_int32), ("fp8_pow2", ctypes.c_int32), ("mode", ctypes.c_int32),
+        ("situ_beta", ctypes.c_float), ("situ_linear_beta", ctypes.c_float),
     ]
 
 
@@ -60,6 +62,7 @@ SIGNATURES = {
     "sb_moe_forward": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sb_moe_forward_profiled": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp,
                                         ctypes.POINTER(_vp)]),
+    "sb_moe_forward_routed": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sb_moe_route": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sb_moe_forward_wire": (_int, [ctypes.POINTER(SbMoeLayer), _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                    _vp]),

@@ -78,6 +78,7 @@ struct Workspace {
 // average: below that the verify kernel's narrow passes cost less (measured on B200 at c1 / c4 shapes).
 constexpr int64_t WIDE_TOKENS_PER_EXPERT = 16;
 bool use_wide(const sb_moe_layer* L, int64_t m) {
+  if (L->mode == SB_MODE_K3) return true;   // 16-bit activations: the prefill kernel at every size
   if (L->layout != SB_LAYOUT_TC || L->prefill == SB_PREFILL_VERIFY) return false;
   if (L->prefill == SB_PREFILL_WIDE) return true;
   return m * L->topk >= WIDE_TOKENS_PER_EXPERT * (int64_t)L->n_experts;
@@ -85,7 +86,12 @@ bool use_wide(const sb_moe_layer* L, int64_t m) {
 
 // Tokens per pass of a routed expert and of the shared expert. The prefill kernel takes passes of
 // 128 tokens, or 64 when fp32 activation scales double its B operand (hi and lo planes).
-int64_t wide_pass(const sb_moe_layer* L) { return L->act_pow2 ? sb::TC_WIDE_PASS : sb::TC_WIDE_PASS / 2; }
+int64_t wide_pass(const sb_moe_layer* L) {
+  return (L->act_pow2 || L->mode == SB_MODE_K3) ? sb::TC_WIDE_PASS : sb::TC_WIDE_PASS / 2;
+}
+
+// hi and lo planes of the prefill kernel's B operands (fp32 activation scales), else one
+int64_t wide_planes(const sb_moe_layer* L) { return (L->act_pow2 || L->mode == SB_MODE_K3) ? 1 : 2; }
 
 int64_t routed_pass_max(const sb_moe_layer* L, int64_t m) {
   return use_wide(L, m) ? wide_pass(L) : sb::tc_pass_max(L->expert_fmt);
@@ -145,7 +151,7 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   w.bpanel = take((size_t)panel_tiles * 2048);
   w.apanel = (float*)take((size_t)panel_tiles * 16 * sizeof(float));
   // fp32 activation scales: a residual plane below each matrix (hi + lo)
-  const int64_t planes = L->act_pow2 ? 1 : 2;
+  const int64_t planes = wide_planes(L);
   w.xw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * w.wide_rows * H : 0);
   w.hw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * w.wide_rows * I : 0);
   w.cx = (float*)take(w.wide ? sizeof(float) * w.wide_rows : 0);
@@ -165,13 +171,20 @@ int check_layer(const sb_moe_layer* L) {
   if (L->expert_fmt != SB_FMT_NVFP4 && L->expert_fmt != SB_FMT_MXFP4 && L->expert_fmt != SB_FMT_FP8)
     return fail(SB_ERR_FORMAT, "expert_fmt=%d unknown", L->expert_fmt);
   if (L->score_func < 0 || L->score_func > 2) return fail(SB_ERR_ARG, "score_func=%d unknown", L->score_func);
-  if (!L->gate_w) return fail(SB_ERR_ARG, "gate_w is NULL");
+  if (L->mode != SB_MODE_V4 && L->mode != SB_MODE_K3) return fail(SB_ERR_ARG, "mode=%d unknown", L->mode);
+  if (L->mode == SB_MODE_K3 &&
+      (L->expert_fmt != SB_FMT_MXFP4 || L->has_shared || L->layout != SB_LAYOUT_TC || L->tid2eid ||
+       !(L->situ_beta > 0.f) || L->situ_linear_beta < 0.f))
+    return fail(SB_ERR_UNSUPPORTED,
+                "K3 mode needs MXFP4 experts in the tensor-core layout, no shared expert, no hash routing, "
+                "situ_beta > 0 and situ_linear_beta >= 0");
+  if (L->mode == SB_MODE_V4 && !L->gate_w) return fail(SB_ERR_ARG, "gate_w is NULL");
   if (!L->w13 || !L->w13_s || !L->w2 || !L->w2_s) return fail(SB_ERR_ARG, "routed expert bank pointer is NULL");
   if (L->expert_fmt == SB_FMT_NVFP4 && (!L->w13_ts || !L->w2_ts))
     return fail(SB_ERR_ARG, "NVFP4 experts need w13_ts and w2_ts");
   if (L->has_shared && (!L->sh_w13 || !L->sh_w13_s || !L->sh_w2 || !L->sh_w2_s))
     return fail(SB_ERR_ARG, "shared expert pointer is NULL");
-  if (!aligned16(L->w13) || !aligned16(L->w2) || !aligned16(L->gate_w) ||
+  if (!aligned16(L->w13) || !aligned16(L->w2) || (L->gate_w && !aligned16(L->gate_w)) ||
       (L->has_shared && (!aligned16(L->sh_w13) || !aligned16(L->sh_w2))))
     return fail(SB_ERR_ARG, "weight pointers must be 16-byte aligned");
   if (L->tid2eid && L->vocab <= 0) return fail(SB_ERR_ARG, "tid2eid given with vocab=%lld", (long long)L->vocab);
@@ -523,6 +536,7 @@ int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int6
                  int64_t* out_indices, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_layer(layer);
   if (rc) return rc;
+  if (layer->mode == SB_MODE_K3) return fail(SB_ERR_UNSUPPORTED, "K3-mode layers have no router");
   if (!x) return fail(SB_ERR_ARG, "x is NULL");
   if (m < 0 || m > (1 << 20)) return fail(SB_ERR_SHAPE, "m=%lld outside 0..2^20", (long long)m);
   if (m == 0) return SB_OK;
@@ -535,7 +549,8 @@ int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int6
 
 static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,
                         float* out_weights, int64_t* out_indices, void* workspace, size_t workspace_bytes,
-                        void* stream, void* const* events, void* wire_q = nullptr, void* wire_s = nullptr) {
+                        void* stream, void* const* events, void* wire_q = nullptr, void* wire_s = nullptr,
+                        const int64_t* ext_idx = nullptr, const float* ext_w = nullptr) {
   cudaStream_t st = (cudaStream_t)stream;
   auto mark = [&](int i) {
     if (events && events[i]) cudaEventRecord((cudaEvent_t)events[i], st);
@@ -551,11 +566,25 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   if (m == 0) return SB_OK;
   if (L->tid2eid && !input_ids) return fail(SB_ERR_ARG, "hash routing needs input_ids");
   if ((int64_t)m * L->topk > (1 << 22)) return fail(SB_ERR_SHAPE, "m * topk too large");
+  const bool k3 = L->mode == SB_MODE_K3;
+  if (k3 != (ext_idx != nullptr))
+    return fail(SB_ERR_UNSUPPORTED, k3 ? "K3-mode layers take the caller's routing (sb_moe_forward_routed)"
+                                       : "the caller's routing is taken by K3-mode layers only");
+  if (k3 && (!ext_w || wire_q)) return fail(SB_ERR_ARG, "K3 mode: routing weights needed, no wire output");
   Workspace w = carve(L, m, (uint8_t*)workspace);
   if (!workspace || workspace_bytes < w.bytes)
     return fail(SB_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", workspace_bytes, w.bytes);
   mark(0);
-  rc = route_impl(L, x, m, input_ids, out_weights, out_indices, w, true, st);
+  if (k3) {
+    // the caller's routing; an id out of range raises the second flag word, folded in by the permutation
+    rc = cuda_check(cudaMemsetAsync(w.err + 1, 0, sizeof(int32_t), st), "routing flag");
+    if (rc) return rc;
+    rc = cuda_check(sb::launch_routing_in(ext_idx, ext_w, (int)m, L->topk, L->n_experts, w.topk_idx, w.topk_w,
+                                          w.err + 1, st),
+                    "routing in");
+  } else {
+    rc = route_impl(L, x, m, input_ids, out_weights, out_indices, w, true, st);
+  }
   if (rc) return rc;
   mark(1);
   sb::PermuteArgs p;
@@ -570,7 +599,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.pair_tok = w.pair_tok;
   p.pair_slot = w.pair_slot;
   p.err = w.err;
-  p.gate_err = use_wide(L, m) ? w.err + 1 : nullptr;
+  p.gate_err = use_wide(L, m) ? w.err + 1 : nullptr;   // the tensor-core gate's (or the routing input's) flag
   p.pass_max = L->layout == SB_LAYOUT_TC ? (int)routed_pass_max(L, m) : 0;
   p.pass_off = L->layout == SB_LAYOUT_TC ? w.pass_off : nullptr;
   p.pass_slot = w.pass_slot;
@@ -600,6 +629,10 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   // the verify kernel's block-scaled items: MXFP4 with power-of-two activation scales, FP8 when its
   // block scales are powers of two as well
   g.bs_mask = L->act_pow2 ? ((1 << SB_FMT_MXFP4) | (L->fp8_pow2 ? (1 << SB_FMT_FP8) : 0)) : 0;
+  g.activation = L->mode == SB_MODE_K3 ? sb::ACT_SITU : sb::ACT_SWIGLU;
+  g.act_beta = L->situ_beta;
+  g.act_lbeta = L->situ_linear_beta;
+  g.weight_after = L->mode == SB_MODE_K3;
   const int n_units = (int)(max_active + (L->has_shared ? 1 : 0));
   if (L->layout == SB_LAYOUT_TC && w.wide) {
     // prefill kernel: x (act-quantised, bf16) in expert order, w13 (+ SwiGLU -> h), h act-quantised
@@ -611,11 +644,14 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     plan.pass_pb = w.pass_pb;
     plan.n_sh_pass = w.n_sh_pass;
     const int64_t R = P + m;
-    const int split = L->act_pow2 ? 0 : 1;
+    const int split = (int)wide_planes(L) - 1;
     const int rbf = L->expert_fmt == SB_FMT_MXFP4 ? 1 : 0;   // MXFP4 experts take bf16 operands
-    rc = cuda_check(sb::launch_wide_x(w.xq, w.xs, w.pair_tok, w.offsets, L->n_experts, (int)m, (int)P, (int)H,
-                                      w.wide_rows, (int)w.sb_row, split, rbf, w.xw, w.cx, st),
-                    "wide x");
+    rc = k3 ? cuda_check(sb::launch_wide_x_raw(x, w.pair_tok, w.offsets, L->n_experts, (int)P, (int)H, w.wide_rows,
+                                                w.xw, w.cx, st),
+                         "wide x (bf16)")
+            : cuda_check(sb::launch_wide_x(w.xq, w.xs, w.pair_tok, w.offsets, L->n_experts, (int)m, (int)P, (int)H,
+                                           w.wide_rows, (int)w.sb_row, split, rbf, w.xw, w.cx, st),
+                         "wide x");
     if (rc) return rc;
     g.mode = sb::MODE_W13;
     g.n_rows = (int)(2 * I);
@@ -631,9 +667,10 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
                     "wide w13");
     if (rc) return rc;
     mark(3);
-    rc = cuda_check(sb::launch_wide_h(w.hbf, w.wide_rows, w.wide_rows, (int)w.sb_row, (int)I, L->act_pow2, rbf, w.hw,
-                                      w.ch, st),
-                    "wide h");
+    rc = k3 ? cuda_check(sb::launch_wide_h_raw(w.hbf, w.wide_rows, w.wide_rows, (int)I, w.hw, w.ch, st), "wide h (bf16)")
+            : cuda_check(sb::launch_wide_h(w.hbf, w.wide_rows, w.wide_rows, (int)w.sb_row, (int)I, L->act_pow2, rbf,
+                                           w.hw, w.ch, st),
+                         "wide h");
     if (rc) return rc;
     g.mode = sb::MODE_W2;
     g.n_rows = (int)H;
@@ -733,7 +770,10 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   if (rc) return rc;
   }
   mark(4);
-  if (wire_q)
+  if (k3)
+    rc = cuda_check(sb::launch_combine_weighted(w.o, w.topk_w, (int)m, L->topk, (int)H, (__nv_bfloat16*)y, st),
+                    "combine (weighted)");
+  else if (wire_q)
     rc = cuda_check(sb::launch_combine_pack(w.o, w.topk_idx, (int)m, L->topk, (int)H, L->has_shared,
                                             (__nv_bfloat16*)y, (uint8_t*)wire_q, (__nv_bfloat16*)wire_s, st),
                     "combine+pack");
@@ -757,6 +797,17 @@ int sb_moe_forward_profiled(const sb_moe_layer* layer, const void* x, int64_t m,
                             void* stream, void* const* events) {
   return forward_impl(layer, x, m, input_ids, y, out_weights, out_indices, workspace, workspace_bytes, stream,
                       events);
+}
+
+int sb_moe_forward_routed(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* topk_idx,
+                          const float* topk_w, void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  if (m > 0 && (!topk_idx || !topk_w)) return fail(SB_ERR_ARG, "topk_idx or topk_w is NULL");
+  if (m == 0) {
+    const int rc = check_layer(layer);
+    return rc ? rc : SB_OK;
+  }
+  return forward_impl(layer, x, m, nullptr, y, nullptr, nullptr, workspace, workspace_bytes, stream, nullptr, nullptr,
+                      nullptr, topk_idx, topk_w);
 }
 
 int sb_moe_forward_wire(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids, void* y,

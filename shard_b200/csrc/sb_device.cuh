@@ -116,6 +116,15 @@ __device__ __forceinline__ uint8_t act_q_pow2(float v, float inv_s) {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// K3's SituAndMul on one (gate, up) pair in fp32 (modeling_kimi_linear.py:64-82):
+// (beta * tanh(g / beta)) * sigmoid(g) * up', up' = linear_beta * tanh(up / linear_beta) when
+// linear_beta is set (lbeta > 0), else up
+__device__ __forceinline__ float situ(float g, float u, float beta, float lbeta) {
+  const float a = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
+  const float up = lbeta > 0.f ? lbeta * tanhf(u / lbeta) : u;
+  return a * up;
+}
+
 // ── tensor-core fragments (mma.sync, fp32 accumulate) ───────────────────────────────────────────
 // m16n8k16 f16: A rows g / g+8, k {2t,2t+1} and {2t+8,2t+9}; B (k x n) k {2t,2t+1},{2t+8,2t+9}, n = g;
 // C rows g / g+8, cols {2t, 2t+1}   (g = lane/4, t = lane%4)

@@ -666,6 +666,71 @@ __global__ void __launch_bounds__(128) combine_kernel(const __nv_bfloat16* __res
   *reinterpret_cast<uint4*>(y + (size_t)t * h + v * 8) = out;
 }
 
+// K3's combine (KimiSparseMoeBlock.moe_infer, modeling_kimi_linear.py:868-875): per token, the fp32
+// sum over its slots in slot order of (bf16 expert output as fp32) x (the slot's routing weight),
+// rounded to bf16. Thread = 8 consecutive columns of one token.
+__global__ void __launch_bounds__(128) combine_weighted_kernel(const __nv_bfloat16* __restrict__ o,
+                                                               const float* __restrict__ topk_w, int m, int topk, int h,
+                                                               __nv_bfloat16* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (t >= m || c >= h) return;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    const float w = topk_w[(size_t)t * topk + k];
+    const uint4 v = *reinterpret_cast<const uint4*>(o + ((size_t)t * topk + k) * h + c);
+    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(p[i]);
+      acc[2 * i] += f.x * w;
+      acc[2 * i + 1] += f.y * w;
+    }
+  }
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+    r[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  *reinterpret_cast<uint4*>(y + (size_t)t * h + c) = make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+cudaError_t launch_combine_weighted(const __nv_bfloat16* o, const float* topk_w, int m, int topk, int h,
+                                    __nv_bfloat16* y, cudaStream_t st) {
+  const dim3 grid(m, (h / 8 + 127) / 128), block(128);
+  return launch_pdl(combine_weighted_kernel, grid, block, 0, st, o, topk_w, m, topk, h, y);
+}
+
+// The caller's routing (int64 ids, fp32 weights) into the workspace's int32 ids and weights; an id
+// outside [0, n_experts) sets *err (the flag the permutation folds into the forward's error flag).
+__global__ void routing_in_kernel(const int64_t* __restrict__ idx_in, const float* __restrict__ w_in, int n, int n_experts,
+                                  int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int* err) {
+  pdl_wait();
+  pdl_trigger();
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+    int64_t e = idx_in[p];
+    if (e < 0 || e >= n_experts) {
+      atomicExch(err, 1);
+      e = 0;
+    }
+    topk_idx[p] = (int32_t)e;
+    topk_w[p] = w_in[p];
+  }
+}
+
+cudaError_t launch_routing_in(const int64_t* idx_in, const float* w_in, int m, int topk, int n_experts,
+                              int32_t* topk_idx, float* topk_w, int* err, cudaStream_t st) {
+  const int n = m * topk;
+  const int grid = (n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024;
+  return launch_pdl(routing_in_kernel, dim3(grid < 1 ? 1 : grid), dim3(256), 0, st, idx_in, w_in, n, n_experts,
+                    topk_idx, topk_w, err);
+}
+
 cudaError_t launch_combine(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h, int has_shared,
                            __nv_bfloat16* y, cudaStream_t st) {
   dim3 grid(m, (h / 8 + 127) / 128);

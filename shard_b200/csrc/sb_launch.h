@@ -84,7 +84,12 @@ struct GroupedArgs {
   uint32_t wait_limit; // tensor-core path: polls of the consumer-side waits (0: the kernel's default)
   int bs_mask;         // verify kernel: bit f set = items of weight format f run block-scaled
                        // (FMT_MXFP4, FMT_FP8; only with power-of-two activation and weight scales)
+  int activation;      // ACT_SWIGLU (Expert.forward) or ACT_SITU (K3's SituAndMul)
+  float act_beta, act_lbeta;  // situ: beta, and linear_beta (0: up is not transformed)
+  int weight_after;    // 1: the routing weight is not applied to h (the combine applies it to o)
 };
+
+enum Activation { ACT_SWIGLU = 0, ACT_SITU = 1 };
 
 // Tensor-core path: the activation operand of every pass, prepared before the grouped launch.
 // Pass order: the shared expert's (or the dense matrix's) passes first, then each active expert's
@@ -144,6 +149,17 @@ cudaError_t launch_tile_scales(int fmt, int kind, const void* src, void* dst, in
 cudaError_t launch_selftest(float* out, cudaStream_t st);
 cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st);
 cudaError_t launch_tc_grouped(const GroupedArgs& a, const TcPlan& plan, int max_items, cudaStream_t st);
+// K3 mode (KimiSparseMoeBlock.moe_infer): the caller's routing into the workspace (ids checked against
+// the expert count: an id out of range sets *err to 1 and is replaced by 0), the bf16 activations
+// copied as they are into the prefill kernel's operand layouts, and the slot-order weighted combine.
+cudaError_t launch_routing_in(const int64_t* idx_in, const float* w_in, int m, int topk, int n_experts,
+                              int32_t* topk_idx, float* topk_w, int* err, cudaStream_t st);
+cudaError_t launch_wide_x_raw(const void* x, const int32_t* pair_tok, const int32_t* offsets, int n_experts, int P,
+                              int h, int64_t r_pad, void* xw, float* cvec, cudaStream_t st);
+cudaError_t launch_wide_h_raw(const __nv_bfloat16* hbf, int64_t rows, int64_t r_pad, int k, void* hw, float* cvec,
+                              cudaStream_t st);
+cudaError_t launch_combine_weighted(const __nv_bfloat16* o, const float* topk_w, int m, int topk, int h,
+                                    __nv_bfloat16* y, cudaStream_t st);
 cudaError_t launch_wire_pack(const void* x, int64_t rows, int64_t dim, uint8_t* q, void* s, cudaStream_t st);
 cudaError_t launch_wire_unpack(const uint8_t* q, const void* s, int64_t rows, int64_t dim, void* y, cudaStream_t st);
 cudaError_t launch_combine_pack(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h,

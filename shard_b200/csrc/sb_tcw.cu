@@ -952,12 +952,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
             for (int e = 0; e < 2; ++e) {
               float gv = bf16_round(__uint_as_float(gd[q + e]) * cb * (cav[c0 + q + e] * ts0));
               float uv = bf16_round(__uint_as_float(ud[q + e]) * cb * (cav[64 + c0 + q + e] * ts1));
-              if (lim > 0.f) {
-                uv = fminf(fmaxf(uv, -lim), lim);
-                gv = fminf(gv, lim);
+              float hvv;
+              if (a.activation == ACT_SITU) {
+                hvv = situ(gv, uv, a.act_beta, a.act_lbeta);
+              } else {
+                if (lim > 0.f) {
+                  uv = fminf(fmaxf(uv, -lim), lim);
+                  gv = fminf(gv, lim);
+                }
+                hvv = silu(gv) * uv;
               }
-              float hvv = silu(gv) * uv;
-              if (!it.shared) hvv = wgt * hvv;
+              if (!it.shared && !a.weight_after) hvv = wgt * hvv;
               h2[e] = hvv;
             }
             const __nv_bfloat162 b = __floats2bfloat162_rn(h2[0], h2[1]);
@@ -1226,6 +1231,45 @@ static cudaError_t launch_one(const WideArgs& a, int grid, cudaStream_t st) {
 #endif
 }
 
+// K3 mode: the bf16 activations enter the expert GEMMs as they are (W4A16). Pair q's token row of x
+// (or row `row` of h) is copied into the padded chunk-major operand layout, 16 bytes per lane step,
+// with the row's divisor c_B = 1.
+__global__ void __launch_bounds__(256) wide_x_raw_kernel(const uint16_t* __restrict__ x,
+                                                         const int32_t* __restrict__ pair_tok,
+                                                         const int32_t* __restrict__ offsets, int n_experts, int P,
+                                                         int h, int64_t r_pad, uint16_t* __restrict__ xw,
+                                                         float* __restrict__ cvec) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t q = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; q < P; q += nw) {
+    int lo = 0, hi = n_experts;   // the expert of pair q: the last e with offsets[e] <= q
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (offsets[mid] <= q) lo = mid; else hi = mid;
+    }
+    const int tok = pair_tok[q];
+    const int64_t row = pbase(offsets[lo], lo) + (int)(q - offsets[lo]);
+    for (int v = lane; v < h / 8; v += 32)
+      *reinterpret_cast<uint4*>(xw + cm_off(row, v, r_pad)) = *reinterpret_cast<const uint4*>(x + (size_t)tok * h + v * 8);
+    if (lane == 0) cvec[row] = 1.f;
+  }
+}
+
+__global__ void __launch_bounds__(256) wide_h_raw_kernel(const uint16_t* __restrict__ hbf, int64_t rows, int64_t r_pad,
+                                                         int k, uint16_t* __restrict__ hw, float* __restrict__ cvec) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {
+    for (int v = lane; v < k / 8; v += 32)
+      *reinterpret_cast<uint4*>(hw + cm_off(row, v, r_pad)) = *reinterpret_cast<const uint4*>(hbf + row * k + v * 8);
+    if (lane == 0) cvec[row] = 1.f;
+  }
+}
+
 static unsigned warp_grid(int64_t rows) {
   const int64_t b = (rows + 7) / 8;   // one warp per row, 8 warps per block
   return (unsigned)(b < 1 ? 1 : (b > 65535 ? 65535 : b));
@@ -1276,6 +1320,18 @@ cudaError_t launch_wide_x(const uint8_t* xq, const float* xs, const int32_t* pai
   return launch_pdl(tcw::wide_x_kernel, dim3(tcw::warp_grid((int64_t)P + m)), dim3(256), 0, st, xq, xs, pair_tok,
                     offsets, n_experts, m, P, h, r_pad, sb_row, split, routed_bf16, reinterpret_cast<uint16_t*>(xw),
                     cvec);
+}
+
+cudaError_t launch_wide_x_raw(const void* x, const int32_t* pair_tok, const int32_t* offsets, int n_experts, int P,
+                              int h, int64_t r_pad, void* xw, float* cvec, cudaStream_t st) {
+  return launch_pdl(tcw::wide_x_raw_kernel, dim3(tcw::warp_grid(P)), dim3(256), 0, st, (const uint16_t*)x, pair_tok,
+                    offsets, n_experts, P, h, r_pad, (uint16_t*)xw, cvec);
+}
+
+cudaError_t launch_wide_h_raw(const __nv_bfloat16* hbf, int64_t rows, int64_t r_pad, int k, void* hw, float* cvec,
+                              cudaStream_t st) {
+  return launch_pdl(tcw::wide_h_raw_kernel, dim3(tcw::warp_grid(rows)), dim3(256), 0, st, (const uint16_t*)hbf, rows,
+                    r_pad, k, (uint16_t*)hw, cvec);
 }
 
 cudaError_t launch_wide_h(const __nv_bfloat16* hbf, int64_t rows, int64_t r_pad, int sb_row, int k, int pow2,

@@ -76,12 +76,16 @@ class MoELayer:
     def __init__(self, *, hidden, inter, n_experts, topk, expert_fmt, gate_w, gate_bias=None, tid2eid=None,
                  score_func="sigmoid", route_scale=1.0, swiglu_limit=0.0, act_pow2=True,
                  w13, w13_s, w13_ts=None, w2, w2_s, w2_ts=None, shared=None, tiled=False, layout=None,
-                 logits_bf16=False, renormalize=True, prefill=0):
+                 logits_bf16=False, renormalize=True, prefill=0, mode="v4", situ_beta=1.0, situ_linear_beta=None):
+        """mode "v4": MoE.forward of DeepSeek-V4 (the gate routes). mode "k3": the routed experts of
+        Kimi-K3's KimiSparseMoeBlock.moe_infer (the caller routes, forward_routed): gate_w may be None,
+        MXFP4 experts, no shared expert, situ activation with situ_beta / situ_linear_beta."""
         self.hidden, self.inter, self.n_experts, self.topk = hidden, inter, n_experts, topk
         self.layout = DEFAULT_LAYOUT if layout is None else layout
         self.expert_fmt = expert_fmt
-        self.device = gate_w.device
-        self.gate_w = gate_w.contiguous().to(torch.bfloat16)
+        self.mode = mode
+        self.device = w13.device
+        self.gate_w = None if gate_w is None else gate_w.contiguous().to(torch.bfloat16)
         self.gate_bias = None if gate_bias is None else gate_bias.contiguous().float()
         self.tid2eid = None if tid2eid is None else tid2eid.contiguous().to(torch.int32)
         e, h, i = n_experts, hidden, inter
@@ -129,6 +133,9 @@ class MoELayer:
         d.logits_bf16 = 1 if logits_bf16 else 0
         d.no_renorm = 0 if renormalize else 1
         d.fp8_pow2 = 1 if self.prefill_exact else 0
+        d.mode = _lib.MODE_K3 if mode == "k3" else _lib.MODE_V4
+        d.situ_beta = float(situ_beta)
+        d.situ_linear_beta = float(situ_linear_beta or 0.0)
         self.prefill = prefill     # 0 auto, 1 verify kernel, 2 prefill kernel
         self._ws = None
         self._ws_need = {}
@@ -175,8 +182,8 @@ class MoELayer:
         return int(self._ws[:4].view(torch.int32).item())
 
     def weight_bytes(self) -> int:
-        ts = [self.gate_w, self.w13, self.w13_s, self.w2, self.w2_s]
-        ts += [t for t in (self.gate_bias, self.w13_ts, self.w2_ts) if t is not None]
+        ts = [self.w13, self.w13_s, self.w2, self.w2_s]
+        ts += [t for t in (self.gate_w, self.gate_bias, self.w13_ts, self.w2_ts) if t is not None]
         ts += list(self.shared or ())
         return sum(t.numel() * t.element_size() for t in ts)
 
@@ -203,6 +210,22 @@ class MoELayer:
         return y
 
     __call__ = forward
+
+    def forward_routed(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weight: torch.Tensor,
+                       out: Optional[torch.Tensor] = None, stream=None):
+        """K3 mode: x bf16 [M, H] (cuda), the router's decision topk_ids [M, k] (distinct ids per
+        token) and topk_weight [M, k] -> y bf16 [M, H] (KimiSparseMoeBlock.moe_infer)."""
+        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] == self.hidden
+        x = x.contiguous()
+        m = x.shape[0]
+        ids = topk_ids.to(device=x.device, dtype=torch.int64).contiguous()
+        w = topk_weight.to(device=x.device, dtype=torch.float32).contiguous()
+        assert ids.shape == (m, self.topk) and w.shape == (m, self.topk)
+        y = out if out is not None else torch.empty_like(x)
+        ws = self.reserve(m)
+        check(lib().sb_moe_forward_routed(ctypes.byref(self.desc), ptr(x), m, ptr(ids), ptr(w), ptr(y), ptr(ws),
+                                          ws.numel(), stream_ptr(stream)), "sb_moe_forward_routed")
+        return y
 
     def forward_wire(self, x: torch.Tensor, input_ids: Optional[torch.Tensor] = None, y: Optional[torch.Tensor] = None,
                      stream=None):

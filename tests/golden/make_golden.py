@@ -233,6 +233,97 @@ def run_case(mod, K, name, out_dir):
     print(f"{name}: M={m} experts routed={len(set(idx.flatten().tolist()))} |y|max={y.float().abs().max():.4f}")
 
 
+# Kimi-K3 routed-expert cases: the reference's KimiSparseMoeBlock (vendor/kimi_k3_ref/
+# modeling_kimi_linear.py:782-876) with MXFP4 experts (the K3 checkpoint format, k3_moe_mxfp4.py:1-9)
+# held as their exact bf16 values; its own KimiMoEGate routes, its moe_infer runs.
+K3_CASES = {
+    # name: (hidden, experts, top-k, intermediate, seed, M, situ beta, situ linear_beta)
+    "k3_mxfp4_m8": (512, 16, 4, 256, 11, 8, 2.0, 4.0),
+    "k3_mxfp4_nolb_m37": (512, 16, 4, 256, 12, 37, 1.0, None),
+}
+
+
+def k3_config(name):
+    h, e, k, i, seed, m, beta, lb = K3_CASES[name]
+    cfg = S.MoEConfig(name, h, e, k, i, n_shared=0, expert_fmt=F.FMT_MXFP4, gate_init="normal", seed=seed)
+    return cfg, m, beta, lb
+
+
+def _load_k3(ref_root):
+    """The reference's K3 modules, imported the way its K3 engine imports them (engines/kimi_k3/
+    k3_stage.py:115-141: the CPU `fla` stand-in first, then the one moved transformers symbol)."""
+    import importlib
+    for p in (os.path.join(ref_root, "engines", "kimi_k3"), os.path.join(ref_root, "vendor"), ref_root):
+        sys.path.insert(0, p)
+    import k3_kda_cpu  # noqa: E402
+    k3_kda_cpu.install()
+    generic = importlib.import_module("transformers.utils.generic")
+    if not hasattr(generic, "OutputRecorder"):
+        generic.OutputRecorder = importlib.import_module("transformers.utils.output_capturing").OutputRecorder
+    from kimi_k3_ref import modeling_kimi_linear as MK  # noqa: E402
+    from kimi_k3_ref.configuration_kimi_k3 import KimiLinearConfig  # noqa: E402
+    return MK, KimiLinearConfig
+
+
+def k3_seam_record(block):
+    rec = {"top_k": block.top_k, "num_experts": block.num_experts, "ep_size": block.ep_size,
+           "ep_rank": block.ep_rank, "experts_per_rank": block.experts_per_rank,
+           "moe_hidden_size": block.moe_hidden_size,
+           "act": {"beta": block.experts[0].act_fn.beta, "linear_beta": block.experts[0].act_fn.linear_beta},
+           "linears": {}, "params": {}}
+    for name, sub in block.named_modules():
+        if isinstance(sub, torch.nn.Linear):
+            rec["linears"][name] = {"in_features": sub.in_features, "out_features": sub.out_features}
+    for name, p in block.named_parameters():
+        if name.startswith("experts."):
+            rec["params"][name] = {"dtype": str(p.dtype), "shape": list(p.shape), "sha": _sha(p)}
+    return rec
+
+
+def run_k3_case(MK, KimiLinearConfig, name, out_dir):
+    cfg, m, beta, lb = k3_config(name)
+    h, e, k, i = cfg.hidden, cfg.n_experts, cfg.topk, cfg.inter
+    kc = KimiLinearConfig(hidden_size=h, num_experts=e, num_experts_per_token=k, moe_intermediate_size=i,
+                          hidden_act="situ", activation_situ_beta=beta, activation_situ_linear_beta=lb,
+                          num_shared_experts=None, moe_renormalize=True, routed_scaling_factor=2.5,
+                          moe_router_activation_func="sigmoid")
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        block = MK.KimiSparseMoeBlock(kc).eval()
+        gw, gb = S.make_gate(cfg)
+        shas = {}
+        with torch.no_grad():
+            block.gate.weight.copy_(gw)
+            block.gate.e_score_correction_bias.copy_(gb)
+            for ex in range(e):
+                ew = S.make_expert(cfg, 0, ex)
+                deq = [F.dequant_weight(F.FMT_MXFP4, ew.w13[:i], ew.w13_s[:i]),
+                       F.dequant_weight(F.FMT_MXFP4, ew.w13[i:], ew.w13_s[i:]),
+                       F.dequant_weight(F.FMT_MXFP4, ew.w2, ew.w2_s)]
+                for lin, w in zip((block.experts[ex].w1, block.experts[ex].w3, block.experts[ex].w2), deq):
+                    assert torch.equal(w.to(torch.bfloat16).float(), w), "MXFP4 values must be exact in bf16"
+                    lin.weight.copy_(w.to(torch.bfloat16))
+                shas[str(ex)] = S.tensor_sha(ew.w13, ew.w13_s, ew.w2, ew.w2_s)
+        x, _ = S.make_inputs(cfg, m)
+        with torch.no_grad():
+            topk_idx, topk_weight = block.gate(x.view(1, m, h))
+            y = block.moe_infer(x, topk_idx, topk_weight)
+    finally:
+        torch.set_default_dtype(prev)
+    meta = dict(case=name, hidden=h, experts=e, topk=k, inter=i, seed=cfg.seed, m=m, situ_beta=beta,
+                situ_linear_beta=lb, reference="leyten/shard vendor/kimi_k3_ref KimiSparseMoeBlock.moe_infer")
+    np.savez_compressed(
+        os.path.join(out_dir, f"{name}.npz"), meta=json.dumps(meta), x_sha=S.tensor_sha(x),
+        expert_sha=json.dumps(shas), topk_idx=topk_idx.numpy().astype(np.int64),
+        topk_weight=topk_weight.float().numpy(), y_bits=y.contiguous().view(torch.int16).numpy().astype(np.uint16))
+    rec = k3_seam_record(block)
+    rec["case"] = name
+    with open(os.path.join(out_dir, f"seam_{name}.json"), "w") as f:
+        json.dump(rec, f, indent=1, sort_keys=True)
+    print(f"{name}: M={m} |y|max={y.float().abs().max():.4f} experts used={len(set(topk_idx.flatten().tolist()))}")
+
+
 def run_kats(mod, K, out_dir):
     torch.manual_seed(11)
     a_bf = (torch.randn(5, 256) * 2).bfloat16()
@@ -274,11 +365,19 @@ def main():
     ap.add_argument("--only", nargs="*")
     a = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
-    mod, K = _load_reference(a.ref)
-    _patch_nvfp4(mod, K)
-    run_kats(mod, K, a.out)
-    for name in (a.only or CASES):
-        run_case(mod, K, name, a.out)
+    only = a.only or (list(CASES) + list(K3_CASES))
+    if any(n in CASES for n in only):
+        mod, K = _load_reference(a.ref)
+        _patch_nvfp4(mod, K)
+        run_kats(mod, K, a.out)
+        for name in only:
+            if name in CASES:
+                run_case(mod, K, name, a.out)
+    if any(n in K3_CASES for n in only):
+        MK, KC = _load_k3(a.ref)
+        for name in only:
+            if name in K3_CASES:
+                run_k3_case(MK, KC, name, a.out)
 
 
 if __name__ == "__main__":
