@@ -18,7 +18,8 @@ bf16 activations between stages and 8 chunks streamed per step. Per-GPU work is 
             same workload on the host cores.
   sweep   = (N=1) c1 at M = 1, 8, 32, 64 over the same 6 layers; one c3 layer (FP8 experts, Zipf
             selection) at M = 1, 16, 64 and one c4 layer (Kimi-K3-scale NVFP4, the prefill regime)
-            at M = 256, 1024, each forward starting from a flushed L2.
+            at M = 256, 1024, each forward starting from a flushed L2; fp8_gemm (the kernel seam's
+            dense GEMM) at V4's attention / indexer / shared-expert shapes, M = 1 and 16.
 
 --impl reference times that CPU path alone (rank 0), as the reference arm.
 """
@@ -373,6 +374,7 @@ def run_gpu(args, rank, world, local_rank):
             if not N_EXPERTS:
                 sweep.update(cfg_sweep("c3", (1, 16, 64)))
                 sweep.update(cfg_sweep("c4", (256, 1024), modes=(0, 1, 2)))
+                sweep.update(dense_sweep())
     clocks = clk.summary(set(range(world)) if world > 1 else {local_rank}) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -552,6 +554,69 @@ def cfg_sweep(name, ms, reps=4, modes=(0,)):
                     "grouped_frac": g / peak, "forward_gbs": f, "forward_frac": f / peak,
                     "l2": "flushed before each forward"}
     del lay, flush
+    torch.cuda.empty_cache()
+    return out
+
+
+# V4-Flash's dense FP8 projections that decode runs through model.linear -> fp8_gemm, [N, K]
+# (engines/deepseek_v4/v4_fp8_gemv.py:9-13): attention and indexer projections, shared expert.
+V4_DENSE = [("wq_a", 1024, 4096), ("wkv", 512, 4096), ("wo_b", 4096, 8192), ("wq_b", 32768, 1024),
+            ("idx_wq_b", 8192, 1024), ("shared_w1", 2048, 4096), ("shared_w2", 4096, 2048)]
+
+
+def dense_sweep(ms=(1, 16), reps=7):
+    """fp8_gemm (sb_qgemm, FP8 128x128 block scales, the tensor-core layout) at the V4 dense shapes:
+    device time of one call from a flushed L2 (median of `reps`), and bytes moved (weights + scales +
+    activations + output) per second against the measured HBM peak. `whole_k_us` is the same call
+    through sb_qgemm_static, which never splits K: the occupancy the split recovers."""
+    import ctypes
+    from shard_b200 import _lib, formats as F, ops
+    from shard_b200.moe import tile
+    peak, _ = hbm_peak()
+    L = _lib.lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    st = _lib.stream_ptr()
+    out = {}
+    for name, n, k in V4_DENSE:
+        g = torch.Generator().manual_seed(n * 7 + k)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        p, sc = F.quant_fp8_block(w)
+        wt, wst = tile(F.FMT_FP8, _lib.MAT_PLAIN, p.view(torch.uint8).to(dev), sc.float().to(dev), 1, n, k,
+                       _lib.LAYOUT_TC)
+        for m in ms:
+            x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+            q, s = ops.act_quant(x, 128, "ue8m0")
+            s = s.float().contiguous()
+            y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            wsb = L.sb_qgemm_workspace_bytes(F.FMT_FP8, _lib.LAYOUT_TC, n, k, m)
+            ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
+
+            def split():
+                _lib.check(L.sb_qgemm(F.FMT_FP8, _lib.LAYOUT_TC, wt.data_ptr(), wst.data_ptr(), None, n, k,
+                                      q.data_ptr(), s.data_ptr(), m, y.data_ptr(), ws.data_ptr(), wsb, st), "sb_qgemm")
+
+            def whole():
+                _lib.check(L.sb_qgemm_static(F.FMT_FP8, wt.data_ptr(), wst.data_ptr(), None, n, k, q.data_ptr(),
+                                             s.data_ptr(), m, y.data_ptr(), st), "sb_qgemm_static")
+            times = {}
+            for key, fn in (("us", split), ("whole_k_us", whole)):
+                fn()
+                ts = []
+                for r in range(reps):
+                    flush.fill_(r & 0xFF)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    fn()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ts.append(e0.elapsed_time(e1) * 1000.0)
+                times[key] = sorted(ts)[len(ts) // 2]
+            nbytes = n * k + (n // 128) * (k // 128) * 4 + m * k + m * (k // 128) * 4 + m * n * 2
+            gbs = nbytes / (times["us"] * 1e-6) / 1e9
+            out[f"fp8_gemm_{name}_m{m}"] = {"n": n, "k": k, "m": m, "us": times["us"], "gbs": gbs, "frac": gbs / peak,
+                                            "whole_k_us": times["whole_k_us"], "l2": "flushed before each call"}
+    del flush
     torch.cuda.empty_cache()
     return out
 

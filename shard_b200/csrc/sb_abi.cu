@@ -291,10 +291,46 @@ static size_t qgemm_ws(int fmt, int layout, int64_t k, int64_t m, uint8_t* base,
   return off;
 }
 
+// K pieces of a dense GEMM on the tensor-core layout. A narrow batch (m <= 64) of a matrix with few
+// 128-row blocks gives the verify kernel fewer items than its 2 CTAs per SM, each streaming its
+// rows' whole K through one ring, so most of HBM's bandwidth stays unused; splitting K into pieces
+// of >= 2 stages raises the items to about 2 per SM (the reference re-tiles the same GEMV shapes
+// for the same reason, v4_fp8_gemv.py:156-270). Returns the piece count (1: no split) and the
+// stages per piece.
+static int qgemm_ksplit(int fmt, int64_t n, int64_t k, int64_t m, int* kstages) {
+  const int nst = (int)(k / 128);
+  *kstages = nst;
+  if (m < 1 || m > 64 || n % 128) return 1;
+  const int64_t pm = sb::tc_pass_max(fmt);
+  const int64_t items = ((m + pm - 1) / pm) * (n / 128);
+  const int64_t target = 2 * 148;   // B200's SMs: a fixed figure, so the split (and the summation
+                                    // order) is a function of the shape alone
+  if (items >= target) return 1;
+  int want = (int)((target + items - 1) / items);
+  if (want > nst / 2) want = nst / 2;
+  if (want < 2) return 1;
+  const int per = (((nst + want - 1) / want) + 1) & ~1;   // a multiple of the kernel's 2-stage unit
+  *kstages = per;
+  return (nst + per - 1) / per;
+}
+
+// The fp32 partials of a split call, placed after the activation panel.
+static size_t qgemm_part_bytes(int fmt, int64_t n, int64_t k, int64_t m) {
+  int per = 0;
+  const int ks = qgemm_ksplit(fmt, n, k, m, &per);
+  return ks > 1 ? align256((size_t)ks * (size_t)m * (size_t)n * sizeof(float)) : 0;
+}
+
 size_t sb_qgemm_workspace_bytes(int fmt, int layout, int64_t n, int64_t k, int64_t m) {
-  (void)n;
   if (k < 128 || k % 128 || m < 0) return 0;
-  return qgemm_ws(fmt, layout, k, m < 1 ? 1 : m, nullptr, nullptr, nullptr, nullptr);
+  const int64_t mm = m < 1 ? 1 : m;
+  size_t need = qgemm_ws(fmt, layout, k, mm, nullptr, nullptr, nullptr, nullptr);
+  if (layout == SB_LAYOUT_TC)   // every m' <= m: the split ones add their partials
+    for (int64_t q = 1; q <= mm && q <= 64; ++q) {
+      const size_t e = qgemm_ws(fmt, layout, k, q, nullptr, nullptr, nullptr, nullptr) + qgemm_part_bytes(fmt, n, k, q);
+      if (e > need) need = e;
+    }
+  return need;
 }
 
 int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
@@ -330,7 +366,10 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
     int* err = nullptr;
     uint8_t* bpanel = nullptr;
     float* apanel = nullptr;
-    const size_t need = qgemm_ws(fmt, layout, k, m, (uint8_t*)workspace, &err, &bpanel, &apanel);
+    const size_t panel = qgemm_ws(fmt, layout, k, m, (uint8_t*)workspace, &err, &bpanel, &apanel);
+    int kstages = 0;
+    const int ksplit = qgemm_ksplit(fmt, n, k, m, &kstages);
+    const size_t need = panel + qgemm_part_bytes(fmt, n, k, m);
     if (!workspace || workspace_bytes < need)
       return fail(SB_ERR_WORKSPACE, "qgemm: workspace %zu bytes < %zu needed", workspace_bytes, need);
     if (!aligned16(q)) return fail(SB_ERR_ARG, "qgemm: activations must be 16-byte aligned");
@@ -365,6 +404,14 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
     a.err = err;
     a.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
     a.items_per_expert = (int)(n / 128);
+    if (ksplit > 1) {
+      a.ksplit = ksplit;
+      a.kstages = kstages;
+      a.part = (float*)((uint8_t*)workspace + panel);
+      rc = cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert * ksplit, st), "qgemm");
+      if (rc) return rc;
+      return cuda_check(sb::launch_ksplit_reduce(a.part, ksplit, m * n, (__nv_bfloat16*)y, st), "qgemm reduce");
+    }
     return cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert, st), "qgemm");
   }
   a.items_per_expert = (int)((n + 255) / 256);

@@ -87,6 +87,9 @@ struct GroupedArgs {
   int activation;      // ACT_SWIGLU (Expert.forward) or ACT_SITU (K3's SituAndMul)
   float act_beta, act_lbeta;  // situ: beta, and linear_beta (0: up is not transformed)
   int weight_after;    // 1: the routing weight is not applied to h (the combine applies it to o)
+  int ksplit;          // verify kernel, DENSE: K pieces per row block (<= 1: whole K per item)
+  int kstages;         // stages (128 K) per piece, a multiple of the kernel's unit of 2
+  float* part;         // ksplit > 1: fp32 partial outputs [ksplit][m][n_rows], reduced afterwards
 };
 
 enum Activation { ACT_SWIGLU = 0, ACT_SITU = 1 };
@@ -149,6 +152,8 @@ cudaError_t launch_tile_scales(int fmt, int kind, const void* src, void* dst, in
 cudaError_t launch_selftest(float* out, cudaStream_t st);
 cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st);
 cudaError_t launch_tc_grouped(const GroupedArgs& a, const TcPlan& plan, int max_items, cudaStream_t st);
+// y bf16 [mn] = the fp32 sum over the ksplit pieces of part [ksplit][mn], pieces in order; mn % 4 == 0
+cudaError_t launch_ksplit_reduce(const float* part, int ksplit, int64_t mn, __nv_bfloat16* y, cudaStream_t st);
 // K3 mode (KimiSparseMoeBlock.moe_infer): the caller's routing into the workspace (ids checked against
 // the expert count: an id out of range sets *err to 1 and is replaced by 0), the bf16 activations
 // copied as they are into the prefill kernel's operand layouts, and the slot-order weighted combine.

@@ -225,13 +225,26 @@ __device__ __forceinline__ bool workers_any(bool pred) {
 // matrix. Items are numbered pass-major: item = pass * nrb + rb, passes being the shared expert's
 // (or the dense matrix's) first, then each active expert's in slot order, so a hot expert's passes
 // run on different CTAs at about the same time and share its weight tiles through L2.
+// A dense GEMM whose row blocks are too few to occupy the GPU splits K: item = (pass, row block,
+// piece), piece ks covering stages [j0, j1); its fp32 partials are summed by a second kernel.
 struct Item {
   int shared, expert, rb, cnt, base, pb, pass;
+  int ks, j0, j1;
 };
 
 template <int FMT_R>
-__device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan, int item, int nrb) {
+__device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan, int item, int nrb, int nst) {
   Item it;
+  if (a.ksplit > 1) {
+    it.ks = item % a.ksplit;
+    item /= a.ksplit;
+    it.j0 = it.ks * a.kstages;
+    it.j1 = min(nst, it.j0 + a.kstages);
+  } else {
+    it.ks = 0;
+    it.j0 = 0;
+    it.j1 = nst;
+  }
   const int p = item / nrb;
   it.rb = item - p * nrb;
   it.pass = p;
@@ -309,7 +322,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   const int nrb = a.n_rows / 128;
   const int n_pass = (a.has_shared ? ta.plan.n_sh_pass : 0) +
                      (a.mode == MODE_DENSE ? 0 : ta.plan.pass_off[*a.n_active]);
-  const int n_items = n_pass * nrb;
+  const int n_items = n_pass * nrb * (a.ksplit > 1 ? a.ksplit : 1);
   const bool w13 = a.mode == MODE_W13;
   // the limit of the consumer-side waits (the MMA issuer's and the readback's); the producer's waits
   // for free slots and the final drains keep WAIT_LIMIT
@@ -332,10 +345,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     uint32_t g = 0, u = 0;
     bool ok = true;
     // the next item's descriptor is loaded one item ahead, so its global loads overlap this item
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb, nst) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb);
+      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const CUtensorMap* map = it.shared ? &ta.map_shared : &ta.map_routed;
@@ -350,8 +363,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
           break;
         }
         const size_t pst = (size_t)it.pass * nst;
-        for (int j = 0; j < nst && ok; j += UNIT, ++u) {
-          const int ns = min(UNIT, nst - j);
+        for (int j = it.j0; j < it.j1 && ok; j += UNIT, ++u) {
+          const int ns = min(UNIT, it.j1 - j);
           const uint32_t us = u % SS;
           if (!warp_wait(sm, err, smem_addr(&sm.sempty[us]), ((u / SS) & 1u) ^ 1u)) {
             ok = false;
@@ -394,10 +407,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     // g counts stages, u units, gq accumulator groups (one per unit, or one per block-scaled item)
     uint32_t g = 0, u = 0, gq = 0;
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb, nst) : Item{};
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb);
+      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
       const int fmt = item_fmt(it);
       if (block_scaled(fmt)) {
         // the whole K into one 16-column accumulator; per stage the weight and activation scale
@@ -410,8 +423,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         }
         const uint32_t cacc = tbase + q * GCOLS, csfa = cacc + SF_A_COL, csfb = cacc + SF_B_COL;
         const uint32_t afmt = fmt == FMT_FP8 ? 0u : 5u;
-        for (int j = 0; j < nst && ok; j += UNIT, ++u) {
-          const int ns = min(UNIT, nst - j);
+        for (int j = it.j0; j < it.j1 && ok; j += UNIT, ++u) {
+          const int ns = min(UNIT, it.j1 - j);
           const uint32_t us = u % SS;
           if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u, clim)) {
             ok = false;
@@ -449,7 +462,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
 #pragma unroll
               for (int c = 0; c < 4; ++c)
                 mma_bs(cacc, sdesc(abase + c * 32), sdesc(bbase + c * 32), idesc_bs(afmt, (uint32_t)c),
-                       csfa | ((uint32_t)c << 30), csfb | ((uint32_t)c << 30), (j + t > 0 || c > 0) ? 1u : 0u);
+                       csfa | ((uint32_t)c << 30), csfb | ((uint32_t)c << 30), (j + t > it.j0 || c > 0) ? 1u : 0u);
               commit(smem_addr(&sm.aempty[s]));   // operand slot and its scale-factor sources
             }
             __syncwarp();
@@ -469,8 +482,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
       }
       const uint32_t id = idesc(fmt == FMT_FP8 ? 0u : 5u);
       {
-        for (int j = 0; j < nst && ok; j += UNIT, ++u, ++gq) {
-          const int ns = min(UNIT, nst - j);
+        for (int j = it.j0; j < it.j1 && ok; j += UNIT, ++u, ++gq) {
+          const int ns = min(UNIT, it.j1 - j);
           const uint32_t q = gq % SA;
           if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.gempty[q]), ((gq / SA) & 1u) ^ 1u, clim)) {
             ok = false;
@@ -515,10 +528,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
     const int r = tid;  // weight row of the item = TMEM lane
     uint32_t u = 0, gq = 0;
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb) : Item{};
+    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb, nst) : Item{};
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb);
+      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pm = tc_pass_max(fmt);
@@ -559,7 +572,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         if (block_scaled(fmt)) {
           // one readback of the fully scaled accumulator per pass; the side slots went to the MMA warp
           const uint32_t q = gq % SA;
-          u += (uint32_t)((nst + UNIT - 1) / UNIT);
+          u += (uint32_t)((it.j1 - it.j0 + UNIT - 1) / UNIT);
           if (ok) ok = warp_wait<PROBE>(sm, err, smem_addr(&sm.gfull[q]), (gq / SA) & 1u, clim);
           if (ok) {
             fence_after();
@@ -574,8 +587,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
           }
           ++gq;
         } else
-        for (int j = 0; j < nst; j += UNIT, ++u, ++gq) {
-          const int ns = min(UNIT, nst - j);
+        for (int j = it.j0; j < it.j1; j += UNIT, ++u, ++gq) {
+          const int ns = min(UNIT, it.j1 - j);
           const uint32_t us = u % SS, q = gq % SA;
           // this unit's scales first (they landed long ago), so their loads overlap the MMA wait
           if (ok) ok = warp_wait<PROBE>(sm, err, smem_addr(&sm.sfull[us]), (u / SS) & 1u, clim);
@@ -761,7 +774,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
             for (int t = 0; t < 16; ++t) {
               if (t < pc) {
                 const int orow = __shfl_sync(0xffffffffu, my_orow, t);
-                a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(acc[t] * ts);
+                if (a.part != nullptr)
+                  a.part[((size_t)it.ks * a.m + orow) * a.n_rows + n0 + r] = acc[t] * ts;
+                else
+                  a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(acc[t] * ts);
               }
             }
           }
@@ -981,6 +997,35 @@ cudaError_t launch_tc_grouped(const GroupedArgs& g, const TcPlan& plan, int max_
     case FMT_MXFP4: return tc::launch_tc_one<FMT_MXFP4>(a, grid, st);
     default: return tc::launch_tc_one<FMT_FP8>(a, grid, st);
   }
+}
+
+// The K pieces of a split dense GEMM: y = bf16(part[0] + part[1] + ...), the pieces in K order.
+__global__ void __launch_bounds__(256) ksplit_reduce_kernel(const float* __restrict__ part, int ksplit, int64_t mn,
+                                                            __nv_bfloat16* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n4 = mn / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = reinterpret_cast<const float4*>(part)[i];
+    for (int ks = 1; ks < ksplit; ++ks) {
+      const float4 w = reinterpret_cast<const float4*>(part + (size_t)ks * mn)[i];
+      v.x += w.x;
+      v.y += w.y;
+      v.z += w.z;
+      v.w += w.w;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    reinterpret_cast<uint2*>(y)[i] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+  }
+}
+
+cudaError_t launch_ksplit_reduce(const float* part, int ksplit, int64_t mn, __nv_bfloat16* y, cudaStream_t st) {
+  const int64_t n4 = mn / 4;
+  int64_t grid = (n4 + 255) / 256;
+  if (grid > 4 * num_sms()) grid = 4 * num_sms();
+  if (grid < 1) grid = 1;
+  return launch_pdl(ksplit_reduce_kernel, dim3((unsigned)grid), dim3(256), 0, st, part, ksplit, mn, y);
 }
 
 // ── TC layout: canonical -> [N/128 row-blocks][K/128 stages][...] ─────────────────────────────────

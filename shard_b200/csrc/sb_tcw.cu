@@ -1,38 +1,36 @@
-// Grouped expert GEMM at prefill widths on the tensor cores: 16-bit operands and the whole K reduced
-// in TMEM, so each pass is read back once (the verify-width kernel, sb_tc.cu, reads back per stage).
+// Grouped expert GEMM at prefill widths on the tensor cores (tcx_kernel): 16-bit operands and the
+// whole K reduced in TMEM, so each pass is read back once (the verify-width kernel, sb_tc.cu, reads
+// back per stage).
 //
-// Items are (pass, 128-row block) as in sb_tc.cu, with passes of up to WN = 128 tokens. Operands per
-// 64-K sub-stage:
-//   A  the weight tile, dequantised by the worker warps from a compact staging copy (TMA, 64-byte
-//      swizzled, so that thread r reading row r is free of bank conflicts) into tensor memory
-//      (tcgen05.st; the MMA reads A from TMEM, so the 16-bit tile never passes through shared
-//      memory):
+// Items are (pass, pair of 128-row blocks) over the same pass table as sb_tc.cu, with passes of up to
+// WN = 128 tokens. The MMA is tcgen05.mma kind::f16 with the pass's tokens as its M side (128 TMEM
+// lanes, one token per lane) and the item's 256 weight rows as its N side, K = 16 per instruction.
+// Operands per 64-K sub-stage:
+//   weights (B, shared memory)  a producer warp copies each stage in compact form (TMA, swizzled so
+//      that thread r reading row r is free of bank conflicts) with its scales into a staging ring;
+//      8 converter warps, one thread per weight row, dequantise it into a 128B-swizzled K-major
+//      16-bit tile:
 //        NVFP4  e2m1 x its e4m3 scale (per 16) in f16: exact (<= 6 significant bits, 2^-10..2688);
 //               the fp32 tensor scale is applied in the epilogue;
 //        FP8    e4m3 x its 128x128 block scale / c_A in f16, c_A = 16 x the item's first block
 //               scale (a power of two for ue8m0 scales): exact while the row block's scales stay
 //               within 2^+-11 of it; c_A is applied in the epilogue;
 //        MXFP4  e2m1 x its e8m0 scale (per 32) in bf16: exact (e8m0 exceeds the f16 range).
-//   B  the pass's activation rows from an expert-ordered activation matrix, copied by a loader warp
-//      with cp.async (the LSU path: the TMA engine carries only the weight stream) into the
-//      128-byte-swizzled K-major layout: dequant(act_quant(v)) = e4m3 x scale, divided by a power of two
-//      c_B per row (f16 rows: c_B = 2^ceil(log2(max scale)) / 128, so |values| <= 448 * 128) or
-//      as is (bf16 rows, MXFP4 experts). With power-of-two activation scales (ue8m0) the values
-//      are exact; with fp32 scales they are carried as two planes, hi = round(v) and
-//      lo = round(v - hi), and each sub-stage multiplies A by both into the same accumulator.
-// tcgen05.mma kind::f16 (M=128, N = tokens rounded up to 16, K=16) accumulates the whole K into one
-// of two TMEM accumulators (double-buffered across passes); the products are exact and the sum is
-// fp32, the reference's dequant-then-fp32-matmul up to summation order. The epilogue scales the
-// accumulator by the powers of two c_A c_B (exact) and the NVFP4 tensor scale.
+//   tokens (A, shared memory)  a loader warp bulk-copies the pass's rows of the padded chunk-major
+//      activation matrix (wide_x / wide_h kernels): dequant(act_quant(v)) = e4m3 x scale divided by a
+//      power of two c_B per row (f16), exact for power-of-two activation scales; fp32 scales are
+//      carried as two planes, hi = round(v) and lo = round(v - hi), both multiplied into the same
+//      accumulator; K3-mode bf16 activations are copied as they are (bf16, c_B = 1).
+// Two TMEM accumulators (128 lanes x 256 columns each) alternate across passes. The products are
+// exact and the sum is fp32, the reference's dequant-then-fp32-matmul up to summation order. The
+// epilogue (the converter warps; lane = token) scales by the powers of two c_A c_B and the NVFP4
+// tensor scale; W13 pairs each gate column with its up column inside one thread (SwiGLU or situ),
+// W2 writes o rows.
 //
-// One CTA per SM (its shared memory holds deep rings), persistent over the items. Roles (352
-// threads): warps 0-7 convert, two threads per weight row r (each one 64-K half of every 128-K
-// stage), handing the A ring over in 256-K super-stages (one mbarrier round trip per 256 K), and
-// after a pass's last super-stage run its epilogue (TMEM lanes = rows, the two halves taking
-// alternate 32-column chunks); warp 8 weight producer (TMA / bulk copies); warp 9 MMA issuer
-// (allocates TMEM); warp 10 B loader. The B ring's 16 KB slots hold the B tiles of 4, 2 or 1 sub-stages (passes of <= 32, <= 64,
-// <= 128 tokens), so narrow passes keep many sub-stages of activations in flight. Every wait is
-// bounded; on timeout the CTA records an error and winds down.
+// One CTA per SM (352 threads), persistent over the items: warps 0-7 convert and run the epilogue,
+// warp 8 weight producer, warp 9 MMA issuer (allocates TMEM), warp 10 token loader. The token ring's
+// 16 KB slots hold the tiles of 4, 2 or 1 sub-stages (passes of <= 32, <= 64, <= 128 tokens). Every
+// wait is bounded; on timeout the CTA records an error and winds down.
 #include <cudaTypedefs.h>
 
 #include "sb_launch.h"
@@ -43,39 +41,14 @@ namespace tcw {
 
 using namespace tc5;
 
-constexpr int NWORK = 8;                // converter / epilogue warps: 2 threads per weight row
-constexpr int NTHREADS = 32 * (NWORK + 3);
-constexpr int PRODUCER_WARP = NWORK;
-constexpr int MMA_WARP = NWORK + 1;
-constexpr int BLOAD_WARP = NWORK + 2;
-constexpr int BLAG = 3;                 // B slots the loader keeps in flight before releasing one
-constexpr int WN = TC_WIDE_PASS;        // tokens (B rows) per pass
-constexpr int SC = 12;                  // staging ring (compact weight stage + scales)
-constexpr int SAR = 2;                  // A slots in TMEM: one 256-K super-stage each (128 columns)
-constexpr int SBR = 6;                  // B slots of 16 KB: the B tiles of 1, 2 or 4 sub-stages
+constexpr int NWORK = 8;                // converter / epilogue warps: one thread per weight row
+constexpr int WN = TC_WIDE_PASS;        // tokens per pass
 constexpr int STG_W = 8192;             // fp4: 128 rows x 64 B (128 K); FP8: 128 rows x 64 B (64 K)
 constexpr int STG_S = 1024;             // NVFP4 [128][8 B], MXFP4 [128][4 B], FP8 16 B
-constexpr int B_BYTES = WN * 128;       // WN rows x 64 16-bit values
+constexpr int B_BYTES = WN * 128;       // a token tile slot: WN rows x 64 16-bit values
 constexpr int BOX_ROWS = 32;
 constexpr int BOX_BYTES = BOX_ROWS * 128;
-constexpr int A_COL0 = 2 * WN;          // TMEM: accumulators in columns 0 .. 2 WN, then the A slots
-constexpr int A_COLS = 128;             // 256 K of 16-bit values, two per column
-constexpr int SUP = 4;                  // 64-K sub-stages per super-stage (the A ring's hand-off unit)
-constexpr int TMEM_COLS = A_COL0 + SAR * A_COLS;
-static_assert(TMEM_COLS == 512, "TMEM columns of one CTA per SM");
 constexpr uint32_t WAIT_LIMIT = 1u << 16;
-
-struct Smem {
-  uint8_t B[SBR][B_BYTES];              // 1024-aligned (128B swizzle atoms)
-  uint8_t stg[SC][STG_W + STG_S];       // each 1024-aligned (64B swizzle atoms)
-  __nv_bfloat16 xchg[2][64][34];        // W13 epilogue: the up rows of each column half
-  uint64_t sfull[SC], sempty[SC], afull[SAR], aempty[SAR], bfull[SBR], bempty[SBR], accfull[2], accempty[2];
-  uint64_t drain;
-  uint32_t tmem_base;
-  int abort;
-};
-constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory of one CTA per SM");
 
 struct WideArgs {
   CUtensorMap map_w4;       // fp4 routed bank as bytes [rows/2][128]: box 128 x 64, 128-byte swizzle
@@ -154,7 +127,7 @@ __device__ __forceinline__ uint4 stg_chunk4(const uint8_t* stg, int r, int c) {
   return *reinterpret_cast<const uint4*>(stg + q * 128 + ((cc ^ (q & 7)) << 4));
 }
 
-// Thread (row r, half hh) converts its row's values of one staging stage into TMEM columns (two
+// Thread (row r, half hh) converts its row's values of one staging stage into 32-bit words (two
 // 16-bit values each, K ascending). fp4 stages hold 128 K: the thread takes sub-stage hh
 // (K 64hh .. 64hh+63, staging chunks 2hh, 2hh+1) -> 32 columns.
 //   NVFP4: e2m1 x e4m3 group scale (scale bytes 4hh .. 4hh+3 of the row) in f16
@@ -226,401 +199,8 @@ __device__ __forceinline__ BGeom bgeom(int pc, int nb) {
   return b;
 }
 
-template <int FMT_R>
-__global__ void __launch_bounds__(NTHREADS, 1) tcw_kernel(const __grid_constant__ WideArgs wa) {
-  const GroupedArgs& a = wa.g;
-  extern __shared__ uint8_t dyn_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~(uintptr_t)1023);
-  int* err = a.err != nullptr ? a.err : &g_tcw_dense_err;
-  volatile int* abort_flag = &sm.abort;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
 
-  if (tid == 0) {
-    for (int s = 0; s < SC; ++s) {
-      mbar_init(smem_addr(&sm.sfull[s]), 1);
-      mbar_init(smem_addr(&sm.sempty[s]), NWORK);
-    }
-    for (int s = 0; s < SAR; ++s) {
-      mbar_init(smem_addr(&sm.afull[s]), NWORK);
-      mbar_init(smem_addr(&sm.aempty[s]), 1);
-    }
-    for (int s = 0; s < SBR; ++s) {
-      mbar_init(smem_addr(&sm.bfull[s]), 1);
-      mbar_init(smem_addr(&sm.bempty[s]), 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_addr(&sm.accfull[s]), 1);
-      mbar_init(smem_addr(&sm.accempty[s]), NWORK);
-    }
-    mbar_init(smem_addr(&sm.drain), 1);
-    sm.abort = 0;
-    mbar_init_fence();
-  }
-  if (warp == MMA_WARP) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(&sm.tmem_base)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
-  }
-  fence_before();
-  __syncthreads();
-  fence_after();
-  const uint32_t tbase = sm.tmem_base;
-  // everything above touched only this CTA's shared memory and TMEM; the inputs come after
-  pdl_wait();
-  pdl_trigger();
-
-  const int P = a.m * a.topk;
-  const int K = a.k;
-  const int nsub = K / 64;
-  const int nst = K / 128;
-  const int nrb = a.n_rows / 128;
-  const int nb = wa.b_split ? 2 : 1;              // B tiles per sub-stage (hi, lo)
-  const int wn = wa.b_split ? WN / 2 : WN;        // tokens per pass
-  const int n_pass = (a.has_shared ? wa.plan.n_sh_pass : 0) + wa.plan.pass_off[*a.n_active];
-  const int n_items = n_pass * nrb;
-  const bool w13 = a.mode == MODE_W13;
-  // shared expert items are FP8; f16 operands for every format but MXFP4
-  auto item_fmt = [&](const Item& it) { return it.shared ? FMT_FP8 : FMT_R; };
-  auto pass_tokens = [&](const Item& it) { return min(wn, it.cnt - it.pb); };
-  auto wait = [&](uint32_t bar, uint32_t parity) { return wait_bounded(abort_flag, err, bar, parity, WAIT_LIMIT); };
-  auto warp_wait = [&](uint32_t bar, uint32_t parity) { return __all_sync(0xffffffffu, wait(bar, parity)); };
-
-  if (warp == PRODUCER_WARP) {
-    // weight stages (TMA) and their scales (bulk copies)
-    if (elect_one()) {
-      if (wa.use_w4) prefetch_map(&wa.map_w4);
-      if (wa.use_w8) prefetch_map(&wa.map_w8);
-      if (wa.use_w8_sh) prefetch_map(&wa.map_w8_sh);
-    }
-    __syncwarp();
-    uint32_t c = 0;   // compact stages (staging ring)
-    bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
-      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(err) != 0)) {
-        *abort_flag = 1;
-        break;
-      }
-      const int fmt = item_fmt(it);
-      const bool fp4 = fmt != FMT_FP8;
-      const WeightSet& ws = it.shared ? a.shared : a.routed;
-      const uint32_t sb = fmt == FMT_NVFP4 ? 1024u : (fmt == FMT_MXFP4 ? 512u : 16u);
-      const uint8_t* sbase = ws.s + (it.shared ? 0 : (size_t)it.expert * ws.s_stride) + (size_t)it.rb * nst * sb;
-      const int row0 = ((it.shared ? 0 : it.expert) * nrb + it.rb) * nst * 128;   // bank row of stage 0
-      const CUtensorMap* mapw = fp4 ? &wa.map_w4 : (it.shared ? &wa.map_w8_sh : &wa.map_w8);
-      const int nstg = fp4 ? nst : nsub;
-      for (int st = 0; st < nstg; ++st, ++c) {
-        const uint32_t s = c % SC;
-        if (!warp_wait(smem_addr(&sm.sempty[s]), ((c / SC) & 1u) ^ 1u)) {
-          ok = false;
-          break;
-        }
-        if (elect_one()) {
-          const uint32_t bar = smem_addr(&sm.sfull[s]);
-          mbar_expect_tx(bar, 8192u + sb);
-          if (fp4)
-            tma_load_2d(smem_addr(sm.stg[s]), mapw, 0, (row0 >> 1) + st * 64, bar);
-          else
-            tma_load_2d(smem_addr(sm.stg[s]), mapw, (st & 1) * 64, row0 + (st >> 1) * 128, bar);
-          bulk_g2s(smem_addr(sm.stg[s] + STG_W), sbase + (size_t)(fp4 ? st : st >> 1) * sb, sb, bar);
-        }
-        __syncwarp();
-      }
-    }
-    // copies still in flight (only when a wait gave up) land before the CTA exits
-    for (uint32_t h = c > (uint32_t)SC ? c - SC : 0; h < c; ++h)
-      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-        if (mbar_try_wait(smem_addr(&sm.sfull[h % SC]), (h / SC) & 1u)) break;
-  } else if (warp == BLOAD_WARP) {
-    // B slots: one bulk copy per sub-stage and plane. In the chunk-major padded matrix a pass's rows
-    // of one 64-K chunk are one contiguous run of 128-byte rows, already 128B-swizzled by row index;
-    // the pass starts at a multiple of 8 rows, so the copy lands in exactly the layout the MMA's
-    // descriptor reads (row t at 128 t, 16-byte chunk k at (k ^ (t & 7)) * 16). Only the pass's
-    // rows (rounded up to 8) are copied: the MMA's rows beyond them feed output columns the
-    // epilogue never reads.
-    uint32_t gb = 0;
-    bool ok = true;
-    const size_t plane = (size_t)(K / 64) * (size_t)wa.r_pad * 128;
-    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
-      const int pc = pass_tokens(it);
-      const BGeom bg = bgeom(pc, nb);
-      const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
-      const uint32_t bytes = (uint32_t)((pc + 7) & ~7) * 128u;
-      for (int i = 0; i < nsub; i += bg.spb, ++gb) {
-        const uint32_t sbf = gb % SBR;
-        if (!warp_wait(smem_addr(&sm.bempty[sbf]), ((gb / SBR) & 1u) ^ 1u)) {
-          ok = false;
-          break;
-        }
-        const int cnt = min(bg.spb, nsub - i);
-        if (elect_one()) {
-          const uint32_t bar = smem_addr(&sm.bfull[sbf]);
-          mbar_expect_tx(bar, (uint32_t)(cnt * nb) * bytes);
-          for (int j = 0; j < cnt; ++j)
-            for (int h = 0; h < nb; ++h)
-              bulk_g2s(smem_addr(sm.B[sbf] + (j * nb + h) * bg.nboxp * BOX_BYTES),
-                       wa.bmat + h * plane + ((size_t)(i + j) * wa.r_pad + brow0) * 128, bytes, bar);
-        }
-        __syncwarp();
-      }
-    }
-    // copies still in flight (only when a wait gave up) land before the CTA exits
-    for (uint32_t h = gb > (uint32_t)SBR ? gb - SBR : 0; h < gb; ++h)
-      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-        if (mbar_try_wait(smem_addr(&sm.bfull[h % SBR]), (h / SBR) & 1u)) break;
-  } else if (warp == MMA_WARP) {
-    // One thread issues everything (waits, MMAs, commits are single-thread operations); the other
-    // lanes idle until the CTA's final barrier. A tcgen05 fence follows each wait, and only waits.
-    if (lane == 0) {
-      uint32_t g = 0, gb = 0, np = 0;  // staging stages (A slots), B slots, passes (accumulator buffers)
-      bool ok = true;
-      Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++np) {
-        const Item it = nxt;
-        if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
-        const int pc = pass_tokens(it);
-        const BGeom bg = bgeom(pc, nb);
-        const uint32_t n = (uint32_t)((pc + 15) & ~15);
-        const uint32_t id = item_fmt(it) == FMT_MXFP4 ? idesc_bf16(n) : idesc_f16(n);
-        const uint32_t buf = np & 1u;
-        const uint32_t tacc = tbase + buf * WN;
-        const uint32_t tile = (uint32_t)(nb * bg.nboxp * BOX_BYTES);   // one sub-stage's B tiles
-        if (!wait(smem_addr(&sm.accempty[buf]), ((np >> 1) & 1u) ^ 1u)) break;
-        int i = 0;   // sub-stage
-        const int nsup = (nsub + SUP - 1) / SUP;
-        for (int ss = 0; ss < nsup && ok; ++ss, ++g) {
-          const uint32_t sa = g % SAR;
-          const uint32_t ta = tbase + A_COL0 + sa * A_COLS;
-          const int nsb = min(SUP, nsub - ss * SUP);
-          if (!wait(smem_addr(&sm.afull[sa]), (g / SAR) & 1u)) {
-            ok = false;
-            break;
-          }
-          bool synced = true;   // a wait since the last tcgen05 fence
-          for (int u = 0; u < nsb; ++u, ++i) {
-            const uint32_t sbf = gb % SBR;
-            const int j = i & (bg.spb - 1);
-            if (j == 0) {
-              if (!wait(smem_addr(&sm.bfull[sbf]), (gb / SBR) & 1u)) {
-                ok = false;
-                break;
-              }
-              synced = true;
-            }
-            if (synced) {
-              fence_after();
-              synced = false;
-            }
-            const bool last_in_slot = j == bg.spb - 1 || i == nsub - 1;
-            for (int h = 0; h < nb; ++h) {
-              // K advances 16 values = 32 bytes = 2 in the descriptor's start-address field
-              const uint64_t bd = sdesc(smem_addr(sm.B[sbf]) + (uint32_t)j * tile + (uint32_t)h * (tile / nb));
-#pragma unroll
-              for (int k = 0; k < 4; ++k)
-                mma_f16_ts(tacc, ta + 32 * u + 8 * k, bd + 2 * k, id, (i > 0 || h > 0 || k > 0) ? 1u : 0u);
-            }
-            if (last_in_slot) {
-              commit(smem_addr(&sm.bempty[sbf]));
-              ++gb;
-            }
-          }
-          if (!ok) break;
-          commit(smem_addr(&sm.aempty[sa]));
-          if (ss == nsup - 1) commit(smem_addr(&sm.accfull[buf]));
-        }
-      }
-      commit(smem_addr(&sm.drain));
-      for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-        if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
-    }
-    __syncwarp();
-  } else {
-    // ── convert + epilogue (warps 0-7): thread (row r = TMEM lane r, half hh) ──
-    const int r = tid & 127, hh = tid >> 7;
-    uint32_t g = 0, c = 0, np = 0;
-    bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrb, wn) : Item{};
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++np) {
-      const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrb, wn);
-      const int fmt = item_fmt(it);
-      const bool fp4 = fmt != FMT_FP8;
-      const WeightSet& ws = it.shared ? a.shared : a.routed;
-      const int pc = pass_tokens(it);
-      const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
-      // this half's column chunks (32 tokens each, j = 2jj + hh): lane t holds token 32j + t's
-      // output row, weight and the power of two its B row was divided by
-      int my_orow[WN / 64];
-      float my_wgt[WN / 64], my_cb[WN / 64];
-#pragma unroll
-      for (int jj = 0; jj < WN / 64; ++jj) {
-        my_orow[jj] = 0;
-        my_wgt[jj] = 1.f;
-        my_cb[jj] = 1.f;
-        const int t = 32 * (2 * jj + hh) + lane;
-        if (t < pc) {
-          const int i = it.pb + t;
-          my_cb[jj] = wa.cvec[brow0 + t];
-          if (w13) {
-            my_orow[jj] = brow0 + t;   // h rows live in the padded row space of the W2 B operand
-            if (!it.shared) {
-              const int qp = it.base + i;
-              my_wgt[jj] = a.topk_w[(size_t)a.pair_tok[qp] * a.topk + a.pair_slot[qp]];
-            }
-          } else if (it.shared) {
-            my_orow[jj] = P + i;
-          } else {
-            const int qp = it.base + i;
-            my_orow[jj] = a.pair_tok[qp] * a.topk + a.pair_slot[qp];
-          }
-        }
-      }
-      float ts = 1.f;
-      if (fmt == FMT_NVFP4 && ws.ts != nullptr) {
-        const float* tsp = ws.ts + (it.shared ? 0 : (size_t)it.expert * ws.ts_stride);
-        ts = (w13 && r >= 64) ? tsp[1] : tsp[0];
-      }
-      float ca = 1.f, ica = 1.f;   // FP8: c_A and its reciprocal, from the item's first block scale
-      const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
-      const int nsup = (nsub + SUP - 1) / SUP;
-      // convert the pass's weights into the TMEM A ring, one 256-K super-stage per hand-off: its 2 fp4
-      // (or 4 FP8) staging stages, each released as soon as it is converted
-      for (int ss = 0; ss < nsup; ++ss, ++g) {
-        const uint32_t sa = g % SAR;
-        const int nsb = min(SUP, nsub - ss * SUP);            // sub-stages in this super-stage
-        const int nq = fp4 ? (nsb + 1) / 2 : nsb;              // its staging stages
-        if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.aempty[sa]), ((g / SAR) & 1u) ^ 1u));
-        if (ok) fence_after();
-        const uint32_t ta = tbase + lanes + A_COL0 + sa * A_COLS;
-        for (int q = 0; q < nq; ++q, ++c) {
-          const uint32_t s = c % SC;
-          if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
-          if (!ok) continue;
-          const uint8_t* stg = sm.stg[s];
-          if (fmt == FMT_FP8) {
-            const float sw = reinterpret_cast<const float*>(stg + STG_W)[w13 && r >= 64 ? 1 : 0];
-            if (ss == 0 && q == 0) {
-              ca = sw > 0.f ? sw * 16.f : 1.f;
-              ica = 1.f / ca;
-            }
-            uint32_t v[16];
-            convert_fp8(stg, r, hh, f16_splat(sw * ica), v);
-            st16(ta + 32 * q + 16 * hh, v);
-          } else {
-            uint32_t v[32];
-            if (fmt == FMT_NVFP4)
-              convert_nvfp4(stg, r, hh, v);
-            else
-              convert_mxfp4(stg, r, hh, v);
-            st32(ta + 64 * q + 32 * hh, v);
-          }
-          __syncwarp();
-          if (lane == 0) arrive(smem_addr(&sm.sempty[s]));   // the stage is in registers / TMEM
-        }
-        if (!ok) continue;
-        st_wait();
-        fence_before();
-        __syncwarp();
-        if (lane == 0) arrive(smem_addr(&sm.afull[sa]));
-      }
-      // epilogue: this pass's accumulator -> h (W13, SwiGLU) or o (W2); each half of the workers
-      // takes every other 32-column chunk
-      const uint32_t buf = np & 1u;
-      if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
-      if (bar_any(1, 32 * NWORK, !ok || *abort_flag)) break;
-      fence_after();
-      const uint32_t taddr = tbase + ((uint32_t)((warp & 3) * 32) << 16) + buf * WN;
-      const int I = a.n_rows / 2;
-      const float cab = ca * ts;
-#pragma unroll
-      for (int jj = 0; jj < WN / 64; ++jj) {
-        const int j = 2 * jj + hh;
-        if (32 * j >= pc) break;                       // uniform across this half's warps
-        uint32_t d[32];
-        ld32(taddr + 32 * j, d);
-        ld_wait();
-        if (w13) {
-          // gate row i = r and up row i + 64 of intermediate index i each compute SwiGLU for 16 of
-          // the chunk's 32 tokens (gate rows tokens 0-15, up rows 16-31), exchanging the other half
-          // of their values through shared memory (bf16: the rounding point of both GEMM outputs)
-          const int i = r & 63;
-          const float lim = a.swiglu_limit;
-          // SwiGLU of token tt from this thread's value `own` and the partner's `other`
-          auto swiglu = [&](int tt, float own, float other, bool up) {
-            const int orow = __shfl_sync(0xffffffffu, my_orow[jj], tt);
-            const float wgt = __shfl_sync(0xffffffffu, my_wgt[jj], tt);
-            if (32 * j + tt < pc) {
-              float gv = up ? other : own, uv = up ? own : other;
-              if (lim > 0.f) {
-                uv = fminf(fmaxf(uv, -lim), lim);
-                gv = fminf(gv, lim);
-              }
-              float hv = silu(gv) * uv;
-              if (!it.shared) hv = wgt * hv;
-              a.hbf[(size_t)orow * I + it.rb * 64 + i] = __float2bfloat16_rn(hv);
-            }
-          };
-          if (r >= 64) {   // up rows (warp-uniform): park tokens 0-15, compute 16-31
-#pragma unroll
-            for (int t = 0; t < 16; ++t)
-              sm.xchg[hh][i][t] =
-                  __float2bfloat16_rn(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab);
-            bar_sync(2 + hh, 128);
-#pragma unroll
-            for (int t = 16; t < 32; ++t)
-              swiglu(t, bf16_round(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab),
-                     __bfloat162float(sm.xchg[hh][i][t]), true);
-          } else {         // gate rows: park tokens 16-31, compute 0-15
-#pragma unroll
-            for (int t = 16; t < 32; ++t)
-              sm.xchg[hh][i][t] =
-                  __float2bfloat16_rn(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab);
-            bar_sync(2 + hh, 128);
-#pragma unroll
-            for (int t = 0; t < 16; ++t)
-              swiglu(t, bf16_round(__uint_as_float(d[t]) * __shfl_sync(0xffffffffu, my_cb[jj], t) * cab),
-                     __bfloat162float(sm.xchg[hh][i][t]), false);
-          }
-          bar_sync(2 + hh, 128);
-        } else {
-          const int n0 = it.rb * 128;
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const int orow = __shfl_sync(0xffffffffu, my_orow[jj], t);
-            const float cb = __shfl_sync(0xffffffffu, my_cb[jj], t);
-            if (32 * j + t < pc)
-              a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(__uint_as_float(d[t]) * cb * cab);
-          }
-        }
-      }
-      fence_before();
-      __syncwarp();
-      if (lane == 0) arrive(smem_addr(&sm.accempty[buf]));
-    }
-  }
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if (warp == MMA_WARP)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(TMEM_COLS));
-}
-
-// ── the prefill kernel with the operands swapped (the default build) ──
-// tcx_kernel computes the same items with the pass's tokens as the MMA's M side (128, TMEM lanes) and
-// 256 weight rows — two 128-row blocks — as its N side: one tcgen05.mma covers twice the weight rows
-// of tcw_kernel's (the MMA issue rate is what bounds both), and an accumulator lane holds one
-// token's outputs, so the W13 epilogue pairs a gate column with its up column inside one thread and
-// writes 64-byte runs of h. The weights are converted into shared memory (the B operand must be
-// there); the token tiles come by bulk copy. Build with -DSB_WIDE_SWAP=0 for tcw_kernel.
-#ifndef SB_WIDE_SWAP
-#define SB_WIDE_SWAP 1
-#endif
-#if SB_WIDE_SWAP
+// ── the prefill kernel ──
 namespace x {
 constexpr int NTHREADS = 32 * (NWORK + 3);
 constexpr int PRODUCER_WARP = NWORK, MMA_WARP = NWORK + 1, TLOAD_WARP = NWORK + 2;
@@ -761,7 +341,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
       for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
         if (mbar_try_wait(smem_addr(&sm.sfull[h % SC]), (h / SC) & 1u)) break;
   } else if (warp == TLOAD_WARP) {
-    // token tiles: one bulk copy per sub-stage and plane (as tcw_kernel's B loader)
+    // token tiles: one bulk copy per sub-stage and plane
     uint32_t gt = 0;
     bool ok = true;
     const size_t plane = (size_t)(K / 64) * (size_t)wa.r_pad * 128;
@@ -853,63 +433,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pc = pass_tokens(it);
       const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
-      float ica = 1.f;
-      if (fmt != FMT_FP8) sm.ca[t] = 1.f;
-      const int nstg = fp4 ? nst : nsub;
-      for (int st = 0; st < nstg; ++st, ++c) {
-        const uint32_t s = c % SC;
-        if (ok) ok = __all_sync(0xffffffffu, cwait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
-        const uint8_t* stg = sm.stg[s] + hb * STG_RB;
-        uint32_t s2 = 0;
-        if (ok && fmt == FMT_FP8) {
-          const float sw = reinterpret_cast<const float*>(stg + STG_W)[w13 && r >= 64 ? 1 : 0];
-          if (st == 0) {
-            const float ca = sw > 0.f ? sw * 16.f : 1.f;
-            ica = 1.f / ca;
-            sm.ca[t] = ca;
-          }
-          s2 = f16_splat(sw * ica);
-        }
-        for (int u = 0; u < (fp4 ? 2 : 1); ++u, ++gw) {
-          const uint32_t sws = gw % SW;
-          if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.wempty[sws]), ((gw / SW) & 1u) ^ 1u));
-          if (!ok) continue;
-          uint32_t o[32];
-          if (fmt == FMT_FP8) {
-            uint32_t o0[16], o1[16];
-            convert_fp8(stg, r, 0, s2, o0);
-            convert_fp8(stg, r, 1, s2, o1);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              o[e] = o0[e];
-              o[16 + e] = o1[e];
-            }
-          } else if (fmt == FMT_NVFP4) {
-            convert_nvfp4(stg, r, u, o);
-          } else {
-            convert_mxfp4(stg, r, u, o);
-          }
-          uint8_t* dst = sm.W[sws] + t * 128;
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            *reinterpret_cast<uint4*>(dst + ((k ^ (t & 7)) << 4)) = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) arrive(smem_addr(&sm.wfull[sws]));
-        }
-        __syncwarp();
-        if (ok && lane == 0) arrive(smem_addr(&sm.sempty[s]));
-      }
-      // epilogue: TMEM lane = token (32 (warp & 3) + lane), the warp half hh takes row block 2 rb + hh
-      const uint32_t buf = np & 1u;
-      if (ok) ok = __all_sync(0xffffffffu, cwait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
-      if (bar_any(1, 32 * NWORK, !ok || *abort_flag)) break;
-      fence_after();
+      // the epilogue's per-token values (lane = token (32 (warp & 3) + lane), the warp half hh takes
+      // row block 2 rb + hh), loaded now so that their latency hides behind the item's conversion
       const int hh = warp >> 2;
       const int tok = (warp & 3) * 32 + lane;
       const bool valid = tok < pc;
       const int rb = 2 * it.rb + hh;
-      const uint32_t taddr = tbase + ((uint32_t)((warp & 3) * 32) << 16) + buf * ROWS + 128 * hh;
       float cb = 1.f, wgt = 1.f;
       int orow = 0;
       if (valid) {
@@ -934,6 +463,62 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
         ts0 = tsp[0];
         ts1 = w13 ? tsp[1] : tsp[0];
       }
+      float ica = 1.f;
+      if (fmt != FMT_FP8) sm.ca[t] = 1.f;
+      const int nstg = fp4 ? nst : nsub;
+      for (int st = 0; st < nstg; ++st, ++c) {
+        const uint32_t s = c % SC;
+        if (ok) ok = __all_sync(0xffffffffu, cwait(smem_addr(&sm.sfull[s]), (c / SC) & 1u));
+        const uint8_t* stg = sm.stg[s] + hb * STG_RB;
+        uint32_t s2 = 0;
+        if (ok && fmt == FMT_FP8) {
+          const float sw = reinterpret_cast<const float*>(stg + STG_W)[w13 && r >= 64 ? 1 : 0];
+          if (st == 0) {
+            const float ca = sw > 0.f ? sw * 16.f : 1.f;
+            ica = 1.f / ca;
+            sm.ca[t] = ca;
+          }
+          s2 = f16_splat(sw * ica);
+        }
+        for (int u = 0; u < (fp4 ? 2 : 1); ++u, ++gw) {
+          const uint32_t sws = gw % SW;
+          // convert into registers first, then claim the tile slot: a slot is held only for the
+          // stores, which shortens its round trip through the MMA and back
+          uint32_t o[32];
+          if (!ok) continue;
+          if (fmt == FMT_FP8) {
+            uint32_t o0[16], o1[16];
+            convert_fp8(stg, r, 0, s2, o0);
+            convert_fp8(stg, r, 1, s2, o1);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              o[e] = o0[e];
+              o[16 + e] = o1[e];
+            }
+          } else if (fmt == FMT_NVFP4) {
+            convert_nvfp4(stg, r, u, o);
+          } else {
+            convert_mxfp4(stg, r, u, o);
+          }
+          ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.wempty[sws]), ((gw / SW) & 1u) ^ 1u));
+          if (!ok) continue;
+          uint8_t* dst = sm.W[sws] + t * 128;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<uint4*>(dst + ((k ^ (t & 7)) << 4)) = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) arrive(smem_addr(&sm.wfull[sws]));
+        }
+        __syncwarp();
+        if (ok && lane == 0) arrive(smem_addr(&sm.sempty[s]));
+      }
+      // epilogue: TMEM lane = token (32 (warp & 3) + lane), the warp half hh takes row block 2 rb + hh
+      const uint32_t buf = np & 1u;
+      if (ok) ok = __all_sync(0xffffffffu, cwait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
+      if (bar_any(1, 32 * NWORK, !ok || *abort_flag)) break;
+      fence_after();
+      const uint32_t taddr = tbase + ((uint32_t)((warp & 3) * 32) << 16) + buf * ROWS + 128 * hh;
       const float* cav = sm.ca + 128 * hh;
       if (w13) {
         const int I = a.n_rows / 2;
@@ -1008,7 +593,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(TMEM_COLS));
 }
 }  // namespace x
-#endif
 
 // ── activation matrices of the wide path (B operands), one warp per row ──
 // Row space: routed pair q of expert e at pbase(offsets[e], e) + (q - offsets[e]), the shared
@@ -1217,18 +801,8 @@ static cudaError_t launch_variant(const WideArgs& a, int grid, cudaStream_t st) 
 
 template <int F>
 static cudaError_t launch_one(const WideArgs& a, int grid, cudaStream_t st) {
-#if SB_WIDE_SWAP
   // the probing variant only when a test wait limit is set
   return a.g.wait_limit ? launch_variant<F, true>(a, grid, st) : launch_variant<F, false>(a, grid, st);
-#else
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tcw_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  return launch_pdl(tcw_kernel<F>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
-#endif
 }
 
 // K3 mode: the bf16 activations enter the expert GEMMs as they are (W4A16). Pair q's token row of x

@@ -68,9 +68,13 @@ def test_workspace_sizes_grow_with_m_and_reject_bad_layers():
     bad = _layer(hidden=100)
     assert L.sb_moe_workspace_bytes(ctypes.byref(bad), 16) == 0
     assert L.sb_qgemm_workspace_bytes(F.FMT_FP8, _lib.LAYOUT_FRAGMENT, 4096, 4096, 16) == 0
-    a = L.sb_qgemm_workspace_bytes(F.FMT_NVFP4, _lib.LAYOUT_TC, 4096, 4096, 8)
-    b = L.sb_qgemm_workspace_bytes(F.FMT_NVFP4, _lib.LAYOUT_TC, 4096, 4096, 9)
-    assert 0 < a < b   # 9 tokens need a second NVFP4 pass (8 tokens per pass)
+    # the dense GEMM's workspace serves every m' <= m (its narrow batches split K and add fp32
+    # partials), so it never shrinks as m grows
+    for fmt in (F.FMT_NVFP4, F.FMT_FP8):
+        for n, k in ((4096, 4096), (512, 7168), (32768, 1024)):
+            sizes = [L.sb_qgemm_workspace_bytes(fmt, _lib.LAYOUT_TC, n, k, m) for m in range(1, 100)]
+            assert sizes[0] > 0 and sizes == sorted(sizes), (fmt, n, k)
+            assert L.sb_qgemm_workspace_bytes(fmt, _lib.LAYOUT_TC, n, k, 1024) >= sizes[-1]
 
 
 def test_workspace_serves_every_smaller_batch_across_the_prefill_switch():
