@@ -314,11 +314,15 @@ static int qgemm_ksplit(int fmt, int64_t n, int64_t k, int64_t m, int* kstages) 
   return (nst + per - 1) / per;
 }
 
-// The fp32 partials of a split call, placed after the activation panel.
+// The pieces' fp32 partials ([pass x row block][piece][128 rows][16 tokens]) and their per-block
+// counters, placed after the activation panel.
 static size_t qgemm_part_bytes(int fmt, int64_t n, int64_t k, int64_t m) {
   int per = 0;
   const int ks = qgemm_ksplit(fmt, n, k, m, &per);
-  return ks > 1 ? align256((size_t)ks * (size_t)m * (size_t)n * sizeof(float)) : 0;
+  if (ks <= 1) return 0;
+  const int64_t pm = sb::tc_pass_max(fmt);
+  const int64_t blocks = ((m + pm - 1) / pm) * (n / 128);
+  return align256((size_t)blocks * ks * 2048 * sizeof(float)) + align256((size_t)blocks * sizeof(int32_t));
 }
 
 size_t sb_qgemm_workspace_bytes(int fmt, int layout, int64_t n, int64_t k, int64_t m) {
@@ -390,6 +394,16 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
     pa.xs = s;
     pa.bpanel = bpanel;
     pa.apanel = apanel;
+    if (ksplit > 1) {
+      // K pieces: partials after the panel, then the counters, zeroed by the panel kernel
+      const int64_t blocks = (int64_t)pa.n_sh_pass * (n / 128);
+      a.ksplit = ksplit;
+      a.kstages = kstages;
+      a.part = (float*)((uint8_t*)workspace + panel);
+      a.kcnt = (int*)((uint8_t*)workspace + panel + align256((size_t)blocks * ksplit * 2048 * sizeof(float)));
+      pa.kzero = a.kcnt;
+      pa.nkzero = (int)blocks;
+    }
     rc = cuda_check(sb::launch_tc_panel(pa, 1, st), "qgemm panel");
     if (rc) return rc;
     sb::TcPlan plan;
@@ -404,15 +418,7 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
     a.err = err;
     a.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
     a.items_per_expert = (int)(n / 128);
-    if (ksplit > 1) {
-      a.ksplit = ksplit;
-      a.kstages = kstages;
-      a.part = (float*)((uint8_t*)workspace + panel);
-      rc = cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert * ksplit, st), "qgemm");
-      if (rc) return rc;
-      return cuda_check(sb::launch_ksplit_reduce(a.part, ksplit, m * n, (__nv_bfloat16*)y, st), "qgemm reduce");
-    }
-    return cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert, st), "qgemm");
+    return cuda_check(sb::launch_tc_grouped(a, plan, plan.n_sh_pass * a.items_per_expert * ksplit, st), "qgemm");
   }
   a.items_per_expert = (int)((n + 255) / 256);
   return cuda_check(sb::launch_grouped(a, a.items_per_expert, 0, (cudaStream_t)stream), "qgemm");
@@ -690,7 +696,6 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     plan.pass_slot = w.pass_slot;
     plan.pass_pb = w.pass_pb;
     plan.n_sh_pass = w.n_sh_pass;
-    const int64_t R = P + m;
     const int split = (int)wide_planes(L) - 1;
     const int rbf = L->expert_fmt == SB_FMT_MXFP4 ? 1 : 0;   // MXFP4 experts take bf16 operands
     rc = k3 ? cuda_check(sb::launch_wide_x_raw(x, w.pair_tok, w.offsets, L->n_experts, (int)P, (int)H, w.wide_rows,

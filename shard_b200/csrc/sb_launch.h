@@ -87,9 +87,10 @@ struct GroupedArgs {
   int activation;      // ACT_SWIGLU (Expert.forward) or ACT_SITU (K3's SituAndMul)
   float act_beta, act_lbeta;  // situ: beta, and linear_beta (0: up is not transformed)
   int weight_after;    // 1: the routing weight is not applied to h (the combine applies it to o)
-  int ksplit;          // verify kernel, DENSE: K pieces per row block (<= 1: whole K per item)
+  int ksplit;          // verify kernel, DENSE: K pieces of each item (<= 1: none)
   int kstages;         // stages (128 K) per piece, a multiple of the kernel's unit of 2
-  float* part;         // ksplit > 1: fp32 partial outputs [ksplit][m][n_rows], reduced afterwards
+  float* part;         // ksplit > 1: fp32 partials [n_sh_pass * nrb][ksplit][128 rows][16]
+  int* kcnt;           // ksplit > 1: [n_sh_pass * nrb] pieces finished (zeroed by the panel kernel)
 };
 
 enum Activation { ACT_SWIGLU = 0, ACT_SITU = 1 };
@@ -124,6 +125,8 @@ struct PanelArgs {
   const int32_t* pair_tok;
   uint8_t* bpanel;
   float* apanel;
+  int* kzero;               // counters of the next grouped launch's K pieces, zeroed here (or NULL)
+  int nkzero;
 };
 
 __host__ __device__ inline int tc_pass_max(int fmt) { return fmt == 1 ? 8 : 16; }
@@ -152,8 +155,6 @@ cudaError_t launch_tile_scales(int fmt, int kind, const void* src, void* dst, in
 cudaError_t launch_selftest(float* out, cudaStream_t st);
 cudaError_t launch_tc_panel(const PanelArgs& a, int max_slots, cudaStream_t st);
 cudaError_t launch_tc_grouped(const GroupedArgs& a, const TcPlan& plan, int max_items, cudaStream_t st);
-// y bf16 [mn] = the fp32 sum over the ksplit pieces of part [ksplit][mn], pieces in order; mn % 4 == 0
-cudaError_t launch_ksplit_reduce(const float* part, int ksplit, int64_t mn, __nv_bfloat16* y, cudaStream_t st);
 // K3 mode (KimiSparseMoeBlock.moe_infer): the caller's routing into the workspace (ids checked against
 // the expert count: an id out of range sets *err to 1 and is replaced by 0), the bf16 activations
 // copied as they are into the prefill kernel's operand layouts, and the slot-order weighted combine.

@@ -66,6 +66,7 @@ struct Smem {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int klast;                    // K pieces: this CTA's piece was the last of its block to finish
   __nv_bfloat16 xchg[64][18];   // W13 epilogue: the up rows' bf16 values
 };
 constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
@@ -225,25 +226,34 @@ __device__ __forceinline__ bool workers_any(bool pred) {
 // matrix. Items are numbered pass-major: item = pass * nrb + rb, passes being the shared expert's
 // (or the dense matrix's) first, then each active expert's in slot order, so a hot expert's passes
 // run on different CTAs at about the same time and share its weight tiles through L2.
-// A dense GEMM whose row blocks are too few to occupy the GPU splits K: item = (pass, row block,
-// piece), piece ks covering stages [j0, j1); its fp32 partials are summed by a second kernel.
+// K pieces. The dense matrix's items (the shared-expert slot of the item space) may be split along
+// K into ksplit pieces of kstages stages: item = (pass, row block, piece), numbered piece-minor, any
+// routed items following unsplit. Each piece writes its fp32 partial accumulator to the workspace
+// and counts itself in; the last piece of a (pass, row block) to finish sums the pieces in K order
+// and runs the epilogue. This occupies the GPU when a dense matrix has few row blocks.
 struct Item {
   int shared, expert, rb, cnt, base, pb, pass;
-  int ks, j0, j1;
+  int ks, kn, j0, j1;   // piece ks of kn, stages [j0, j1)
 };
 
 template <int FMT_R>
 __device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan, int item, int nrb, int nst) {
   Item it;
+  it.ks = 0;
+  it.kn = 1;
+  it.j0 = 0;
+  it.j1 = nst;
   if (a.ksplit > 1) {
-    it.ks = item % a.ksplit;
-    item /= a.ksplit;
-    it.j0 = it.ks * a.kstages;
-    it.j1 = min(nst, it.j0 + a.kstages);
-  } else {
-    it.ks = 0;
-    it.j0 = 0;
-    it.j1 = nst;
+    const int nsh = plan.n_sh_pass * nrb;   // shared items before the split
+    if (item < nsh * a.ksplit) {
+      it.kn = a.ksplit;
+      it.ks = item % a.ksplit;
+      item /= a.ksplit;
+      it.j0 = it.ks * a.kstages;
+      it.j1 = min(nst, it.j0 + a.kstages);
+    } else {
+      item -= nsh * (a.ksplit - 1);
+    }
   }
   const int p = item / nrb;
   it.rb = item - p * nrb;
@@ -322,7 +332,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   const int nrb = a.n_rows / 128;
   const int n_pass = (a.has_shared ? ta.plan.n_sh_pass : 0) +
                      (a.mode == MODE_DENSE ? 0 : ta.plan.pass_off[*a.n_active]);
-  const int n_items = n_pass * nrb * (a.ksplit > 1 ? a.ksplit : 1);
+  const int n_items = n_pass * nrb + (a.ksplit > 1 && a.has_shared ? ta.plan.n_sh_pass * nrb * (a.ksplit - 1) : 0);
   const bool w13 = a.mode == MODE_W13;
   // the limit of the consumer-side waits (the MMA issuer's and the readback's); the producer's waits
   // for free slots and the final drains keep WAIT_LIMIT
@@ -739,7 +749,60 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         }
         // one decision for all workers: the W13 epilogue below synchronises them
         if (workers_any(!ok || aborted(sm))) stop = true;
-        if (!stop) {
+        bool merged_away = false;
+        if (!stop && it.kn > 1) {
+          // a K piece: publish the partial, count in; the last piece of the block sums all of them
+          // in K order (its own from registers) and goes on to the epilogue
+          const int kid = it.pass * nrb + it.rb;
+          float* blk = a.part + (size_t)kid * it.kn * 2048;
+          float4* mine = reinterpret_cast<float4*>(blk + (size_t)it.ks * 2048 + r * 16);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) mine[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+          __threadfence();
+          asm volatile("bar.sync 1, 128;\n" ::: "memory");
+          if (r == 0) {
+            const int prev = atomicAdd(a.kcnt + kid, 1);
+            sm.klast = prev == it.kn - 1;
+            if (sm.klast) a.kcnt[kid] = 0;   // ready for the next launch
+          }
+          asm volatile("bar.sync 1, 128;\n" ::: "memory");
+          if (sm.klast) {
+            __threadfence();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+            // this piece's own partial included, re-read; per float4 of the pass's tokens, eight
+            // pieces' loads in flight at a time, added in piece order
+            const int nq = pc <= 4 ? 1 : (pc <= 8 ? 2 : 4);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              if (v >= nq) continue;
+              float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int q0 = 0; q0 < it.kn; q0 += 8) {
+                float4 w[8];
+#pragma unroll
+                for (int dq = 0; dq < 8; ++dq)
+                  w[dq] = q0 + dq < it.kn
+                              ? __ldcg(reinterpret_cast<const float4*>(blk + (size_t)(q0 + dq) * 2048 + r * 16) + v)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int dq = 0; dq < 8; ++dq) {
+                  sum.x += w[dq].x;
+                  sum.y += w[dq].y;
+                  sum.z += w[dq].z;
+                  sum.w += w[dq].w;
+                }
+              }
+              acc[4 * v] = sum.x;
+              acc[4 * v + 1] = sum.y;
+              acc[4 * v + 2] = sum.z;
+              acc[4 * v + 3] = sum.w;
+            }
+          } else {
+            merged_away = true;
+          }
+          asm volatile("bar.sync 1, 128;\n" ::: "memory");   // klast is rewritten by the next piece
+        }
+        if (!stop && !merged_away) {
           if (w13) {
             // rows r < 64 are w1 (gate) rows, r >= 64 the matching w3 (up) rows
             const int I = a.n_rows / 2;
@@ -774,10 +837,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
             for (int t = 0; t < 16; ++t) {
               if (t < pc) {
                 const int orow = __shfl_sync(0xffffffffu, my_orow, t);
-                if (a.part != nullptr)
-                  a.part[((size_t)it.ks * a.m + orow) * a.n_rows + n0 + r] = acc[t] * ts;
-                else
-                  a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(acc[t] * ts);
+                a.o[(size_t)orow * a.n_rows + n0 + r] = __float2bfloat16_rn(acc[t] * ts);
               }
             }
           }
@@ -809,6 +869,8 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
   const int P = a.m * a.topk;
   pdl_wait();
   pdl_trigger();
+  if (a.kzero != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < a.nkzero; i += blockDim.x) a.kzero[i] = 0;
   int shared, cnt, base, pass0, nv;
   if (slot < a.has_shared) {
     shared = 1;
@@ -999,34 +1061,6 @@ cudaError_t launch_tc_grouped(const GroupedArgs& g, const TcPlan& plan, int max_
   }
 }
 
-// The K pieces of a split dense GEMM: y = bf16(part[0] + part[1] + ...), the pieces in K order.
-__global__ void __launch_bounds__(256) ksplit_reduce_kernel(const float* __restrict__ part, int ksplit, int64_t mn,
-                                                            __nv_bfloat16* __restrict__ y) {
-  pdl_wait();
-  pdl_trigger();
-  const int64_t n4 = mn / 4;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    float4 v = reinterpret_cast<const float4*>(part)[i];
-    for (int ks = 1; ks < ksplit; ++ks) {
-      const float4 w = reinterpret_cast<const float4*>(part + (size_t)ks * mn)[i];
-      v.x += w.x;
-      v.y += w.y;
-      v.z += w.z;
-      v.w += w.w;
-    }
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-    reinterpret_cast<uint2*>(y)[i] =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
-  }
-}
-
-cudaError_t launch_ksplit_reduce(const float* part, int ksplit, int64_t mn, __nv_bfloat16* y, cudaStream_t st) {
-  const int64_t n4 = mn / 4;
-  int64_t grid = (n4 + 255) / 256;
-  if (grid > 4 * num_sms()) grid = 4 * num_sms();
-  if (grid < 1) grid = 1;
-  return launch_pdl(ksplit_reduce_kernel, dim3((unsigned)grid), dim3(256), 0, st, part, ksplit, mn, y);
-}
 
 // ── TC layout: canonical -> [N/128 row-blocks][K/128 stages][...] ─────────────────────────────────
 // fp4 values   [128 rows][64 B]                  (128 K packed, low nibble first)
