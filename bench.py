@@ -373,7 +373,7 @@ def run_gpu(args, rank, world, local_rank):
             sweep = m_sweep(layers, cfg)
             if not N_EXPERTS:
                 sweep.update(cfg_sweep("c3", (1, 16, 64)))
-                sweep.update(cfg_sweep("c4", (256, 1024), modes=(0, 1, 2)))
+                sweep.update(cfg_sweep("c4", (256, 1024), modes=(0, 1, 2, 3)))
                 sweep.update(dense_sweep())
     clocks = clk.summary(set(range(world)) if world > 1 else {local_rank}) if rank == 0 else None
     cpu = None
@@ -517,7 +517,8 @@ def cfg_sweep(name, ms, reps=4, modes=(0,)):
     NVFP4 prefill) at each M: every timed forward gets fresh tokens and starts with L2 flushed
     (a 256 MB write outside the timed region), since a single layer's active experts can be close to
     the 126 MB L2 at small M. modes: expert-kernel choices timed (0 the default choice, keyed
-    `<name>_m<M>`; 1 the verify kernel and 2 the prefill kernel, keyed with a suffix)."""
+    `<name>_m<M>`; 1 the verify kernel, 2 the prefill kernel and 3 the hybrid dispatch, keyed with a
+    suffix)."""
     from shard_b200 import synth as S
     peak, _ = hbm_peak()
     cfg = S.CONFIGS[name]
@@ -549,7 +550,7 @@ def cfg_sweep(name, ms, reps=4, modes=(0,)):
         nb = algorithmic_bytes(cfg, [r_[0] for r_ in rows], m)
         g = sum(b[0] for b in nb) / sum(r_[1]["grouped"] for r_ in rows) / 1e9
         f = sum(b[1] for b in nb) / len(nb) / t_fwd / 1e9
-        key = f"{name}_m{m}" + {0: "", 1: "_verify", 2: "_prefill"}[mode]
+        key = f"{name}_m{m}" + {0: "", 1: "_verify", 2: "_prefill", 3: "_hybrid"}[mode]
         out[key] = {"tokens_per_s": m / t_fwd, "forward_us": t_fwd * 1e6, "grouped_gbs": g,
                     "grouped_frac": g / peak, "forward_gbs": f, "forward_frac": f / peak,
                     "l2": "flushed before each forward"}

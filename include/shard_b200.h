@@ -101,12 +101,19 @@ typedef struct sb_moe_layer {
    *              renormalize=False, m25_stage.py:301) */
   int32_t logits_bf16;
   int32_t no_renorm;
-  /* Which tensor-core grouped kernel runs the experts (SB_LAYOUT_TC only). SB_PREFILL_AUTO picks the
-   * prefill kernel (16-bit operands, the whole K in TMEM, passes of 128 tokens) when the batch routes
-   * at least 16 tokens per expert on average, else the verify kernel (per-stage readback, passes of
-   * 8-16 tokens). Each kernel is row-invariant on its own; the two differ in summation order. The
-   * prefill kernel's dequantised weights are exact for NVFP4, MXFP4 and for FP8 whose 128x128
-   * block scales are powers of two; pick SB_PREFILL_VERIFY for FP8 banks with other scales. */
+  /* Which tensor-core grouped kernels run the experts (SB_LAYOUT_TC only): the verify kernel
+   * (per-stage readback, passes of 8-16 tokens), the prefill kernel (16-bit operands, the whole K in
+   * TMEM, passes of 128 tokens), or the hybrid dispatch (SB_PREFILL_HYBRID: each routed expert that
+   * routes at least 24 tokens (NVFP4), 48 (MXFP4) or 64 (FP8), three or four verify passes, on the
+   * prefill kernel, the others on the verify kernel; the shared expert on the prefill kernel from
+   * 256 tokens on, 128 with fp32 activation scales). SB_PREFILL_AUTO picks the hybrid dispatch when
+   * the batch routes at least 4 tokens per expert on average, else the verify kernel, and always the
+   * verify kernel for FP8 experts (it streams FP8 weights faster than the prefill kernel). A forced
+   * VERIFY or WIDE choice is row-invariant (a token's output does not depend on its batch); the
+   * hybrid dispatch is not, since an expert's kernel depends on the batch. The kernels differ only in
+   * summation order. The prefill kernel's dequantised weights are exact for NVFP4, MXFP4 and for
+   * FP8 whose 128x128 block scales are powers of two; pick SB_PREFILL_VERIFY for FP8 banks with
+   * other scales. */
   int32_t prefill;
   /* 1: every FP8 128x128 block scale of the layer (the shared expert's and, for FP8 experts, the
    * routed bank's) is a power of two, as in ue8m0-scaled checkpoints (the reference stores them as
@@ -134,7 +141,7 @@ typedef struct sb_moe_layer {
 
 enum sb_moe_mode { SB_MODE_V4 = 0, SB_MODE_K3 = 1 };
 
-enum sb_prefill { SB_PREFILL_AUTO = 0, SB_PREFILL_VERIFY = 1, SB_PREFILL_WIDE = 2 };
+enum sb_prefill { SB_PREFILL_AUTO = 0, SB_PREFILL_VERIFY = 1, SB_PREFILL_WIDE = 2, SB_PREFILL_HYBRID = 3 };
 
 /* ── introspection ───────────────────────────────────────────────────────────────────────────── */
 int sb_abi_version(void);

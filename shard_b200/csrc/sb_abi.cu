@@ -67,21 +67,41 @@ struct Workspace {
   __nv_bfloat16* hw;   //                 act-quantised h as bf16, rows of h
   float* cx;           //                 the power of two each row of xw / hw was divided by
   float* ch;
-  bool wide;           // the forward runs the prefill kernel
-  int64_t sb_row;      //   its padded row space: the shared expert's first row, and all rows
+  bool wide;           // the forward runs the prefill kernel alone
+  bool hybrid;         // the forward runs the hybrid dispatch (both kernels)
+  int64_t sb_row;      //   the padded row space: the shared expert's first row, and all rows
   int64_t wide_rows;
-  int n_sh_pass;
+  int n_sh_pass;       // shared passes of the first pass table's kernel
+  int n_sh_pass2;      // hybrid: shared passes of the prefill kernel
+  int32_t* pass_off2;  // hybrid: the prefill kernel's pass table (hot experts)
+  int32_t* pass_slot2;
+  int32_t* pass_pb2;
   size_t bytes;
 };
 
-// The prefill kernel runs when asked, or by default when the batch routes >= 16 tokens per expert on
-// average: below that the verify kernel's narrow passes cost less (measured on B200 at c1 / c4 shapes).
+// The expert kernels of a forward on the tensor-core layout: the verify kernel alone, the prefill
+// kernel alone, or the hybrid dispatch (each routed expert on the kernel its token count suits: the
+// hot ones, routing >= sb::hybrid_hot_min tokens, on the prefill kernel, the others on the verify
+// kernel; the shared expert on the prefill kernel from 2 full passes on). By default the hybrid
+// dispatch runs once a batch routes >= 4 tokens per expert on average, below that the verify kernel;
+// FP8 expert banks stay on the verify kernel, which streams FP8 weights faster than the prefill
+// kernel converts them (measured at c3's shapes).
+enum Kernels { K_VERIFY = 0, K_WIDE = 1, K_HYBRID = 2 };
+constexpr int64_t HYBRID_TOKENS_PER_EXPERT = 4;
+// the tensor-core gate takes batches of >= 16 tokens per expert (and every batch of a forced prefill)
 constexpr int64_t WIDE_TOKENS_PER_EXPERT = 16;
-bool use_wide(const sb_moe_layer* L, int64_t m) {
-  if (L->mode == SB_MODE_K3) return true;   // 16-bit activations: the prefill kernel at every size
-  if (L->layout != SB_LAYOUT_TC || L->prefill == SB_PREFILL_VERIFY) return false;
-  if (L->prefill == SB_PREFILL_WIDE) return true;
-  return m * L->topk >= WIDE_TOKENS_PER_EXPERT * (int64_t)L->n_experts;
+int kernels(const sb_moe_layer* L, int64_t m) {
+  if (L->mode == SB_MODE_K3) return K_WIDE;   // 16-bit activations: the prefill kernel at every size
+  if (L->layout != SB_LAYOUT_TC || L->prefill == SB_PREFILL_VERIFY) return K_VERIFY;
+  if (L->prefill == SB_PREFILL_WIDE) return K_WIDE;
+  if (L->prefill == SB_PREFILL_HYBRID) return K_HYBRID;
+  if (L->expert_fmt == SB_FMT_FP8) return K_VERIFY;
+  return m * L->topk >= HYBRID_TOKENS_PER_EXPERT * (int64_t)L->n_experts ? K_HYBRID : K_VERIFY;
+}
+bool use_wide(const sb_moe_layer* L, int64_t m) { return kernels(L, m) == K_WIDE; }
+bool use_hybrid(const sb_moe_layer* L, int64_t m) { return kernels(L, m) == K_HYBRID; }
+bool tc_gate(const sb_moe_layer* L, int64_t m) {
+  return use_wide(L, m) || (use_hybrid(L, m) && m * L->topk >= WIDE_TOKENS_PER_EXPERT * (int64_t)L->n_experts);
 }
 
 // Tokens per pass of a routed expert and of the shared expert. The prefill kernel takes passes of
@@ -93,14 +113,28 @@ int64_t wide_pass(const sb_moe_layer* L) {
 // hi and lo planes of the prefill kernel's B operands (fp32 activation scales), else one
 int64_t wide_planes(const sb_moe_layer* L) { return (L->act_pow2 || L->mode == SB_MODE_K3) ? 1 : 2; }
 
+// hybrid dispatch: the shared expert runs on the prefill kernel once it fills HYBRID_SHARED_PASSES of
+// its passes (below that its many narrow verify passes spread over the verify kernel's CTAs beat a
+// few long prefill items)
+constexpr int64_t HYBRID_SHARED_PASSES = 2;
+bool hybrid_shared_wide(const sb_moe_layer* L, int64_t m) {
+  return L->has_shared && use_hybrid(L, m) && m >= HYBRID_SHARED_PASSES * wide_pass(L);
+}
+
+// Tokens per pass of the first pass table (the only one, or the hybrid dispatch's verify table).
 int64_t routed_pass_max(const sb_moe_layer* L, int64_t m) {
   return use_wide(L, m) ? wide_pass(L) : sb::tc_pass_max(L->expert_fmt);
 }
 
-// Tensor-core layout: passes of the shared expert (FP8: 16 tokens each, more in the prefill kernel).
+// Tensor-core layout: passes of the shared expert in the first table's kernel (FP8: 16 tokens each,
+// more in the prefill kernel), and in the hybrid dispatch's prefill kernel.
 int64_t shared_passes(const sb_moe_layer* L, int64_t m) {
+  if (!L->has_shared || hybrid_shared_wide(L, m)) return 0;
   const int64_t pm = use_wide(L, m) ? wide_pass(L) : 16;
-  return L->has_shared ? (m + pm - 1) / pm : 0;
+  return (m + pm - 1) / pm;
+}
+int64_t shared_passes_wide(const sb_moe_layer* L, int64_t m) {
+  return hybrid_shared_wide(L, m) ? (m + wide_pass(L) - 1) / wide_pass(L) : 0;
 }
 
 // Upper bound of the routed passes of one grouped launch: sum over experts of
@@ -108,6 +142,10 @@ int64_t shared_passes(const sb_moe_layer* L, int64_t m) {
 int64_t max_routed_passes(const sb_moe_layer* L, int64_t m) {
   const int64_t P = m * L->topk, E = L->n_experts;
   return P / routed_pass_max(L, m) + (P < E ? P : E);
+}
+int64_t max_routed_passes_wide(const sb_moe_layer* L, int64_t m) {
+  const int64_t P = m * L->topk, E = L->n_experts;
+  return use_hybrid(L, m) ? P / wide_pass(L) + (P < E ? P : E) : 0;
 }
 
 int64_t max_passes(const sb_moe_layer* L, int64_t m) { return shared_passes(L, m) + max_routed_passes(L, m); }
@@ -141,9 +179,11 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   w.o = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * H);
   // the prefill kernel keeps h in the padded row space of its B operands (wide_rows >= R)
   w.wide = use_wide(L, m);
+  w.hybrid = use_hybrid(L, m);
+  const bool wide_ops = w.wide || w.hybrid;   // the prefill kernel's operand matrices
   w.sb_row = sb::wide_sb_row(P, E);
   w.wide_rows = w.sb_row + ((m + 7) & ~(int64_t)7);
-  w.hbf = (__nv_bfloat16*)take(tc ? sizeof(__nv_bfloat16) * (w.wide ? w.wide_rows : R) * I : 0);
+  w.hbf = (__nv_bfloat16*)take(tc ? sizeof(__nv_bfloat16) * (wide_ops ? w.wide_rows : R) * I : 0);
   w.pass_off = (int32_t*)take(tc ? sizeof(int32_t) * (E + 1) : 0);
   w.pass_slot = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
   w.pass_pb = (int32_t*)take(tc ? sizeof(int32_t) * max_routed_passes(L, m) : 0);
@@ -152,11 +192,15 @@ Workspace carve(const sb_moe_layer* L, int64_t m, uint8_t* base) {
   w.apanel = (float*)take((size_t)panel_tiles * 16 * sizeof(float));
   // fp32 activation scales: a residual plane below each matrix (hi + lo)
   const int64_t planes = wide_planes(L);
-  w.xw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * w.wide_rows * H : 0);
-  w.hw = (__nv_bfloat16*)take(w.wide ? sizeof(__nv_bfloat16) * planes * w.wide_rows * I : 0);
-  w.cx = (float*)take(w.wide ? sizeof(float) * w.wide_rows : 0);
-  w.ch = (float*)take(w.wide ? sizeof(float) * w.wide_rows : 0);
+  w.xw = (__nv_bfloat16*)take(wide_ops ? sizeof(__nv_bfloat16) * planes * w.wide_rows * H : 0);
+  w.hw = (__nv_bfloat16*)take(wide_ops ? sizeof(__nv_bfloat16) * planes * w.wide_rows * I : 0);
+  w.cx = (float*)take(wide_ops ? sizeof(float) * w.wide_rows : 0);
+  w.ch = (float*)take(wide_ops ? sizeof(float) * w.wide_rows : 0);
   w.n_sh_pass = (int)shared_passes(L, m);
+  w.n_sh_pass2 = (int)shared_passes_wide(L, m);
+  w.pass_off2 = (int32_t*)take(w.hybrid ? sizeof(int32_t) * (E + 1) : 0);
+  w.pass_slot2 = (int32_t*)take(w.hybrid ? sizeof(int32_t) * max_routed_passes_wide(L, m) : 0);
+  w.pass_pb2 = (int32_t*)take(w.hybrid ? sizeof(int32_t) * max_routed_passes_wide(L, m) : 0);
   w.bytes = off;
   return w;
 }
@@ -189,7 +233,7 @@ int check_layer(const sb_moe_layer* L) {
     return fail(SB_ERR_ARG, "weight pointers must be 16-byte aligned");
   if (L->tid2eid && L->vocab <= 0) return fail(SB_ERR_ARG, "tid2eid given with vocab=%lld", (long long)L->vocab);
   if (L->layout != SB_LAYOUT_FRAGMENT && L->layout != SB_LAYOUT_TC) return fail(SB_ERR_ARG, "layout=%d unknown", L->layout);
-  if (L->prefill < SB_PREFILL_AUTO || L->prefill > SB_PREFILL_WIDE) return fail(SB_ERR_ARG, "prefill=%d unknown", L->prefill);
+  if (L->prefill < SB_PREFILL_AUTO || L->prefill > SB_PREFILL_HYBRID) return fail(SB_ERR_ARG, "prefill=%d unknown", L->prefill);
   return SB_OK;
 }
 
@@ -534,13 +578,18 @@ size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
   if (check_layer(layer) != SB_OK || m < 0) return 0;
   if (m < 1) m = 1;
   size_t need = carve(layer, m, nullptr).bytes;
-  // A workspace sized for m serves every m' <= m: past the verify/prefill switch the largest
-  // verify-kernel batch can need more than the prefill kernel at m.
-  if (layer->layout == SB_LAYOUT_TC && layer->prefill == SB_PREFILL_AUTO && use_wide(layer, m)) {
-    const int64_t m_verify = (WIDE_TOKENS_PER_EXPERT * layer->n_experts + layer->topk - 1) / layer->topk - 1;
-    if (m_verify >= 1) {
-      const size_t v = carve(layer, m_verify < m ? m_verify : m, nullptr).bytes;
-      if (v > need) need = v;
+  // A workspace sized for m serves every m' <= m. Between the batch sizes where the kernel choice
+  // changes (the default's switch to the hybrid dispatch; the hybrid dispatch moving the shared
+  // expert to the prefill kernel) every buffer grows with m, so the largest batch below each switch
+  // covers the rest.
+  if (layer->layout == SB_LAYOUT_TC) {
+    const int64_t sw[2] = {(HYBRID_TOKENS_PER_EXPERT * layer->n_experts + layer->topk - 1) / layer->topk,
+                           HYBRID_SHARED_PASSES * wide_pass(layer)};
+    for (int64_t q : sw) {
+      if (q - 1 >= 1 && q - 1 < m) {
+        const size_t v = carve(layer, q - 1, nullptr).bytes;
+        if (v > need) need = v;
+      }
     }
   }
   return need;
@@ -548,13 +597,14 @@ size_t sb_moe_workspace_bytes(const sb_moe_layer* layer, int64_t m) {
 
 static int route_impl(const sb_moe_layer* L, const void* x, int64_t m, const int64_t* ids, float* out_w,
                       int64_t* out_idx, const Workspace& w, bool quant, cudaStream_t st) {
-  // the prefill kernel's batches take the tensor-core gate (a token's logits then come from the
-  // same kernel whether it runs alone or in its batch, under either kernel choice)
-  if (use_wide(L, m)) {
+  // prefill batches take the tensor-core gate (under a forced prefill kernel every batch does, so a
+  // token's logits come from the same kernel whether it runs alone or in its batch)
+  const bool tcg = tc_gate(L, m);
+  if (tcg) {
     const int rc0 = cuda_check(cudaMemsetAsync(w.err + 1, 0, sizeof(int32_t), st), "gate flag");
     if (rc0) return rc0;
   }
-  int rc = use_wide(L, m)
+  int rc = tcg
                ? cuda_check(sb::launch_gate_tc(x, L->gate_w, w.logits, (int)m, L->n_experts, L->hidden,
                                                sb::gate_ksplit(L->hidden), w.err + 1, st),
                             "gate_tc")
@@ -641,6 +691,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   if (rc) return rc;
   mark(1);
   sb::PermuteArgs p;
+  memset(&p, 0, sizeof p);
   p.topk_idx = w.topk_idx;
   p.m = (int)m;
   p.topk = L->topk;
@@ -652,7 +703,14 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
   p.pair_tok = w.pair_tok;
   p.pair_slot = w.pair_slot;
   p.err = w.err;
-  p.gate_err = use_wide(L, m) ? w.err + 1 : nullptr;   // the tensor-core gate's (or the routing input's) flag
+  p.gate_err = tc_gate(L, m) ? w.err + 1 : nullptr;   // the tensor-core gate's (or the routing input's) flag
+  if (w.hybrid) {
+    p.hot_min = sb::hybrid_hot_min(L->expert_fmt);
+    p.pass_max2 = (int)wide_pass(L);
+    p.pass_off2 = w.pass_off2;
+    p.pass_slot2 = w.pass_slot2;
+    p.pass_pb2 = w.pass_pb2;
+  }
   p.pass_max = L->layout == SB_LAYOUT_TC ? (int)routed_pass_max(L, m) : 0;
   p.pass_off = L->layout == SB_LAYOUT_TC ? w.pass_off : nullptr;
   p.pass_slot = w.pass_slot;
@@ -702,7 +760,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
                                                 w.xw, w.cx, st),
                          "wide x (bf16)")
             : cuda_check(sb::launch_wide_x(w.xq, w.xs, w.pair_tok, w.offsets, L->n_experts, (int)m, (int)P, (int)H,
-                                           w.wide_rows, (int)w.sb_row, split, rbf, w.xw, w.cx, st),
+                                           w.wide_rows, (int)w.sb_row, split, rbf, 0, w.xw, w.cx, st),
                          "wide x");
     if (rc) return rc;
     g.mode = sb::MODE_W13;
@@ -721,7 +779,7 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     mark(3);
     rc = k3 ? cuda_check(sb::launch_wide_h_raw(w.hbf, w.wide_rows, w.wide_rows, (int)I, w.hw, w.ch, st), "wide h (bf16)")
             : cuda_check(sb::launch_wide_h(w.hbf, w.wide_rows, w.wide_rows, (int)w.sb_row, (int)I, L->act_pow2, rbf,
-                                           w.hw, w.ch, st),
+                                           w.offsets, L->n_experts, 0, 0, w.hw, w.ch, st),
                          "wide h");
     if (rc) return rc;
     g.mode = sb::MODE_W2;
@@ -734,6 +792,117 @@ static int forward_impl(const sb_moe_layer* layer, const void* x, int64_t m, con
     rc = cuda_check(sb::launch_tc_wide(g, plan, w.hw, w.ch, w.wide_rows, (int)w.sb_row, split,
                                        (int)(n_pass_max * g.items_per_expert), st),
                     "wide w2");
+    if (rc) return rc;
+  } else if (L->layout == SB_LAYOUT_TC && w.hybrid) {
+    // hybrid dispatch: cold experts (and a narrow shared expert) on the verify kernel, hot experts
+    // (and a wide shared expert) on the prefill kernel; h of both in the prefill kernel's padded row
+    // space, o of both in the combine's (token, slot) rows
+    const bool shw = hybrid_shared_wide(L, m);
+    const int hot = sb::hybrid_hot_min(L->expert_fmt);
+    const int split = (int)wide_planes(L) - 1;
+    const int rbf = L->expert_fmt == SB_FMT_MXFP4 ? 1 : 0;
+    sb::TcPlan vplan;   // verify kernel: the first pass table (cold experts)
+    vplan.bpanel = w.bpanel;
+    vplan.apanel = w.apanel;
+    vplan.pass_off = w.pass_off;
+    vplan.pass_slot = w.pass_slot;
+    vplan.pass_pb = w.pass_pb;
+    vplan.n_sh_pass = w.n_sh_pass;
+    sb::TcPlan wplan;   // prefill kernel: the second (hot experts)
+    memset(&wplan, 0, sizeof wplan);
+    wplan.pass_off = w.pass_off2;
+    wplan.pass_slot = w.pass_slot2;
+    wplan.pass_pb = w.pass_pb2;
+    wplan.n_sh_pass = w.n_sh_pass2;
+    rc = cuda_check(sb::launch_wide_x(w.xq, w.xs, w.pair_tok, w.offsets, L->n_experts, shw ? (int)m : 0, (int)P,
+                                      (int)H, w.wide_rows, (int)w.sb_row, split, rbf, hot, w.xw, w.cx, st),
+                    "hybrid wide x");
+    if (rc) return rc;
+    sb::PanelArgs pa;
+    memset(&pa, 0, sizeof pa);
+    pa.mode = sb::MODE_W13;
+    pa.m = (int)m;
+    pa.topk = L->topk;
+    pa.k = (int)H;
+    pa.act_pow2 = L->act_pow2;
+    pa.has_shared = shw ? 0 : L->has_shared;
+    pa.n_sh_pass = w.n_sh_pass;
+    pa.nv_routed = L->expert_fmt == SB_FMT_NVFP4;
+    pa.nv_shared = 0;
+    pa.xq = w.xq;
+    pa.xs = w.xs;
+    pa.hbf = w.hbf;
+    pa.counts = w.counts;
+    pa.offsets = w.offsets;
+    pa.active = w.active;
+    pa.n_active = w.n_active;
+    pa.pass_off = w.pass_off;
+    pa.pair_tok = w.pair_tok;
+    pa.bpanel = w.bpanel;
+    pa.apanel = w.apanel;
+    pa.hot_min = hot;
+    pa.hpad = 1;
+    pa.hsh0 = (int)w.sb_row;
+    rc = cuda_check(sb::launch_tc_panel(pa, n_units, st), "hybrid w13 panel");
+    if (rc) return rc;
+    sb::GroupedArgs gv = g;   // the verify kernel's launches
+    gv.has_shared = shw ? 0 : L->has_shared;
+    gv.hpad = 1;
+    gv.hsh0 = (int)w.sb_row;
+    gv.mode = sb::MODE_W13;
+    gv.n_rows = (int)(2 * I);
+    gv.k = (int)H;
+    gv.routed = routed_set(L, true);
+    gv.shared = shared_set(L, true);
+    gv.hbf = w.hbf;
+    gv.n_experts = L->n_experts;
+    gv.items_per_expert = (int)(I / 64);
+    const int64_t v_pass_max = max_passes(L, m);
+    rc = cuda_check(sb::launch_tc_grouped(gv, vplan, (int)(v_pass_max * gv.items_per_expert), st), "hybrid w13 verify");
+    if (rc) return rc;
+    sb::GroupedArgs gw = g;   // the prefill kernel's launches
+    gw.has_shared = shw ? L->has_shared : 0;
+    gw.mode = sb::MODE_W13;
+    gw.n_rows = (int)(2 * I);
+    gw.k = (int)H;
+    gw.routed = routed_set(L, true);
+    gw.shared = shared_set(L, true);
+    gw.hbf = w.hbf;
+    gw.n_experts = L->n_experts;
+    gw.items_per_expert = (int)(I / 64);
+    const int64_t w_pass_max = shared_passes_wide(L, m) + max_routed_passes_wide(L, m);
+    rc = cuda_check(sb::launch_tc_wide(gw, wplan, w.xw, w.cx, w.wide_rows, (int)w.sb_row, split,
+                                       (int)(w_pass_max * gw.items_per_expert), st),
+                    "hybrid w13 prefill");
+    if (rc) return rc;
+    mark(3);
+    pa.mode = sb::MODE_W2;
+    pa.k = (int)I;
+    rc = cuda_check(sb::launch_tc_panel(pa, n_units, st), "hybrid w2 panel");
+    if (rc) return rc;
+    rc = cuda_check(sb::launch_wide_h(w.hbf, w.wide_rows, w.wide_rows, (int)w.sb_row, (int)I, L->act_pow2, rbf,
+                                      w.offsets, L->n_experts, hot, shw ? (int)m : 0, w.hw, w.ch, st),
+                    "hybrid wide h");
+    if (rc) return rc;
+    gv.mode = sb::MODE_W2;
+    gv.n_rows = (int)H;
+    gv.k = (int)I;
+    gv.routed = routed_set(L, false);
+    gv.shared = shared_set(L, false);
+    gv.o = w.o;
+    gv.items_per_expert = (int)(H / 128);
+    rc = cuda_check(sb::launch_tc_grouped(gv, vplan, (int)(v_pass_max * gv.items_per_expert), st), "hybrid w2 verify");
+    if (rc) return rc;
+    gw.mode = sb::MODE_W2;
+    gw.n_rows = (int)H;
+    gw.k = (int)I;
+    gw.routed = routed_set(L, false);
+    gw.shared = shared_set(L, false);
+    gw.o = w.o;
+    gw.items_per_expert = (int)(H / 128);
+    rc = cuda_check(sb::launch_tc_wide(gw, wplan, w.hw, w.ch, w.wide_rows, (int)w.sb_row, split,
+                                       (int)(w_pass_max * gw.items_per_expert), st),
+                    "hybrid w2 prefill");
     if (rc) return rc;
   } else if (L->layout == SB_LAYOUT_TC) {
     // tensor-core path: w13 panel, w13 (+ SwiGLU -> h bf16), w2 panel (act_quant of h), w2

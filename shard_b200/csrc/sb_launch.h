@@ -41,6 +41,13 @@ struct PermuteArgs {
   int32_t* pass_off; // [E+1] by active slot: first pass of the slot, total passes at [n_active]
   int32_t* pass_slot;// [routed passes] active slot of each pass
   int32_t* pass_pb;  // [routed passes] first token (within its expert) of each pass
+  // hybrid dispatch: experts routing >= hot_min tokens get their passes (of pass_max2 tokens) in a
+  // second table, for the prefill kernel, and none in the first (hot_min 0: one table)
+  int hot_min;
+  int pass_max2;
+  int32_t* pass_off2;
+  int32_t* pass_slot2;
+  int32_t* pass_pb2;
 };
 
 // One family of tiled weight matrices (one per expert, or a single matrix).
@@ -91,6 +98,8 @@ struct GroupedArgs {
   int kstages;         // stages (128 K) per piece, a multiple of the kernel's unit of 2
   float* part;         // ksplit > 1: fp32 partials [n_sh_pass * nrb][ksplit][128 rows][16]
   int* kcnt;           // ksplit > 1: [n_sh_pass * nrb] pieces finished (zeroed by the panel kernel)
+  int hpad;            // verify kernel, W13: h rows in the prefill kernel's padded row space (hybrid),
+  int hsh0;            // the shared expert's first h row there
 };
 
 enum Activation { ACT_SWIGLU = 0, ACT_SITU = 1 };
@@ -127,9 +136,21 @@ struct PanelArgs {
   float* apanel;
   int* kzero;               // counters of the next grouped launch's K pieces, zeroed here (or NULL)
   int nkzero;
+  int hot_min;              // hybrid dispatch: routed experts with >= hot_min tokens are skipped
+  int hpad;                 // W2: h rows in the prefill kernel's padded row space (hybrid),
+  int hsh0;                 // the shared expert's first h row there
 };
 
 __host__ __device__ inline int tc_pass_max(int fmt) { return fmt == 1 ? 8 : 16; }
+
+// Hybrid dispatch: a routed expert is "hot", and runs on the prefill kernel, when it routes at least
+// three of the verify kernel's passes' worth of tokens, four for FP8 experts (the measured
+// break-even of a 128-token prefill pass against narrow verify passes that each stream the expert's
+// weights; the verify kernel streams FP8 closer to the HBM rate).
+__host__ __device__ inline int hybrid_hot_min(int fmt) { return fmt == 3 ? 4 * tc_pass_max(fmt) : 3 * tc_pass_max(fmt); }
+
+// Padded row space of the prefill kernel's operands: expert e's rows start at a multiple of 8.
+__host__ __device__ inline int wide_pbase(int off, int e) { return (off + 8 * e + 7) & ~7; }
 
 // Byte offset of weight row r's four e8m0 scales within a tensor-core-layout MXFP4 scale stage
 // (128 rows x 4 per-32 scales): 16 (r % 32) + 4 (r / 32), the source order of the scale-factor copy
@@ -179,11 +200,15 @@ constexpr int TC_WIDE_PASS = 128;   // tokens per pass of the prefill kernel (sb
 constexpr int wide_sb_row(int64_t P, int64_t n_experts) { return (int)((P + 8 * n_experts + 7) & ~(int64_t)7); }
 cudaError_t launch_tc_wide(const GroupedArgs& g, const TcPlan& plan, const void* bmat, const float* cvec,
                            int64_t r_pad, int sb_row, int split, int max_items, cudaStream_t st);
+// (hot_min > 0: the hybrid dispatch, rows of experts routing fewer tokens are skipped; m: the shared
+// expert's rows, 0 when it does not run in the prefill kernel)
 cudaError_t launch_wide_x(const uint8_t* xq, const float* xs, const int32_t* pair_tok, const int32_t* offsets,
                           int n_experts, int m, int P, int h, int64_t r_pad, int sb_row, int split, int routed_bf16,
-                          void* xw, float* cvec, cudaStream_t st);
+                          int hot_min, void* xw, float* cvec, cudaStream_t st);
+// (hot_min > 0: the hybrid dispatch, only hot experts' rows and the first sh_rows shared rows)
 cudaError_t launch_wide_h(const __nv_bfloat16* hbf, int64_t rows, int64_t r_pad, int sb_row, int k, int pow2,
-                          int routed_bf16, void* hw, float* cvec, cudaStream_t st);
+                          int routed_bf16, const int32_t* offsets, int n_experts, int hot_min, int sh_rows, void* hw,
+                          float* cvec, cudaStream_t st);
 cudaError_t launch_tc_tile(int fmt, int kind, bool scales, const void* src, void* dst, int64_t n_mat, int64_t n,
                            int64_t k, cudaStream_t st);
 

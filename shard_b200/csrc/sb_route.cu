@@ -353,48 +353,58 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
   const int e = threadIdx.x;
   const int c = e < E ? cnt[e] : 0;
   const int flag = c > 0 ? 1 : 0;
-  const int np = a.pass_max > 0 ? (c + a.pass_max - 1) / a.pass_max : 0;  // passes of expert e
+  // passes of expert e: in the first table, or (a hot expert of the hybrid dispatch) the second
+  const bool hot = a.hot_min > 0 && c >= a.hot_min;
+  const int np = (a.pass_max > 0 && !hot) ? (c + a.pass_max - 1) / a.pass_max : 0;
+  const int np2 = hot ? (c + a.pass_max2 - 1) / a.pass_max2 : 0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl = c, fincl = flag, pincl = np;
+  int incl = c, fincl = flag, pincl = np, qincl = np2;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int v = __shfl_up_sync(0xffffffffu, incl, o);
     const int fv = __shfl_up_sync(0xffffffffu, fincl, o);
     const int pv = __shfl_up_sync(0xffffffffu, pincl, o);
+    const int qv = __shfl_up_sync(0xffffffffu, qincl, o);
     if (lane >= o) {
       incl += v;
       fincl += fv;
       pincl += pv;
+      qincl += qv;
     }
   }
-  __shared__ int warp_ftot[32], warp_ptot[32];
+  __shared__ int warp_ftot[32], warp_ptot[32], warp_qtot[32];
   if (lane == 31) {
     warp_tot[warp] = incl;
     warp_ftot[warp] = fincl;
     warp_ptot[warp] = pincl;
+    warp_qtot[warp] = qincl;
   }
   __syncthreads();
   if (warp == 0) {
-    int v = warp_tot[lane], fv = warp_ftot[lane], pv = warp_ptot[lane];
+    int v = warp_tot[lane], fv = warp_ftot[lane], pv = warp_ptot[lane], qv = warp_qtot[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int u = __shfl_up_sync(0xffffffffu, v, o);
       const int fu = __shfl_up_sync(0xffffffffu, fv, o);
       const int pu = __shfl_up_sync(0xffffffffu, pv, o);
+      const int qu = __shfl_up_sync(0xffffffffu, qv, o);
       if (lane >= o) {
         v += u;
         fv += fu;
         pv += pu;
+        qv += qu;
       }
     }
     warp_tot[lane] = v;
     warp_ftot[lane] = fv;
     warp_ptot[lane] = pv;
+    warp_qtot[lane] = qv;
   }
   __syncthreads();
   const int base = warp > 0 ? warp_tot[warp - 1] : 0;
   const int fbase = warp > 0 ? warp_ftot[warp - 1] : 0;
   const int pbase = warp > 0 ? warp_ptot[warp - 1] : 0;
+  const int qbase = warp > 0 ? warp_qtot[warp - 1] : 0;
   if (e < E) {
     const int off = base + incl - c;
     a.offsets[e] = off;
@@ -409,10 +419,19 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteArgs a) {
         a.pass_pb[p0 + i] = i * a.pass_max;
       }
     }
+    if (flag && a.pass_off2) {
+      const int slot = fbase + fincl - 1, q0 = qbase + qincl - np2;
+      a.pass_off2[slot] = q0;
+      for (int i = 0; i < np2; ++i) {
+        a.pass_slot2[q0 + i] = slot;
+        a.pass_pb2[q0 + i] = i * a.pass_max2;
+      }
+    }
     if (e == E - 1) {
       a.offsets[E] = base + incl;
       *a.n_active = fbase + fincl;
       if (a.pass_off) a.pass_off[fbase + fincl] = pbase + pincl;
+      if (a.pass_off2) a.pass_off2[fbase + fincl] = qbase + qincl;
     }
   }
   __syncthreads();

@@ -564,12 +564,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
         if (lane < pc) {
           const int i = pb + lane;
           if (it.shared) {
-            my_orow = a.mode == MODE_DENSE ? i : P + i;
+            my_orow = a.mode == MODE_DENSE ? i : (w13 && a.hpad ? a.hsh0 : P) + i;
           } else {
             const int qp = it.base + i;
             const int tok = a.pair_tok[qp], slot = a.pair_slot[qp];
             if (w13) {
-              my_orow = qp;
+              my_orow = a.hpad ? wide_pbase(it.base, it.expert) + i : qp;
               my_wgt = a.topk_w[(size_t)tok * a.topk + slot];
             } else {
               my_orow = tok * a.topk + slot;
@@ -872,6 +872,7 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
   if (a.kzero != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
     for (int i = threadIdx.x; i < a.nkzero; i += blockDim.x) a.kzero[i] = 0;
   int shared, cnt, base, pass0, nv;
+  int hrow0 = -1;   // W2, hybrid: first h row of the expert in the padded row space
   if (slot < a.has_shared) {
     shared = 1;
     cnt = a.m;
@@ -884,7 +885,9 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
     const int e = a.active[s];
     shared = 0;
     cnt = a.counts[e];
+    if (a.hot_min > 0 && cnt >= a.hot_min) return;   // a hot expert of the hybrid dispatch
     base = a.offsets[e];
+    if (a.hpad) hrow0 = wide_pbase(base, e);
     pass0 = a.n_sh_pass + a.pass_off[s];
     nv = a.nv_routed;
   }
@@ -898,7 +901,7 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
     int srow = 0;
     if (valid) {
       if (a.mode != MODE_W2) srow = (shared || a.pair_tok == nullptr) ? i : a.pair_tok[base + i];
-      else srow = shared ? P + i : base + i;
+      else srow = shared ? (a.hpad ? a.hsh0 : P) + i : (hrow0 >= 0 ? hrow0 : base) + i;
     }
     uint4 v[PANEL_STAGES];
     float sc[PANEL_STAGES];

@@ -66,7 +66,7 @@ struct WideArgs {
 
 // Padded row space of the B matrices: expert e's rows start at pbase(offsets[e], e), a multiple of 8
 // (its passes then start at multiples of 8 too); the shared expert's tokens follow at sb_row.
-__host__ __device__ __forceinline__ int pbase(int off, int e) { return (off + 8 * e + 7) & ~7; }
+__host__ __device__ __forceinline__ int pbase(int off, int e) { return wide_pbase(off, e); }
 
 struct Item {
   int shared, expert, rb, cnt, base, pb, pass;
@@ -637,7 +637,8 @@ __global__ void __launch_bounds__(256) wide_x_kernel(const uint8_t* __restrict__
                                                      const int32_t* __restrict__ pair_tok,
                                                      const int32_t* __restrict__ offsets, int n_experts, int m, int P,
                                                      int h, int64_t r_pad, int sb_row, int split, int routed_bf16,
-                                                     uint16_t* __restrict__ xw, float* __restrict__ cvec) {
+                                                     int hot_min, uint16_t* __restrict__ xw,
+                                                     float* __restrict__ cvec) {
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
@@ -651,6 +652,8 @@ __global__ void __launch_bounds__(256) wide_x_kernel(const uint8_t* __restrict__
         const int mid = (lo + hi) >> 1;
         if (offsets[mid] <= q) lo = mid; else hi = mid;
       }
+      // hybrid dispatch: only the hot experts' rows are read by the prefill kernel
+      if (hot_min > 0 && offsets[lo + 1] - offsets[lo] < hot_min) continue;
       tok = pair_tok[q];
       row = pbase(offsets[lo], lo) + (int)(q - offsets[lo]);
     } else {
@@ -690,13 +693,30 @@ __global__ void __launch_bounds__(256) wide_x_kernel(const uint8_t* __restrict__
 // values 4l..4l+3 of each 128-block; a first sweep finds the row's largest scale (for c_B)
 __global__ void __launch_bounds__(256) wide_h_kernel(const __nv_bfloat16* __restrict__ hbf, int64_t rows,
                                                      int64_t r_pad, int sb_row, int k, int pow2, int routed_bf16,
-                                                     uint16_t* __restrict__ hw, float* __restrict__ cvec) {
+                                                     const int32_t* __restrict__ offsets, int n_experts, int hot_min,
+                                                     int sh_rows, uint16_t* __restrict__ hw,
+                                                     float* __restrict__ cvec) {
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int nkb = k / 128;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {
+    if (hot_min > 0) {
+      // hybrid dispatch: only the rows the prefill kernel reads, those of hot experts (and of the
+      // shared expert when it runs there)
+      if (row >= sb_row) {
+        if (row >= (int64_t)sb_row + sh_rows) continue;
+      } else {
+        int lo = 0, hi = n_experts;   // the last e whose padded rows start at or before row
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (pbase(offsets[mid], mid) <= row) lo = mid; else hi = mid;
+        }
+        const int cnt = offsets[lo + 1] - offsets[lo];
+        if (cnt < hot_min || row - pbase(offsets[lo], lo) >= cnt) continue;
+      }
+    }
     const bool bf = routed_bf16 && row < sb_row;
     const __nv_bfloat16* hr = hbf + row * k;
     // the block's 4 values of this lane, and the block's amax
@@ -890,10 +910,10 @@ cudaError_t launch_tc_wide(const GroupedArgs& g, const TcPlan& plan, const void*
 
 cudaError_t launch_wide_x(const uint8_t* xq, const float* xs, const int32_t* pair_tok, const int32_t* offsets,
                           int n_experts, int m, int P, int h, int64_t r_pad, int sb_row, int split, int routed_bf16,
-                          void* xw, float* cvec, cudaStream_t st) {
+                          int hot_min, void* xw, float* cvec, cudaStream_t st) {
   return launch_pdl(tcw::wide_x_kernel, dim3(tcw::warp_grid((int64_t)P + m)), dim3(256), 0, st, xq, xs, pair_tok,
-                    offsets, n_experts, m, P, h, r_pad, sb_row, split, routed_bf16, reinterpret_cast<uint16_t*>(xw),
-                    cvec);
+                    offsets, n_experts, m, P, h, r_pad, sb_row, split, routed_bf16, hot_min,
+                    reinterpret_cast<uint16_t*>(xw), cvec);
 }
 
 cudaError_t launch_wide_x_raw(const void* x, const int32_t* pair_tok, const int32_t* offsets, int n_experts, int P,
@@ -909,9 +929,10 @@ cudaError_t launch_wide_h_raw(const __nv_bfloat16* hbf, int64_t rows, int64_t r_
 }
 
 cudaError_t launch_wide_h(const __nv_bfloat16* hbf, int64_t rows, int64_t r_pad, int sb_row, int k, int pow2,
-                          int routed_bf16, void* hw, float* cvec, cudaStream_t st) {
+                          int routed_bf16, const int32_t* offsets, int n_experts, int hot_min, int sh_rows, void* hw,
+                          float* cvec, cudaStream_t st) {
   return launch_pdl(tcw::wide_h_kernel, dim3(tcw::warp_grid(rows)), dim3(256), 0, st, hbf, rows, r_pad, sb_row, k,
-                    pow2, routed_bf16, reinterpret_cast<uint16_t*>(hw), cvec);
+                    pow2, routed_bf16, offsets, n_experts, hot_min, sh_rows, reinterpret_cast<uint16_t*>(hw), cvec);
 }
 
 }  // namespace sb

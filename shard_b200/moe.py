@@ -136,24 +136,26 @@ class MoELayer:
         d.mode = _lib.MODE_K3 if mode == "k3" else _lib.MODE_V4
         d.situ_beta = float(situ_beta)
         d.situ_linear_beta = float(situ_linear_beta or 0.0)
-        self.prefill = prefill     # 0 auto, 1 verify kernel, 2 prefill kernel
+        self.prefill = prefill     # 0 auto, 1 verify kernel, 2 prefill kernel, 3 hybrid dispatch
         self._ws = None
         self._ws_need = {}
         self.score_func, self.route_scale, self.swiglu_limit, self.act_pow2 = score_func, route_scale, swiglu_limit, act_pow2
 
     @property
     def prefill(self) -> int:
-        """Expert-kernel choice on the tensor-core layout: 0 by batch size (the prefill kernel once
-        the batch routes >= 16 tokens per expert), 1 always the verify kernel, 2 always the prefill
-        kernel."""
+        """Expert-kernel choice on the tensor-core layout: 0 by batch size (the hybrid dispatch once
+        the batch routes >= 4 tokens per expert, else the verify kernel; FP8 experts always the verify
+        kernel), 1 always the verify kernel,
+        2 always the prefill kernel, 3 always the hybrid dispatch (hot experts on the prefill kernel,
+        the others on the verify kernel)."""
         return int(self.desc.prefill)
 
     @prefill.setter
     def prefill(self, mode: int):
         """0 resolves to 1 on layers whose FP8 block scales are not all powers of two."""
         mode = int(mode)
-        if mode not in (0, 1, 2):
-            raise ValueError(f"prefill mode {mode} is not 0, 1 or 2")
+        if mode not in (0, 1, 2, 3):
+            raise ValueError(f"prefill mode {mode} is not 0, 1, 2 or 3")
         self.desc.prefill = 1 if mode == 0 and not self.prefill_exact else mode
 
     # ── scratch ───────────────────────────────────────────────────────────────────────────────

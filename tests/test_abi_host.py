@@ -79,23 +79,26 @@ def test_workspace_sizes_grow_with_m_and_reject_bad_layers():
 
 def test_workspace_serves_every_smaller_batch_across_the_prefill_switch():
     """A workspace sized for m serves every m' <= m: under the default kernel choice the size at m
-    covers both the verify kernel's largest batch below the switch and the prefill kernel at m."""
+    covers the verify kernel's largest batch below the switch to the hybrid dispatch and the hybrid
+    dispatch at m; the hybrid dispatch's own size covers the batches before its shared expert moves
+    to the prefill kernel."""
     L = _lib.lib()
     for e, k in ((16, 4), (256, 8), (384, 8)):
         d = _layer(n_experts=e, topk=k)
         sizes = {}
-        for mode in (0, 1, 2):
+        top = max(16 * e // k, 512) + 40
+        for mode in (0, 1, 2, 3):
             d.prefill = mode
-            sizes[mode] = [L.sb_moe_workspace_bytes(ctypes.byref(d), m) for m in range(1, 16 * e // k + 40)]
+            sizes[mode] = [L.sb_moe_workspace_bytes(ctypes.byref(d), m) for m in range(1, top)]
             assert all(s > 0 for s in sizes[mode])
             assert sizes[mode] == sorted(sizes[mode]), (e, k, mode)
-        switch = 16 * e // k                             # first m the default sends to the prefill kernel
+        switch = -(-4 * e // k)                          # first m the default sends to the hybrid dispatch
         for m in range(1, len(sizes[0]) + 1):
-            below = max(sizes[1][:min(m, switch - 1)])
+            below = max(sizes[1][:min(m, switch - 1)] or [0])
             assert sizes[0][m - 1] >= below
-            assert sizes[0][m - 1] >= (sizes[2][m - 1] if m >= switch else sizes[1][m - 1])
+            assert sizes[0][m - 1] >= (sizes[3][m - 1] if m >= switch else sizes[1][m - 1])
     d = _layer()
-    d.prefill = 3
+    d.prefill = 4
     assert L.sb_moe_workspace_bytes(ctypes.byref(d), 16) == 0
     assert L.sb_moe_forward(ctypes.byref(d), FAKE, 16, None, FAKE, None, None, FAKE, 1 << 30, None) == -1
 

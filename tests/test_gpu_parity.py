@@ -92,8 +92,10 @@ def test_quantised_gemm_matches_oracle(fmt, m, n, k, layout):
     assert (_np(y) != ref).mean() < 0.02
 
 
-# (layout, prefill): the tensor-core layout's verify kernel and prefill kernel, the fragment layout
-KERNELS = {"tc_verify": (1, 1), "tc_prefill": (1, 2), "fragment": (0, 0)}
+# (layout, prefill): the tensor-core layout's verify kernel, prefill kernel and hybrid dispatch (at
+# these sizes every routed expert is cold: the verify kernel with h in the prefill kernel's padded
+# rows, and prefill launches with no items), the fragment layout
+KERNELS = {"tc_verify": (1, 1), "tc_prefill": (1, 2), "tc_hybrid": (1, 3), "fragment": (0, 0)}
 
 
 def _golden_layer(name, layout=None, prefill=0):
@@ -134,7 +136,8 @@ def test_full_size_forward(cname, m, layout):
     """Full configuration shapes. The oracle checks a sample of tokens (its cost grows with the experts
     they route to); the whole batch is checked for row invariance: every token's output equals the
     same token run alone through the same kernel, bit for bit. The tensor-core layout runs both of
-    its expert kernels (verify and prefill), and the default choice must equal the one it picks."""
+    its expert kernels (verify and prefill) and the hybrid dispatch (not row-invariant: an expert's
+    kernel depends on its batch), and the default choice must equal the one it picks."""
     cfg = S.CONFIGS[cname]
     x, ids = S.make_inputs(cfg, m)
     gw, gb = S.make_gate(cfg)
@@ -159,17 +162,28 @@ def test_full_size_forward(cname, m, layout):
         assert lay.device_error() == 0
         ys[mode] = y
     if layout == 1:
+        lay.prefill = 3
+        y3, w3, idx3 = lay.forward(x.cuda(), ids.cuda(), routing=True)
+        assert np.array_equal(idx3.cpu().numpy(), idx_o), "router top-k indices must be bit-exact"
+        err = O.max_rel_err(_np(y3[sample]), yo)
+        assert err < TOL, f"{cname} M={m} hybrid: max rel err {err:.3e}"
+        assert torch.isfinite(y3.float()).all()
+        assert lay.device_error() == 0
+        assert torch.equal(lay.forward(x.cuda(), ids.cuda()), y3), "the hybrid dispatch is deterministic"
         lay.prefill = 0
         auto = lay.forward(x.cuda(), ids.cuda())
-        wide = m * cfg.topk >= 16 * cfg.n_experts
-        assert torch.equal(auto, ys[2 if wide else 1])
-        # the two kernels sum in different orders; they agree to well within the parity bar
+        hybrid = m * cfg.topk >= 4 * cfg.n_experts and cfg.expert_fmt != F.FMT_FP8
+        assert torch.equal(auto, y3 if hybrid else ys[1])
+        # the kernels sum in different orders; they agree to well within the parity bar
         assert O.max_rel_err(_np(ys[1]), _np(ys[2])) < TOL
+        assert O.max_rel_err(_np(ys[1]), _np(y3)) < TOL
 
 
 @pytest.mark.parametrize("cname,m", [("c1", 64), ("c3", 64), ("c4", 256), ("c4", 1024)])
 def test_full_size_forward_every_token(cname, m):
-    """Every token of a full-size batch against the oracle, through both tensor-core expert kernels.
+    """Every token of a full-size batch against the oracle, through both tensor-core expert kernels
+    and the hybrid dispatch (at c4 sizes its hot experts run on the prefill kernel, the rest on the
+    verify kernel).
     The layer's experts are N(0, 0.02) draws quantised on the device (the benchmark's layers); the
     oracle regenerates the bytes of each routed expert it needs and runs its C dequant-GEMM."""
     import threading
@@ -191,7 +205,7 @@ def test_full_size_forward_every_token(cname, m):
                        shared=None if sh is None else tuple(t.numpy() for t in (sh.w13, sh.w13_s, sh.w13_ts, sh.w2,
                                                                                    sh.w2_s, sh.w2_ts)))
     yo, wo, io = O.moe_forward(ol, x.float().numpy(), workers=16)
-    for mode in (1, 2):
+    for mode in (1, 2, 3):
         lay.prefill = mode
         y, w, idx = lay.forward(x.cuda(), ids.cuda(), routing=True)
         torch.cuda.synchronize()
@@ -225,7 +239,7 @@ def test_merged_chunks_equal_unmerged(prefill):
     assert torch.equal(torch.cat([ya, yb]), yab)
 
 
-@pytest.mark.parametrize("prefill", [1, 2])
+@pytest.mark.parametrize("prefill", [1, 2, 3])
 def test_hash_routing_drops_earlier_duplicate_slots(prefill):
     """Hash layers (model.py:581-582): ids from tid2eid, repeated ids keep only the last slot
     (the reference's `y[idx] +=` semantics, v4_moe_grouped.py:98-118); through the verify kernel
