@@ -5,6 +5,9 @@ I=2048, NVFP4 routed experts, FP8 128x128 shared expert, sigmoid router), verify
 tokens, 6 distinct layers per GPU. At N GPUs the 6N-layer stack is pipeline-partitioned into
 contiguous 6-layer blocks, one per rank (N=8 is config c2's 48 layers), with NCCL send/recv of the
 bf16 activations between stages and 8 chunks streamed per step. Per-GPU work is fixed: weak scaling.
+Each layer runs as the reference block's ffn half, x + moe(rmsnorm(x)) (the residual add and the norm
+fused in one kernel of this library), so the routing stays as spread deep in the stack as at its
+first layer.
 
   value   = token-layers per second over the whole job: chunks * M tokens * layers / time, with
             the inputs already in HBM (one layer's MoE forward on M tokens = M token-layers; at N=1
@@ -49,7 +52,7 @@ METRIC = "MoE stage tokens/s (token-layers/s), verify M=16, c1/c2 V4-Flash MoE l
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum of one forward's W13 and W2 grouped
 # launches) over that forward's algorithmic bytes, from one capture of the small case
 # (--layers 1 --experts 32) per kernel family; roofline.traffic applies it to the live workload.
-TRAFFIC_RATIO = {"tcgen05": 492.5 / 469.0, "mma.sync": (1.018e9 + 13.4e6 + 0.509e9 + 12.5e6) / 1.44e9}
+TRAFFIC_RATIO = {"tcgen05": (321.2 + 3.9 + 160.6 + 4.1) / 469.0, "mma.sync": (1.018e9 + 13.4e6 + 0.509e9 + 12.5e6) / 1.44e9}
 UNIT = "tokens/s"
 
 
@@ -278,7 +281,7 @@ def run_gpu(args, rank, world, local_rank):
     if args.config == "c4":
         return run_c4_pipeline(args, rank, world, device)
     cfg, layers = build_layers(rank, LAYERS_PER_GPU, device)
-    pipe = Pipeline(StageStack(layers), HEADLINE_M, cfg.hidden, rank, world, device, wire=args.wire)
+    pipe = Pipeline(StageStack(layers, residual=True), HEADLINE_M, cfg.hidden, rank, world, device, wire=args.wire)
     C = CHUNKS_PER_STEP
     xs_dev = chunk_inputs(cfg, C, device) if rank == 0 else None
     outs_dev = [torch.empty(HEADLINE_M, cfg.hidden, dtype=torch.bfloat16, device=device) for _ in range(C)] \
@@ -392,10 +395,16 @@ def run_gpu(args, rank, world, local_rank):
                            "routed_fmt": "nvfp4", "shared_fmt": "fp8-128x128",
                            "kernels": "tcgen05" if layers[0].layout == 1 else "mma.sync",
                            "l2": "no flush: each step streams >1 GB of distinct expert weights per layer (L2 126 MB)",
+                           "block": "x + moe(rmsnorm(x)) per layer (the reference block's ffn half; keeps routing "
+                                    "spread through the stack)",
                            "parallelism": f"pp{world}", "wire": args.wire},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": bytes_io,
                         "d2h_bytes_per_step": bytes_io},
-                "gpu_launches": args.steps * C * LAYERS_PER_GPU * 6 * world,
+                # per chunk and stage: 8 kernels per MoE forward on the verify path plus the fused
+                # residual/RMSNorm before each layer and the final residual add; fp8 wire: a pack
+                # and an unpack per stage boundary
+                "gpu_launches": args.steps * C * ((LAYERS_PER_GPU * 9 + 1) * world +
+                                                  (2 * (world - 1) if args.wire == "fp8" else 0)),
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clocks, "sweep": sweep}
         print(json.dumps(line), flush=True)
     return 0
@@ -426,7 +435,7 @@ def run_c4_pipeline(args, rank, world, device):
     C = CHUNKS_PER_STEP
     for lay in layers:
         lay.reserve(m)
-    pipe = Pipeline(StageStack(layers), m, cfg.hidden, rank, world, device)
+    pipe = Pipeline(StageStack(layers, residual=True), m, cfg.hidden, rank, world, device)
     xs = [S.make_inputs(cfg, m, step=j)[0].to(device) for j in range(C)] if rank == 0 else None
     outs = [torch.empty(m, cfg.hidden, dtype=torch.bfloat16, device=device) for _ in range(C)] \
         if rank == world - 1 else None
@@ -469,6 +478,7 @@ def run_c4_pipeline(args, rank, world, device):
                            "m": m, "layers": C4_LAYERS, "layers_per_rank": [len(b) for b in blocks],
                            "distinct_banks_per_rank": min(distinct, len(mine)), "chunks_per_step": C,
                            "pipeline_depth": pipe.depth, "parallelism": f"pp{world}",
+                           "block": "x + moe(rmsnorm(x)) per layer",
                            "l2": "no flush: each forward streams GBs of distinct expert weights"},
                 "clocks": clk.summary(set(range(world)) if world > 1 else {device.index})}
         print(json.dumps(line), flush=True)

@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define SB_ABI_VERSION 6
+#define SB_ABI_VERSION 7
 
 enum sb_status {
   SB_OK = 0,
@@ -229,6 +229,13 @@ int sb_moe_forward_wire(const sb_moe_layer* layer, const void* x, int64_t m, con
 int sb_wire_pack(const void* x, int64_t rows, int64_t dim, void* q, void* scale, void* stream);
 /* unpack: y bf16 [rows, dim] = bf16(e4m3(q) * scale). */
 int sb_wire_unpack(const void* q, const void* scale, int64_t rows, int64_t dim, void* y, void* stream);
+
+/* The block around the MoE operator (Block.forward's ffn half, model.py:701-706, without its
+ * hyper-connections; RMSNorm.forward, model.py:197-202): x bf16 [rows, dim] (in/out) <- bf16(x + y)
+ * when y is given (the residual stream), then out bf16 = bf16(weight * (x * rsqrt(mean(x^2) + eps))) in
+ * fp32; weight NULL means ones; out NULL does the residual add alone. dim % 8 == 0. */
+int sb_residual_rmsnorm(void* x, const void* y, int64_t rows, int64_t dim, const float* weight, float eps, void* out,
+                        void* stream);
 
 /* Routing alone (Gate.forward, model.py:569-589): weights fp32 [M, k], indices int64 [M, k]. */
 int sb_moe_route(const sb_moe_layer* layer, const void* x, int64_t m, const int64_t* input_ids,

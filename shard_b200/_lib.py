@@ -15,7 +15,7 @@ SB_OK = 0
 STATUS = {0: "SB_OK", -1: "SB_ERR_ARG", -2: "SB_ERR_SHAPE", -3: "SB_ERR_FORMAT", -4: "SB_ERR_WORKSPACE",
           -5: "SB_ERR_CUDA", -6: "SB_ERR_UNSUPPORTED"}
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 SCORE = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 MAT_PLAIN, MAT_W13 = 0, 1
 KIND_TC = 4                      # OR'ed into a tiling kind: the tensor-core (tcgen05) layout
@@ -70,6 +70,7 @@ SIGNATURES = {
     "sb_wire_unpack": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "sb_selftest_formats": (_int, [_vp, _vp]),
     "sb_debug_set_wait_limit": (_int, [_i64]),
+    "sb_residual_rmsnorm": (_int, [_vp, _vp, _i64, _i64, _vp, ctypes.c_float, _vp, _vp]),
 }
 
 _LIB = None

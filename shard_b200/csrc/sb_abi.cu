@@ -422,8 +422,7 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
       return fail(SB_ERR_WORKSPACE, "qgemm: workspace %zu bytes < %zu needed", workspace_bytes, need);
     if (!aligned16(q)) return fail(SB_ERR_ARG, "qgemm: activations must be 16-byte aligned");
     cudaStream_t st = (cudaStream_t)stream;
-    int rc = cuda_check(cudaMemsetAsync(err, 0, sizeof(int), st), "qgemm");
-    if (rc) return rc;
+    int rc = SB_OK;
     const int pm = sb::tc_pass_max(fmt);
     sb::PanelArgs pa;
     memset(&pa, 0, sizeof pa);
@@ -438,6 +437,7 @@ int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* t
     pa.xs = s;
     pa.bpanel = bpanel;
     pa.apanel = apanel;
+    pa.zero_err = err;   // cleared by the panel kernel, which the grouped kernel waits for
     if (ksplit > 1) {
       // K pieces: partials after the panel, then the counters, zeroed by the panel kernel
       const int64_t blocks = (int64_t)pa.n_sh_pass * (n / 128);
@@ -1057,6 +1057,19 @@ int sb_wire_unpack(const void* q, const void* scale, int64_t rows, int64_t dim, 
   if (!aligned16(y) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(SB_ERR_ARG, "wire_unpack: y 16-byte, q 8-byte aligned");
   if (rows == 0) return SB_OK;
   return cuda_check(sb::launch_wire_unpack((const uint8_t*)q, scale, rows, dim, y, (cudaStream_t)stream), "wire_unpack");
+}
+
+int sb_residual_rmsnorm(void* x, const void* y, int64_t rows, int64_t dim, const float* weight, float eps, void* out,
+                        void* stream) {
+  if (!x) return fail(SB_ERR_ARG, "residual_rmsnorm: x is NULL");
+  if (rows < 0 || rows > (1 << 30) || dim <= 0 || dim % 8)
+    return fail(SB_ERR_SHAPE, "residual_rmsnorm: need rows >= 0 and dim a positive multiple of 8 (rows=%lld dim=%lld)",
+                (long long)rows, (long long)dim);
+  if (!aligned16(x) || !aligned16(y) || !aligned16(out)) return fail(SB_ERR_ARG, "residual_rmsnorm: 16-byte alignment");
+  if (!(eps >= 0.f)) return fail(SB_ERR_ARG, "residual_rmsnorm: eps must be >= 0");
+  if (rows == 0) return SB_OK;
+  return cuda_check(sb::launch_residual_rmsnorm(x, y, rows, dim, weight, eps, out, (cudaStream_t)stream),
+                    "residual_rmsnorm");
 }
 
 int sb_debug_set_wait_limit(int64_t polls) {

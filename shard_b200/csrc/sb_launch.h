@@ -136,6 +136,7 @@ struct PanelArgs {
   float* apanel;
   int* kzero;               // counters of the next grouped launch's K pieces, zeroed here (or NULL)
   int nkzero;
+  int* zero_err;            // the next grouped launch's error flag, cleared here (or NULL)
   int hot_min;              // hybrid dispatch: routed experts with >= hot_min tokens are skipped
   int hpad;                 // W2: h rows in the prefill kernel's padded row space (hybrid),
   int hsh0;                 // the shared expert's first h row there
@@ -188,6 +189,8 @@ cudaError_t launch_wide_h_raw(const __nv_bfloat16* hbf, int64_t rows, int64_t r_
 cudaError_t launch_combine_weighted(const __nv_bfloat16* o, const float* topk_w, int m, int topk, int h,
                                     __nv_bfloat16* y, cudaStream_t st);
 cudaError_t launch_wire_pack(const void* x, int64_t rows, int64_t dim, uint8_t* q, void* s, cudaStream_t st);
+cudaError_t launch_residual_rmsnorm(void* x, const void* y, int64_t rows, int64_t dim, const float* w, float eps,
+                                    void* out, cudaStream_t st);
 cudaError_t launch_wire_unpack(const uint8_t* q, const void* s, int64_t rows, int64_t dim, void* y, cudaStream_t st);
 cudaError_t launch_combine_pack(const __nv_bfloat16* o, const int32_t* topk_idx, int m, int topk, int h,
                                 int has_shared, __nv_bfloat16* y, uint8_t* q, __nv_bfloat16* s, cudaStream_t st);

@@ -869,8 +869,11 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
   const int P = a.m * a.topk;
   pdl_wait();
   pdl_trigger();
-  if (a.kzero != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
-    for (int i = threadIdx.x; i < a.nkzero; i += blockDim.x) a.kzero[i] = 0;
+  if (blockIdx.x == 0 && blockIdx.y == 0) {
+    if (a.kzero != nullptr)
+      for (int i = threadIdx.x; i < a.nkzero; i += blockDim.x) a.kzero[i] = 0;
+    if (a.zero_err != nullptr && threadIdx.x == 0) *a.zero_err = 0;
+  }
   int shared, cnt, base, pass0, nv;
   int hrow0 = -1;   // W2, hybrid: first h row of the expert in the padded row space
   if (slot < a.has_shared) {

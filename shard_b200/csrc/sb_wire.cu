@@ -236,4 +236,70 @@ cudaError_t launch_combine_pack(const __nv_bfloat16* o, const int32_t* topk_idx,
   return launch_pdl(combine_pack_kernel<16>, grid, block, 0, st, o, topk_idx, m, topk, h, has_shared, y, q, s);
 }
 
+
+// ── the block around the MoE operator: residual add and RMSNorm (model.py:189-202, 701-706) ──
+// One CTA per row: x <- bf16(x + y) (when y is given), then out = bf16(w * (x * rsqrt(mean(x^2) +
+// eps))) in fp32 (w = 1 when not given), as RMSNorm.forward computes it on the bf16 residual stream.
+__global__ void __launch_bounds__(WIRE_THREADS) residual_rmsnorm_kernel(uint16_t* __restrict__ x,
+                                                                        const uint16_t* __restrict__ y, int64_t dim,
+                                                                        const float* __restrict__ w, float eps,
+                                                                        uint16_t* __restrict__ out) {
+  __shared__ float red[WIRE_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  uint16_t* xr = x + row * dim;
+  float ss = 0.f;
+  for (int64_t v = threadIdx.x; v < dim / 8; v += blockDim.x) {
+    uint4 a = reinterpret_cast<const uint4*>(xr)[v];
+    if (y != nullptr) {
+      const uint4 b = reinterpret_cast<const uint4*>(y + row * dim)[v];
+      __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
+      const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fa = __bfloat1622float2(pa[e]), fb = __bfloat1622float2(pb[e]);
+        pa[e] = __floats2bfloat162_rn(fa.x + fb.x, fa.y + fb.y);
+      }
+      reinterpret_cast<uint4*>(xr)[v] = a;
+    }
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(pa[e]);
+      ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+    }
+  }
+  if (out == nullptr) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < WIRE_THREADS / 32; ++i) tot += red[i];
+  const float r = rsqrtf(tot / (float)dim + eps);
+  for (int64_t v = threadIdx.x; v < dim / 8; v += blockDim.x) {
+    // this thread's own writes of x above: re-read them
+    const uint4 a = reinterpret_cast<const uint4*>(xr)[v];
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+    uint4 o4;
+    __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o4);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(pa[e]);
+      const float w0 = w != nullptr ? w[v * 8 + 2 * e] : 1.f, w1 = w != nullptr ? w[v * 8 + 2 * e + 1] : 1.f;
+      po[e] = __floats2bfloat162_rn(w0 * (f.x * r), w1 * (f.y * r));
+    }
+    reinterpret_cast<uint4*>(out + row * dim)[v] = o4;
+  }
+}
+
+cudaError_t launch_residual_rmsnorm(void* x, const void* y, int64_t rows, int64_t dim, const float* w, float eps,
+                                    void* out, cudaStream_t st) {
+  return launch_pdl(residual_rmsnorm_kernel, dim3((unsigned)rows), dim3(WIRE_THREADS), 0, st, (uint16_t*)x,
+                    (const uint16_t*)y, dim, w, eps, (uint16_t*)out);
+}
+
 }  // namespace sb

@@ -40,14 +40,31 @@ def even_tiling(n_layers: int, n_stages: int) -> List[range]:
 
 class StageStack:
     """The layers one stage owns, run in order. Each layer is a MoELayer (or anything callable
-    x -> y with the same [M, H] bf16 shape)."""
+    x -> y with the same [M, H] bf16 shape).
 
-    def __init__(self, layers: Sequence):
+    residual=False chains the operators (x <- layer(x)). residual=True runs each layer as the ffn half
+    of the reference block (model.py:701-706, hyper-connections aside): x <- x + layer(RMSNorm(x)),
+    with the add and the norm fused in one kernel (shard_b200.wire.residual_rmsnorm; CUDA tensors).
+    Chained random-weight MoE layers drive every token onto the same experts within ~10 layers; the
+    residual stream and the norm keep a synthetic stack's routing as spread as its first layer's."""
+
+    def __init__(self, layers: Sequence, residual: bool = False, eps: float = 1e-6):
         self.layers = list(layers)
+        self.residual = residual
+        self.eps = eps
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not self.residual:
+            for layer in self.layers:
+                x = layer.forward(x)
+            return x
+        from .wire import residual_rmsnorm
+        x = x.clone()            # the residual stream; the caller's chunk is left as it is
+        y = None
         for layer in self.layers:
-            x = layer.forward(x)
+            y = layer.forward(residual_rmsnorm(x, y, eps=self.eps))
+        if y is not None:
+            residual_rmsnorm(x, y, norm=False)
         return x
 
     __call__ = forward
@@ -55,6 +72,8 @@ class StageStack:
     def forward_wire(self, x: torch.Tensor, pack):
         """The stack's output in the FP8 wire form: the last layer emits it directly when it can,
         otherwise `pack` is applied to the output."""
+        if self.residual:
+            return pack(self.forward(x))
         for layer in self.layers[:-1]:
             x = layer.forward(x)
         last = self.layers[-1] if self.layers else None

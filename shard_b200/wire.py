@@ -12,6 +12,8 @@ there is no CPU path.
 """
 from __future__ import annotations
 
+from typing import Optional
+
 import torch
 
 from ._lib import check, lib, ptr, stream_ptr
@@ -38,6 +40,24 @@ def unpack(q: torch.Tensor, scale: torch.Tensor, stream=None) -> torch.Tensor:
     y = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
     check(lib().sb_wire_unpack(ptr(q), ptr(scale), rows, dim, ptr(y), stream_ptr(stream)), "sb_wire_unpack")
     return y
+
+
+def residual_rmsnorm(x: torch.Tensor, y: Optional[torch.Tensor] = None, weight: Optional[torch.Tensor] = None,
+                     eps: float = 1e-6, norm: bool = True, stream=None) -> Optional[torch.Tensor]:
+    """The block around the MoE operator (model.py:701-706, hyper-connections aside): x (bf16, the
+    residual stream, updated in place) += y when given; returns RMSNorm(x) (model.py:197-202) in bf16,
+    or None when norm is False (the add alone)."""
+    assert x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous(), "residual_rmsnorm: contiguous bf16 CUDA x"
+    dim = x.shape[-1]
+    rows = x.numel() // dim
+    if y is not None:
+        assert y.dtype == torch.bfloat16 and y.shape == x.shape
+        y = y.contiguous()
+    w = None if weight is None else weight.float().contiguous()
+    out = torch.empty_like(x) if norm else None
+    check(lib().sb_residual_rmsnorm(ptr(x), ptr(y), rows, dim, ptr(w), float(eps), ptr(out), stream_ptr(stream)),
+          "sb_residual_rmsnorm")
+    return out
 
 
 # the reference's names (v4_pipe.py:335, :379)
