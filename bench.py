@@ -4,7 +4,8 @@ Workload (all N): the V4-Flash-shaped MoE layer of config c1 (H=4096, 256 routed
 I=2048, NVFP4 routed experts, FP8 128x128 shared expert, sigmoid router), verify chunks of M=16
 tokens, 6 distinct layers per GPU. At N GPUs the 6N-layer stack is pipeline-partitioned into
 contiguous 6-layer blocks, one per rank (N=8 is config c2's 48 layers), with NCCL send/recv of the
-bf16 activations between stages and 8 chunks streamed per step. Per-GPU work is fixed: weak scaling.
+bf16 activations between stages and 16 chunks streamed per step (4 in flight per hop). Per-GPU work
+is fixed: weak scaling.
 Each layer runs as the reference block's ffn half, x + moe(rmsnorm(x)) (the residual add and the norm
 fused in one kernel of this library), so the routing stays as spread deep in the stack as at its
 first layer.
@@ -47,7 +48,10 @@ HEADLINE_M = 16
 LAYERS_PER_GPU = 6
 N_EXPERTS = None       # --experts: fewer routed experts per layer (the small case for ncu captures)
 PREFILL = 0            # --prefill: expert-kernel choice of the tensor-core layout (0 by batch size)
-CHUNKS_PER_STEP = 8
+# chunks per step: the timed region starts and ends with the pipeline empty (a barrier on each side),
+# so N stages lose N-1 chunk times of fill and drain per timed region; 16 chunks a step keep that
+# under 5% of 10 steps at 8 GPUs
+CHUNKS_PER_STEP = 16
 METRIC = "MoE stage tokens/s (token-layers/s), verify M=16, c1/c2 V4-Flash MoE layer"
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum of one forward's W13 and W2 grouped
 # launches) over that forward's algorithmic bytes, from one capture of the small case
