@@ -202,8 +202,9 @@ __device__ __forceinline__ BGeom bgeom(int pc, int nb) {
 
 // ── the prefill kernel ──
 namespace x {
-constexpr int NTHREADS = 32 * (NWORK + 3);
-constexpr int PRODUCER_WARP = NWORK, MMA_WARP = NWORK + 1, TLOAD_WARP = NWORK + 2;
+constexpr int NEPI = 4;                      // epilogue warps: one per TMEM lane quarter (token = lane)
+constexpr int NTHREADS = 32 * (NWORK + 3 + NEPI);
+constexpr int PRODUCER_WARP = NWORK, MMA_WARP = NWORK + 1, TLOAD_WARP = NWORK + 2, EPI_WARP0 = NWORK + 3;
 constexpr int ROWS = 256;                    // weight rows per item (two 128-row blocks) = MMA N
 constexpr int SC = 3;                        // staging ring: one stage of both row blocks per slot
 constexpr int SW = 3;                        // f16 weight tiles (64 K each)
@@ -217,7 +218,7 @@ struct Smem {
   uint8_t W[SW][W_BYTES];                    // 1024-aligned (128B swizzle atoms)
   uint8_t T[STT][T_BYTES];
   uint8_t stg[SC][2 * STG_RB];
-  float ca[ROWS];                            // FP8: c_A of each weight row of the current item
+  float ca[2][ROWS];                         // FP8: c_A of each weight row, per accumulator buffer
   uint64_t sfull[SC], sempty[SC], wfull[SW], wempty[SW], tfull[STT], tempty[STT], accfull[2], accempty[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_addr(&sm.accfull[s]), 1);
-      mbar_init(smem_addr(&sm.accempty[s]), NWORK);
+      mbar_init(smem_addr(&sm.accempty[s]), NEPI);
     }
     mbar_init(smem_addr(&sm.drain), 1);
     sm.abort = 0;
@@ -419,8 +420,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
         if (mbar_try_wait_sleep(smem_addr(&sm.drain), 0, 1000u)) break;
     }
     __syncwarp();
-  } else {
-    // ── convert (thread t = weight row t of the item's 256) + epilogue (lane = token) ──
+  } else if (warp < NWORK) {
+    // ── convert (thread t = weight row t of the item's 256) ──
     const int t = tid, hb = t >> 7, r = t & 127;
     uint32_t c = 0, gw = 0, np = 0;
     bool ok = true;
@@ -433,38 +434,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pc = pass_tokens(it);
       const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
-      // the epilogue's per-token values (lane = token (32 (warp & 3) + lane), the warp half hh takes
-      // row block 2 rb + hh), loaded now so that their latency hides behind the item's conversion
-      const int hh = warp >> 2;
-      const int tok = (warp & 3) * 32 + lane;
-      const bool valid = tok < pc;
-      const int rb = 2 * it.rb + hh;
-      float cb = 1.f, wgt = 1.f;
-      int orow = 0;
-      if (valid) {
-        const int i = it.pb + tok;
-        cb = wa.cvec[brow0 + tok];
-        if (w13) {
-          orow = brow0 + tok;
-          if (!it.shared) {
-            const int qp = it.base + i;
-            wgt = a.topk_w[(size_t)a.pair_tok[qp] * a.topk + a.pair_slot[qp]];
-          }
-        } else if (it.shared) {
-          orow = P + i;
-        } else {
-          const int qp = it.base + i;
-          orow = a.pair_tok[qp] * a.topk + a.pair_slot[qp];
-        }
-      }
-      float ts0 = 1.f, ts1 = 1.f;   // NVFP4 tensor scales: w1 (or w2) rows, w3 rows
-      if (fmt == FMT_NVFP4 && ws.ts != nullptr) {
-        const float* tsp = ws.ts + (it.shared ? 0 : (size_t)it.expert * ws.ts_stride);
-        ts0 = tsp[0];
-        ts1 = w13 ? tsp[1] : tsp[0];
-      }
+      // ca[buf] is read by the epilogue of the item two before this one: wait until it is done
+      const uint32_t cbuf = np & 1u;
+      if (ok) ok = __all_sync(0xffffffffu, wait(smem_addr(&sm.accempty[cbuf]), ((np >> 1) & 1u) ^ 1u));
       float ica = 1.f;
-      if (fmt != FMT_FP8) sm.ca[t] = 1.f;
+      if (fmt != FMT_FP8) sm.ca[cbuf][t] = 1.f;
       const int nstg = fp4 ? nst : nsub;
       for (int st = 0; st < nstg; ++st, ++c) {
         const uint32_t s = c % SC;
@@ -476,7 +450,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
           if (st == 0) {
             const float ca = sw > 0.f ? sw * 16.f : 1.f;
             ica = 1.f / ca;
-            sm.ca[t] = ca;
+            sm.ca[cbuf][t] = ca;
           }
           s2 = f16_splat(sw * ica);
         }
@@ -513,77 +487,118 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
         __syncwarp();
         if (ok && lane == 0) arrive(smem_addr(&sm.sempty[s]));
       }
-      // epilogue: TMEM lane = token (32 (warp & 3) + lane), the warp half hh takes row block 2 rb + hh
+    }
+  } else {
+    // ── epilogue (warps EPI_WARP0..): TMEM lane = token 32 (warp & 3) + lane, both row blocks of the
+    // item in turn; it runs while the converters and the MMA work on the next item ──
+    const int tok = (warp & 3) * 32 + lane;
+    uint32_t np = 0;
+    bool ok = true;
+    Item nxt = blockIdx.x < n_items ? item_of(a, wa.plan, blockIdx.x, nrp, wn) : Item{};
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++np) {
+      const Item it = nxt;
+      if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrp, wn);
+      const int fmt = item_fmt(it);
+      const WeightSet& ws = it.shared ? a.shared : a.routed;
+      const int pc = pass_tokens(it);
+      const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
+      // the per-token values first: their latency overlaps the wait for the accumulator
+      const bool valid = tok < pc;
+      float cb = 1.f, wgt = 1.f;
+      int orow = 0;
+      if (valid) {
+        const int i = it.pb + tok;
+        cb = wa.cvec[brow0 + tok];
+        if (w13) {
+          orow = brow0 + tok;
+          if (!it.shared) {
+            const int qp = it.base + i;
+            wgt = a.topk_w[(size_t)a.pair_tok[qp] * a.topk + a.pair_slot[qp]];
+          }
+        } else if (it.shared) {
+          orow = P + i;
+        } else {
+          const int qp = it.base + i;
+          orow = a.pair_tok[qp] * a.topk + a.pair_slot[qp];
+        }
+      }
+      float ts0 = 1.f, ts1 = 1.f;   // NVFP4 tensor scales: w1 (or w2) rows, w3 rows
+      if (fmt == FMT_NVFP4 && ws.ts != nullptr) {
+        const float* tsp = ws.ts + (it.shared ? 0 : (size_t)it.expert * ws.ts_stride);
+        ts0 = tsp[0];
+        ts1 = w13 ? tsp[1] : tsp[0];
+      }
       const uint32_t buf = np & 1u;
       if (ok) ok = __all_sync(0xffffffffu, cwait(smem_addr(&sm.accfull[buf]), (np >> 1) & 1u));
-      if (bar_any(1, 32 * NWORK, !ok || *abort_flag)) break;
+      if (bar_any(2, 32 * NEPI, !ok || *abort_flag)) break;
       fence_after();
-      const uint32_t taddr = tbase + ((uint32_t)((warp & 3) * 32) << 16) + buf * ROWS + 128 * hh;
-      const float* cav = sm.ca + 128 * hh;
-      if (w13) {
-        const int I = a.n_rows / 2;
-        const float lim = a.swiglu_limit;
+      for (int hh = 0; hh < 2; ++hh) {
+        const int rb = 2 * it.rb + hh;
+        const uint32_t taddr = tbase + ((uint32_t)((warp & 3) * 32) << 16) + buf * ROWS + 128 * hh;
+        const float* cav = sm.ca[buf] + 128 * hh;
+        if (w13) {
+          const int I = a.n_rows / 2;
+          const float lim = a.swiglu_limit;
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 32) {
-          uint32_t gd[32], ud[32];
-          ld32(taddr + c0, gd);
-          ld32(taddr + 64 + c0, ud);
-          ld_wait();
-          uint32_t hv[16];
+          for (int c0 = 0; c0 < 64; c0 += 32) {
+            uint32_t gd[32], ud[32];
+            ld32(taddr + c0, gd);
+            ld32(taddr + 64 + c0, ud);
+            ld_wait();
+            uint32_t hv[16];
 #pragma unroll
-          for (int q = 0; q < 32; q += 2) {
-            float h2[2];
+            for (int q = 0; q < 32; q += 2) {
+              float h2[2];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              float gv = bf16_round(__uint_as_float(gd[q + e]) * cb * (cav[c0 + q + e] * ts0));
-              float uv = bf16_round(__uint_as_float(ud[q + e]) * cb * (cav[64 + c0 + q + e] * ts1));
-              float hvv;
-              if (a.activation == ACT_SITU) {
-                hvv = situ(gv, uv, a.act_beta, a.act_lbeta);
-              } else {
-                if (lim > 0.f) {
-                  uv = fminf(fmaxf(uv, -lim), lim);
-                  gv = fminf(gv, lim);
+              for (int e = 0; e < 2; ++e) {
+                float gv = bf16_round(__uint_as_float(gd[q + e]) * cb * (cav[c0 + q + e] * ts0));
+                float uv = bf16_round(__uint_as_float(ud[q + e]) * cb * (cav[64 + c0 + q + e] * ts1));
+                float hvv;
+                if (a.activation == ACT_SITU) {
+                  hvv = situ(gv, uv, a.act_beta, a.act_lbeta);
+                } else {
+                  if (lim > 0.f) {
+                    uv = fminf(fmaxf(uv, -lim), lim);
+                    gv = fminf(gv, lim);
+                  }
+                  hvv = silu(gv) * uv;
                 }
-                hvv = silu(gv) * uv;
+                if (!it.shared && !a.weight_after) hvv = wgt * hvv;
+                h2[e] = hvv;
               }
-              if (!it.shared && !a.weight_after) hvv = wgt * hvv;
-              h2[e] = hvv;
+              const __nv_bfloat162 b = __floats2bfloat162_rn(h2[0], h2[1]);
+              hv[q / 2] = *reinterpret_cast<const uint32_t*>(&b);
             }
-            const __nv_bfloat162 b = __floats2bfloat162_rn(h2[0], h2[1]);
-            hv[q / 2] = *reinterpret_cast<const uint32_t*>(&b);
+            if (valid) {
+              uint4* dst = reinterpret_cast<uint4*>(a.hbf + (size_t)orow * I + rb * 64 + c0);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(hv[4 * v], hv[4 * v + 1], hv[4 * v + 2], hv[4 * v + 3]);
+            }
           }
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(a.hbf + (size_t)orow * I + rb * 64 + c0);
+        } else {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(hv[4 * v], hv[4 * v + 1], hv[4 * v + 2], hv[4 * v + 3]);
-          }
-        }
-      } else {
+          for (int c0 = 0; c0 < 128; c0 += 32) {
+            uint32_t d[32];
+            ld32(taddr + c0, d);
+            ld_wait();
+            uint32_t ov[16];
 #pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t d[32];
-          ld32(taddr + c0, d);
-          ld_wait();
-          uint32_t ov[16];
+            for (int q = 0; q < 32; q += 2) {
+              const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(d[q]) * cb * (cav[c0 + q] * ts0),
+                                                             __uint_as_float(d[q + 1]) * cb * (cav[c0 + q + 1] * ts0));
+              ov[q / 2] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+            if (valid) {
+              uint4* dst = reinterpret_cast<uint4*>(a.o + (size_t)orow * a.n_rows + rb * 128 + c0);
 #pragma unroll
-          for (int q = 0; q < 32; q += 2) {
-            const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(d[q]) * cb * (cav[c0 + q] * ts0),
-                                                           __uint_as_float(d[q + 1]) * cb * (cav[c0 + q + 1] * ts0));
-            ov[q / 2] = *reinterpret_cast<const uint32_t*>(&b);
-          }
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(a.o + (size_t)orow * a.n_rows + rb * 128 + c0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(ov[4 * v], ov[4 * v + 1], ov[4 * v + 2], ov[4 * v + 3]);
+              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(ov[4 * v], ov[4 * v + 1], ov[4 * v + 2], ov[4 * v + 3]);
+            }
           }
         }
       }
       fence_before();
       __syncwarp();
       if (lane == 0) arrive(smem_addr(&sm.accempty[buf]));
-      // the next item's converters overwrite ca: every thread has read it
-      bar_sync(1, 32 * NWORK);
     }
   }
   fence_before();
