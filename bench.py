@@ -425,7 +425,8 @@ def run_c4_pipeline(args, rank, world, device):
     import datetime  # noqa: F401
     import torch.distributed as dist
     from shard_b200.pipeline import Pipeline, StageStack, even_tiling
-    blocks = even_tiling(C4_LAYERS, world)
+    n_layers = args.c4_layers
+    blocks = even_tiling(n_layers, world)
     mine = blocks[rank]
     free, _ = torch.cuda.mem_get_info(device)
     from shard_b200 import formats as F
@@ -473,13 +474,14 @@ def run_c4_pipeline(args, rank, world, device):
     torch.cuda.synchronize()
     if rank == 0:
         tokens = args.steps * C * m
-        line = {"metric": "c4 MoE stack tokens/s (61 layers, prefill chunks)", "value": tokens / t, "unit": "tokens/s",
+        line = {"metric": f"c4 MoE stack tokens/s ({n_layers} layers, prefill chunks)", "value": tokens / t,
+                "unit": "tokens/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": t / args.steps * 1000.0, "higher_is_better": True, "scaling": "strong",
-                "token_layers_per_s": tokens * C4_LAYERS / t, "dtype": "nvfp4", "data": "synthetic",
-                "config": {"workload": f"c4 61-layer MoE stack, pp{world} (even_tiling: "
+                "token_layers_per_s": tokens * n_layers / t, "dtype": "nvfp4", "data": "synthetic",
+                "config": {"workload": f"c4 {n_layers}-layer MoE stack, pp{world} (even_tiling: "
                                        f"{[len(b) for b in blocks]}), M={m} chunks, {C} chunks per step",
-                           "m": m, "layers": C4_LAYERS, "layers_per_rank": [len(b) for b in blocks],
+                           "m": m, "layers": n_layers, "layers_per_rank": [len(b) for b in blocks],
                            "distinct_banks_per_rank": min(distinct, len(mine)), "chunks_per_step": C,
                            "pipeline_depth": pipe.depth, "parallelism": f"pp{world}",
                            "block": "x + moe(rmsnorm(x)) per layer",
@@ -664,13 +666,17 @@ def main():
     ap.add_argument("--m", type=int, default=HEADLINE_M,
                     help="tokens per chunk (default 16, the headline; larger M with fewer --experts is the "
                          "small case for ncu captures of the prefill kernel)")
-    ap.add_argument("--prefill", type=int, choices=[0, 1, 2], default=0,
-                    help="expert kernel on the tensor-core layout: 0 by batch size, 1 verify, 2 prefill")
+    ap.add_argument("--prefill", type=int, choices=[0, 1, 2, 3], default=0,
+                    help="expert kernels on the tensor-core layout: 0 by batch size, 1 verify, 2 prefill, "
+                         "3 hybrid dispatch")
     ap.add_argument("--config", choices=["c1", "c4"], default="c1",
                     help="c1: the headline (c1 layers, verify chunks, weak scaling); c4: the 61-layer "
                          "Kimi-K3-scale stack split over the GPUs with prefill chunks (--m, default 256)")
     ap.add_argument("--distinct", type=int, default=None,
                     help="c4: distinct layer banks per rank (default: as many as fit in 60%% of free HBM)")
+    ap.add_argument("--c4-layers", type=int, default=C4_LAYERS,
+                    help="c4: layers of the stack (default 61; a shorter stack is the small case for "
+                         "launch-list captures)")
     args = ap.parse_args()
     if args.layout is not None:
         import shard_b200.moe as sbm
