@@ -88,8 +88,9 @@ struct Workspace {
 // kernel converts them (measured at c3's shapes).
 enum Kernels { K_VERIFY = 0, K_WIDE = 1, K_HYBRID = 2 };
 constexpr int64_t HYBRID_TOKENS_PER_EXPERT = 4;
-// the tensor-core gate takes batches of >= 16 tokens per expert (and every batch of a forced prefill)
-constexpr int64_t WIDE_TOKENS_PER_EXPERT = 16;
+// the tensor-core gate takes the hybrid dispatch's batches of >= 128 tokens (one full tile; at c4's
+// M=256 the CUDA-core gate GEMV took 8% of the forward) and every batch of a forced prefill kernel
+constexpr int64_t TC_GATE_MIN_TOKENS = 128;
 int kernels(const sb_moe_layer* L, int64_t m) {
   if (L->mode == SB_MODE_K3) return K_WIDE;   // 16-bit activations: the prefill kernel at every size
   if (L->layout != SB_LAYOUT_TC || L->prefill == SB_PREFILL_VERIFY) return K_VERIFY;
@@ -101,7 +102,7 @@ int kernels(const sb_moe_layer* L, int64_t m) {
 bool use_wide(const sb_moe_layer* L, int64_t m) { return kernels(L, m) == K_WIDE; }
 bool use_hybrid(const sb_moe_layer* L, int64_t m) { return kernels(L, m) == K_HYBRID; }
 bool tc_gate(const sb_moe_layer* L, int64_t m) {
-  return use_wide(L, m) || (use_hybrid(L, m) && m * L->topk >= WIDE_TOKENS_PER_EXPERT * (int64_t)L->n_experts);
+  return use_wide(L, m) || (use_hybrid(L, m) && m >= TC_GATE_MIN_TOKENS);
 }
 
 // Tokens per pass of a routed expert and of the shared expert. The prefill kernel takes passes of
