@@ -98,6 +98,8 @@ struct GroupedArgs {
   int kstages;         // stages (128 K) per piece, a multiple of the kernel's unit of 2
   float* part;         // ksplit > 1: fp32 partials [n_sh_pass * nrb][ksplit][128 rows][16]
   int* kcnt;           // ksplit > 1: [n_sh_pass * nrb] pieces finished (zeroed by the panel kernel)
+  int* sched;          // verify kernel: launch-wide item counter (zeroed beforehand), or NULL for a
+                       // round-robin schedule
   int hpad;            // verify kernel, W13: h rows in the prefill kernel's padded row space (hybrid),
   int hsh0;            // the shared expert's first h row there
 };
@@ -137,6 +139,7 @@ struct PanelArgs {
   int* kzero;               // counters of the next grouped launch's K pieces, zeroed here (or NULL)
   int nkzero;
   int* zero_err;            // the next grouped launch's error flag, cleared here (or NULL)
+  int* zero_sched;          // the next grouped launch's item counter, cleared here (or NULL)
   int hot_min;              // hybrid dispatch: routed experts with >= hot_min tokens are skipped
   int hpad;                 // W2: h rows in the prefill kernel's padded row space (hybrid),
   int hsh0;                 // the shared expert's first h row there

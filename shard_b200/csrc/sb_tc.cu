@@ -55,6 +55,13 @@ constexpr int SF_SRC = 512;      // one scale-factor copy source: 32 rows x 16 B
 constexpr int SF_A_COL = 64;     // block-scaled items: TMEM columns of the group holding the weight
 constexpr int SF_B_COL = 68;     // and activation scale factors (the accumulator is columns 0-15)
 
+// One item: (expert or shared expert / dense matrix, 128-row block, pass), and its K range.
+struct Item {
+  int shared, expert, rb, cnt, base, pb, pass;
+  int ks, kn, j0, j1;   // piece ks of kn, stages [j0, j1)
+};
+constexpr int IQ = 4;           // dynamic schedule: items queued from the producer to the other roles
+
 struct Smem {
   uint8_t A[ST][A_BYTES];       // 1024-aligned (128B swizzle atoms)
   uint8_t B[ST][B_BYTES];
@@ -67,6 +74,8 @@ struct Smem {
   uint32_t tmem_base;
   int abort;
   int klast;                    // K pieces: this CTA's piece was the last of its block to finish
+  Item iq[IQ];                  // dynamic schedule: the producer's items in order (pass < 0: the end)
+  uint64_t iqfull[IQ], iqempty[IQ];
   __nv_bfloat16 xchg[64][18];   // W13 epilogue: the up rows' bf16 values
 };
 constexpr int SMEM_BYTES = (int)sizeof(Smem) + 1024;
@@ -231,10 +240,6 @@ __device__ __forceinline__ bool workers_any(bool pred) {
 // routed items following unsplit. Each piece writes its fp32 partial accumulator to the workspace
 // and counts itself in; the last piece of a (pass, row block) to finish sums the pieces in K order
 // and runs the epilogue. This occupies the GPU when a dense matrix has few row blocks.
-struct Item {
-  int shared, expert, rb, cnt, base, pb, pass;
-  int ks, kn, j0, j1;   // piece ks of kn, stages [j0, j1)
-};
 
 template <int FMT_R>
 __device__ __forceinline__ Item item_of(const GroupedArgs& a, const TcPlan& plan, int item, int nrb, int nst) {
@@ -309,6 +314,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
       mbar_init(smem_addr(&sm.gfull[q]), 1);
       mbar_init(smem_addr(&sm.gempty[q]), 4);
     }
+    for (int q = 0; q < IQ; ++q) {
+      mbar_init(smem_addr(&sm.iqfull[q]), 1);
+      mbar_init(smem_addr(&sm.iqempty[q]), 5);   // the MMA warp and the 4 readback warps
+    }
     mbar_init(smem_addr(&sm.drain), 1);
     sm.abort = 0;
     mbar_init_fence();
@@ -334,6 +343,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
                      (a.mode == MODE_DENSE ? 0 : ta.plan.pass_off[*a.n_active]);
   const int n_items = n_pass * nrb + (a.ksplit > 1 && a.has_shared ? ta.plan.n_sh_pass * nrb * (a.ksplit - 1) : 0);
   const bool w13 = a.mode == MODE_W13;
+  const bool dyn = a.sched != nullptr;   // items from the launch-wide counter (zeroed by the panel kernel)
   // the limit of the consumer-side waits (the MMA issuer's and the readback's); the producer's waits
   // for free slots and the final drains keep WAIT_LIMIT
   const uint32_t clim = a.wait_limit ? a.wait_limit : WAIT_LIMIT;
@@ -352,13 +362,40 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
       prefetch_map(&ta.map_shared);
     }
     __syncwarp();
-    uint32_t g = 0, u = 0;
+    uint32_t g = 0, u = 0, qn = 0;
     bool ok = true;
-    // the next item's descriptor is loaded one item ahead, so its global loads overlap this item
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb, nst) : Item{};
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+    // Items come from a launch-wide counter when the launch has one (each CTA takes the next item as
+    // it gets to it, so CTAs that drew heavier items take fewer), else round-robin. The next item's
+    // index and descriptor are fetched one item ahead, so their global loads overlap this item.
+    auto fetch = [&]() -> int {
+      int v = 0;
+      if (lane == 0) v = atomicAdd(a.sched, 1);
+      return __shfl_sync(0xffffffffu, v, 0);
+    };
+    int item = dyn ? fetch() : (int)blockIdx.x;
+    Item nxt = item < n_items ? item_of<FMT_R>(a, ta.plan, item, nrb, nst) : Item{};
+    while (ok) {
+      if (dyn) {
+        // publish the item (or the end) to the MMA issuer and the readback
+        const uint32_t qs = qn % IQ;
+        if (!warp_wait(sm, err, smem_addr(&sm.iqempty[qs]), ((qn / IQ) & 1u) ^ 1u)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          Item e = nxt;
+          if (item >= n_items) e.pass = -1;
+          sm.iq[qs] = e;
+          arrive(smem_addr(&sm.iqfull[qs]));
+        }
+        __syncwarp();
+        ++qn;
+      }
+      if (item >= n_items) break;
       const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
+      const int next = dyn ? fetch() : item + (int)gridDim.x;
+      if (next < n_items) nxt = item_of<FMT_R>(a, ta.plan, next, nrb, nst);
+      item = next;
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const CUtensorMap* map = it.shared ? &ta.map_shared : &ta.map_routed;
@@ -415,12 +452,29 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   } else if (warp == MMA_WARP) {
     // the whole warp runs the loop (uniform control flow); one elected lane issues MMAs and commits.
     // g counts stages, u units, gq accumulator groups (one per unit, or one per block-scaled item)
-    uint32_t g = 0, u = 0, gq = 0;
+    uint32_t g = 0, u = 0, gq = 0, qn = 0;
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb, nst) : Item{};
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
+    int item = blockIdx.x;
+    Item nxt = !dyn && item < n_items ? item_of<FMT_R>(a, ta.plan, item, nrb, nst) : Item{};
+    while (ok) {
+      Item it;
+      if (dyn) {
+        const uint32_t qs = qn % IQ;
+        if (!warp_wait<PROBE>(sm, err, smem_addr(&sm.iqfull[qs]), (qn / IQ) & 1u, clim)) {
+          ok = false;
+          break;
+        }
+        it = sm.iq[qs];
+        __syncwarp();
+        if (lane == 0) arrive(smem_addr(&sm.iqempty[qs]));
+        ++qn;
+        if (it.pass < 0) break;
+      } else {
+        if (item >= n_items) break;
+        it = nxt;
+        if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
+        item += gridDim.x;
+      }
       const int fmt = item_fmt(it);
       if (block_scaled(fmt)) {
         // the whole K into one 16-column accumulator; per stage the weight and activation scale
@@ -536,12 +590,28 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
   } else {
     // ── readback + epilogue (warps 0-3) ──
     const int r = tid;  // weight row of the item = TMEM lane
-    uint32_t u = 0, gq = 0;
+    uint32_t u = 0, gq = 0, qn = 0;
     bool ok = true;
-    Item nxt = blockIdx.x < n_items ? item_of<FMT_R>(a, ta.plan, blockIdx.x, nrb, nst) : Item{};
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-      const Item it = nxt;
-      if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
+    int item = blockIdx.x;
+    Item nxt = !dyn && item < n_items ? item_of<FMT_R>(a, ta.plan, item, nrb, nst) : Item{};
+    for (;;) {
+      Item it;
+      if (dyn) {
+        const uint32_t qs = qn % IQ;
+        if (ok) ok = warp_wait<PROBE>(sm, err, smem_addr(&sm.iqfull[qs]), (qn / IQ) & 1u, clim);
+        // one decision for all four warps (the epilogue's named barriers need all of them)
+        if (workers_any(!ok)) break;
+        it = sm.iq[qs];
+        __syncwarp();
+        if (lane == 0) arrive(smem_addr(&sm.iqempty[qs]));
+        ++qn;
+        if (it.pass < 0) break;
+      } else {
+        if (item >= n_items) break;
+        it = nxt;
+        if (item + (int)gridDim.x < n_items) nxt = item_of<FMT_R>(a, ta.plan, item + gridDim.x, nrb, nst);
+        item += gridDim.x;
+      }
       const int fmt = item_fmt(it);
       const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pm = tc_pass_max(fmt);
@@ -873,6 +943,7 @@ __global__ void __launch_bounds__(128) panel_kernel(PanelArgs a) {
     if (a.kzero != nullptr)
       for (int i = threadIdx.x; i < a.nkzero; i += blockDim.x) a.kzero[i] = 0;
     if (a.zero_err != nullptr && threadIdx.x == 0) *a.zero_err = 0;
+    if (a.zero_sched != nullptr && threadIdx.x == 0) *a.zero_sched = 0;
   }
   int shared, cnt, base, pass0, nv;
   int hrow0 = -1;   // W2, hybrid: first h row of the expert in the padded row space

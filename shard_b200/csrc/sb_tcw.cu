@@ -204,7 +204,7 @@ __device__ __forceinline__ BGeom bgeom(int pc, int nb) {
 namespace x {
 constexpr int NEPI = 4;                      // epilogue warps: one per TMEM lane quarter (token = lane)
 constexpr int NTHREADS = 32 * (NWORK + 3 + NEPI);
-constexpr int PRODUCER_WARP = NWORK, MMA_WARP = NWORK + 1, TLOAD_WARP = NWORK + 2, EPI_WARP0 = NWORK + 3;
+constexpr int PRODUCER_WARP = NWORK, MMA_WARP = NWORK + 1, TLOAD_WARP = NWORK + 2;   // then the epilogue warps
 constexpr int ROWS = 256;                    // weight rows per item (two 128-row blocks) = MMA N
 constexpr int SC = 3;                        // staging ring: one stage of both row blocks per slot
 constexpr int SW = 3;                        // f16 weight tiles (64 K each)
@@ -431,7 +431,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
       if (item + (int)gridDim.x < n_items) nxt = item_of(a, wa.plan, item + gridDim.x, nrp, wn);
       const int fmt = item_fmt(it);
       const bool fp4 = fmt != FMT_FP8;
-      const WeightSet& ws = it.shared ? a.shared : a.routed;
       const int pc = pass_tokens(it);
       const int brow0 = it.shared ? wa.sb_row + it.pb : pbase(it.base, it.expert) + it.pb;
       // ca[buf] is read by the epilogue of the item two before this one: wait until it is done
@@ -489,7 +488,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tcx_kernel(const __grid_constant_
       }
     }
   } else {
-    // ── epilogue (warps EPI_WARP0..): TMEM lane = token 32 (warp & 3) + lane, both row blocks of the
+    // ── epilogue (the last NEPI warps): TMEM lane = token 32 (warp & 3) + lane, both row blocks of the
     // item in turn; it runs while the converters and the MMA work on the next item ──
     const int tok = (warp & 3) * 32 + lane;
     uint32_t np = 0;
