@@ -1,7 +1,9 @@
 // Grouped expert GEMV/GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // One CTA walks ITEMS = (expert or shared expert, 128-row block of a weight matrix) of the
-// device-side permutation (shared expert first); an item runs its expert's token PASSES (up to 16
+// device-side permutation (shared expert first), round-robin or, when the launch has an item
+// counter, taking the next item as it gets to it (the producer fetches and hands each item to the
+// other roles through a small shared-memory queue); an item runs its expert's token PASSES (up to 16
 // B rows each) over the K stages (128 K per stage). Roles (192 threads):
 //   warp 4     producer: lane 0 keeps up to ST stages of asynchronous copies in flight. A stage is
 //                - the weight tile, 128 rows x 128 K, by a TMA tensor load that lands it directly

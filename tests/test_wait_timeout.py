@@ -26,9 +26,10 @@ def _restore_limit():
     _lib.check(_lib.lib().sb_debug_set_wait_limit(0), "sb_debug_set_wait_limit")
 
 
-@pytest.mark.parametrize("prefill", [1, 2])
-def test_wait_that_runs_out_sets_the_flag_and_the_next_forward_recovers(prefill):
-    name = "c0_nvfp4_m8"
+# the verify kernel (round-robin items), the prefill kernel, and the verify kernel on FP8 experts,
+# whose items come from the launch's item counter through the producer's item queue
+@pytest.mark.parametrize("name,prefill", [("c0_nvfp4_m8", 1), ("c0_nvfp4_m8", 2), ("small_fp8_noshared_m16", 1)])
+def test_wait_that_runs_out_sets_the_flag_and_the_next_forward_recovers(name, prefill):
     g = load_golden(name)
     cfg, m, xs, _ = case_config(name)
     lay = S.device_layer(cfg, 0, "cuda", prefill=prefill)
