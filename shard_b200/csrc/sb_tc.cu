@@ -295,7 +295,9 @@ struct TcArgs {
   TcPlan plan;
 };
 
-template <int FMT_R, bool PROBE>
+// DYN: the items come from the launch's item counter (a separate instantiation, so the round-robin
+// kernel compiles without the queue)
+template <int FMT_R, bool PROBE, bool DYN>
 __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_constant__ TcArgs ta) {
   const GroupedArgs& a = ta.g;
   extern __shared__ uint8_t dyn_raw[];
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) tc_grouped_kernel(const __grid_co
                      (a.mode == MODE_DENSE ? 0 : ta.plan.pass_off[*a.n_active]);
   const int n_items = n_pass * nrb + (a.ksplit > 1 && a.has_shared ? ta.plan.n_sh_pass * nrb * (a.ksplit - 1) : 0);
   const bool w13 = a.mode == MODE_W13;
-  const bool dyn = a.sched != nullptr;   // items from the launch-wide counter (zeroed by the panel kernel)
+  constexpr bool dyn = DYN;   // items from the launch-wide counter (zeroed by the panel kernel)
   // the limit of the consumer-side waits (the MMA issuer's and the readback's); the producer's waits
   // for free slots and the final drains keep WAIT_LIMIT
   const uint32_t clim = a.wait_limit ? a.wait_limit : WAIT_LIMIT;
@@ -1093,22 +1095,25 @@ static cudaError_t make_map(CUtensorMap* map, const void* base, int fmt, uint64_
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int F, bool PROBE>
+template <int F, bool PROBE, bool DYN>
 static cudaError_t launch_tc_variant(const TcArgs& a, int grid, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(tc_grouped_kernel<F, PROBE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<F, PROBE, DYN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  return launch_pdl(tc_grouped_kernel<F, PROBE>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
+  return launch_pdl(tc_grouped_kernel<F, PROBE, DYN>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, a);
 }
 
-// the probing variant only when a test wait limit is set
+// the probing variant only when a test wait limit is set; the item-counter variant only when the
+// launch has a counter
 template <int F>
 static cudaError_t launch_tc_one(const TcArgs& a, int grid, cudaStream_t st) {
-  return a.g.wait_limit ? launch_tc_variant<F, true>(a, grid, st) : launch_tc_variant<F, false>(a, grid, st);
+  if (a.g.sched != nullptr)
+    return a.g.wait_limit ? launch_tc_variant<F, true, true>(a, grid, st) : launch_tc_variant<F, false, true>(a, grid, st);
+  return a.g.wait_limit ? launch_tc_variant<F, true, false>(a, grid, st) : launch_tc_variant<F, false, false>(a, grid, st);
 }
 
 }  // namespace tc
