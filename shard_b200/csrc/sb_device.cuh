@@ -147,27 +147,6 @@ __device__ __forceinline__ void mma_e4m3(float (&c)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// streaming 16-byte weight load: read once, keep it out of L1
-__device__ __forceinline__ uint4 ld_stream16(const void* p) {
-  uint4 v;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ uint2 ld_stream8(const void* p) {
-  uint2 v;
-  asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ uint32_t ld_stream4(const void* p) {
-  uint32_t v;
-  asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
-  return v;
-}
-
 // ── bulk async copies (TMA, non-tensor) and mbarriers ───────────────────────────────────────────
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
