@@ -155,3 +155,71 @@ def test_three_stage_pipeline_streams_runs_back_to_back():
             for l in range(N_LAYERS):
                 x = Affine(l).forward(x)
             assert torch.equal(got[r][j], x), f"run {r} chunk {j}"
+
+
+class _Failing(Affine):
+    """A stand-in layer that raises on its `at`-th call: a stage that dies mid-stream."""
+
+    def __init__(self, l, at):
+        super().__init__(l)
+        self.calls, self.at = 0, at
+
+    def forward(self, x):
+        self.calls += 1
+        if self.calls == self.at:
+            raise RuntimeError("simulated stage failure")
+        return super().forward(x)
+
+
+def _failing_rank_main(rank, world, port, out_dir):
+    """Rank world-1 dies on its second chunk; every other rank must leave its run with an error
+    (the hop to the dead stage fails, or the process group's short timeout ends the wait) instead
+    of waiting for good. Each rank records how its run ended."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    status = "ok"
+    try:
+        block = even_tiling(N_LAYERS, world)[rank]
+        layers = [Affine(l) for l in block]
+        if rank == world - 1:
+            layers[0] = _Failing(block[0], at=2)
+        pipe = Pipeline(StageStack(layers), M, HIDDEN, rank, world, torch.device("cpu"), depth=2)
+        outs = [torch.empty(M, HIDDEN, dtype=torch.bfloat16) for _ in range(CHUNKS)] if rank == world - 1 else None
+        for r in range(3):
+            pipe.run(CHUNKS, _inputs() if rank == 0 else None, outs)
+            pipe.flush()
+        dist.barrier()
+    except Exception as e:   # noqa: BLE001  (the test reads how each rank's run ended)
+        status = f"error: {type(e).__name__}"
+    with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+        f.write(status)
+    if status == "ok":
+        dist.destroy_process_group()
+    os._exit(0)   # a failed group is not torn down: leave without waiting on it
+
+
+def test_a_stage_that_dies_ends_the_other_ranks_runs_with_an_error():
+    """Failure detection on the host: the stage that raised reports it, and its neighbour's run ends
+    with an error within the process group's timeout rather than hanging."""
+    import time
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.get_context("spawn")
+        port = _free_port()
+        procs = [ctx.Process(target=_failing_rank_main, args=(r, world, port, d)) for r in range(world)]
+        t0 = time.time()
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+        hung = [p.pid for p in procs if p.is_alive()]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert not hung, "a rank did not finish after its peer died"
+        status = [open(os.path.join(d, f"rank{r}")).read() for r in range(world)]
+        assert status[world - 1].startswith("error: RuntimeError"), status
+        assert status[0].startswith("error"), status
+        assert time.time() - t0 < 120
