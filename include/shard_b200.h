@@ -165,7 +165,10 @@ int sb_tile_scales(int fmt, int kind, const void* src, void* dst, int64_t n_mat,
 int sb_act_quant(const void* x, int64_t m, int64_t k, int pow2, void* q, float* s, void* stream);
 /* fp8_gemm / fp4_gemm: y bf16 [M, N] = dequant(q, s) @ dequant(W)^T with W tiled (PLAIN kind, `layout`).
  * ts: NVFP4 tensor scale (device fp32 [1]) or NULL. The tensor-core layout needs a workspace of
- * sb_qgemm_workspace_bytes() (the activation panel); the fragment layout needs none (0, NULL ok). */
+ * sb_qgemm_workspace_bytes() (the activation panel, and for narrow batches (m <= 64) of matrices
+ * with few 128-row blocks the fp32 partials of K pieces, summed in K order by the last piece of each
+ * block; the split depends on the shape alone); the size for m serves every m' <= m. The fragment
+ * layout needs none (0, NULL ok). */
 size_t sb_qgemm_workspace_bytes(int fmt, int layout, int64_t n, int64_t k, int64_t m);
 int sb_qgemm(int fmt, int layout, const void* w, const void* w_s, const float* ts, int64_t n, int64_t k,
              const void* q, const float* s, int64_t m, void* y, void* workspace, size_t workspace_bytes,
