@@ -202,3 +202,48 @@ def test_non_power_of_two_fp8_scales_keep_the_verify_kernel():
     assert lay.prefill_exact and lay.prefill == 0
     with pytest.raises(ValueError):
         lay.prefill = 4
+
+
+def _k3_layer():
+    d = _layer(hidden=512, inter=256, n_experts=16, topk=4, fmt=F.FMT_MXFP4)
+    d.has_shared = 0
+    d.mode = _lib.MODE_K3
+    d.situ_beta, d.situ_linear_beta = 2.0, 4.0
+    d.gate_w = None   # K3 takes the caller's routing: no gate needed
+    return d
+
+
+def test_k3_mode_is_validated_before_launching():
+    """sb_moe_forward_routed (KimiSparseMoeBlock.moe_infer's seam): the layer and the call are checked
+    on the host, with no device work; each refusal names its reason."""
+    L = _lib.lib()
+    d = _k3_layer()
+    need = L.sb_moe_workspace_bytes(ctypes.byref(d), 8)
+    assert need > 0
+    # a V4-mode layer does not take the caller's routing, a K3-mode one only takes it
+    v4 = _layer()
+    rc = L.sb_moe_forward_routed(ctypes.byref(v4), FAKE, 8, FAKE, FAKE, FAKE, FAKE, 1 << 30, None)
+    assert rc == -6 and "K3-mode layers" in _msg()
+    rc = L.sb_moe_forward(ctypes.byref(d), FAKE, 8, None, FAKE, None, None, FAKE, 1 << 30, None)
+    assert rc == -6 and "sb_moe_forward_routed" in _msg()
+    # K3 needs routing weights
+    rc = L.sb_moe_forward_routed(ctypes.byref(d), FAKE, 8, FAKE, None, FAKE, FAKE, 1 << 30, None)
+    assert rc == -1
+    # the layer constraints: MXFP4 experts, no shared expert, situ_beta > 0, linear beta >= 0
+    for field, value in (("expert_fmt", F.FMT_NVFP4), ("has_shared", 1), ("situ_beta", 0.0),
+                         ("situ_linear_beta", -1.0)):
+        bad = _k3_layer()
+        setattr(bad, field, value)
+        if field == "has_shared":
+            for f in ("sh_w13", "sh_w13_s", "sh_w2", "sh_w2_s"):
+                setattr(bad, f, FAKE.value)
+        assert L.sb_moe_workspace_bytes(ctypes.byref(bad), 8) == 0, field
+        rc = L.sb_moe_forward_routed(ctypes.byref(bad), FAKE, 8, FAKE, FAKE, FAKE, FAKE, 1 << 30, None)
+        assert rc == -6 and "K3 mode" in _msg(), field
+    # a mode that does not exist
+    bad = _k3_layer()
+    bad.mode = 7
+    assert L.sb_moe_workspace_bytes(ctypes.byref(bad), 8) == 0
+    # the workspace bound is checked like sb_moe_forward's
+    rc = L.sb_moe_forward_routed(ctypes.byref(d), FAKE, 8, FAKE, FAKE, FAKE, FAKE, need - 1, None)
+    assert rc == -4 and "workspace" in _msg()
