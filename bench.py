@@ -22,10 +22,13 @@ first layer.
             same workload on the host cores.
   sweep   = (N=1) c1 at M = 1, 8, 32, 64 over the same 6 layers; one c3 layer (FP8 experts, Zipf
             selection) at M = 1, 16, 64 and one c4 layer (Kimi-K3-scale NVFP4, the prefill regime)
-            at M = 256, 1024, each forward starting from a flushed L2; fp8_gemm (the kernel seam's
-            dense GEMM) at V4's attention / indexer / shared-expert shapes, M = 1 and 16.
+            at M = 256, 1024 under the default and each forced kernel choice (verify, prefill,
+            hybrid), each forward starting from a flushed L2; fp8_gemm (the kernel seam's dense
+            GEMM) at V4's attention / indexer / shared-expert shapes, M = 1 and 16.
 
---impl reference times that CPU path alone (rank 0), as the reference arm.
+--config c4 runs config c4's 61-layer stack instead (prefill chunks of M=256, split over the ranks
+by even_tiling, strong scaling). --impl reference times the CPU path alone (rank 0), as the
+reference arm.
 """
 from __future__ import annotations
 
